@@ -1,0 +1,77 @@
+"""Pin the numpy oracle against golden vectors produced by the reference itself.
+
+The fixtures come from ``tests/golden/make_golden.py``, which ran the
+reference's eager code (vutils normalizers, ``backends.scaled_dot_product_attention``,
+``paged.paged_attention`` and the varlen test loop) on the reference tests'
+own seeds.  Tolerances: float64 cases agree to 1e-10; float32 normalizer
+cases to 1e-6 (both implementations sort and cumsum in float32).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+NORMS = ("softmax1", "sparsemax", "entmax15")
+
+
+@pytest.mark.parametrize("label", ["plain", "masked"])
+@pytest.mark.parametrize("dt", ["f64", "f32"])
+@pytest.mark.parametrize("name", NORMS)
+def test_normalizers_match_reference(golden, name, dt, label):
+    g = golden("normalizers")
+    x = g[f"norm_{label}_{dt}_x"]
+    dy = g[f"norm_{label}_{dt}_dy"]
+    y = oracle.normalize(name, x)
+    dx = oracle.normalize_backward(name, x, y, dy)
+    tol = 1e-10 if dt == "f64" else 2e-6
+    np.testing.assert_allclose(y, g[f"norm_{label}_{dt}_{name}_y"], rtol=0, atol=tol)
+    np.testing.assert_allclose(dx, g[f"norm_{label}_{dt}_{name}_dx"], rtol=0, atol=tol * 10)
+
+
+@pytest.mark.parametrize("tag", ["mha", "gqa"])
+@pytest.mark.parametrize("name", NORMS)
+def test_dense_attention_matches_reference(golden, tag, name):
+    g = golden("dense")
+    q, k, v, do = (g[f"dense_{tag}_{x}"] for x in ("q", "k", "v", "do"))
+    o, dq, dk, dv = oracle.attention_backward(q, k, v, do, name, causal=True)
+    for label, a in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        np.testing.assert_allclose(a, g[f"dense_{tag}_{name}_{label}"], rtol=0, atol=1e-10)
+
+
+@pytest.mark.parametrize("name", NORMS)
+def test_varlen_matches_reference_loop(golden, name):
+    g = golden("varlen")
+    q, k, v, do = (g[f"varlen_{name}_{x}"] for x in ("q", "k", "v", "do"))
+    o, dq, dk, dv = oracle.varlen_backward(q, k, v, do, g["varlen_cu_q"], g["varlen_cu_k"], name)
+    for label, a in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        np.testing.assert_allclose(a, g[f"varlen_{name}_{label}"], rtol=0, atol=1e-10)
+
+
+@pytest.mark.parametrize("tag", ["unique", "shared", "decode"])
+@pytest.mark.parametrize("name", NORMS)
+def test_paged_matches_reference(golden, tag, name):
+    g = golden("paged")
+    pre = f"paged_{tag}_{name}_"
+    o, dq, dkc, dvc = oracle.paged_backward(
+        g[pre + "q"], g[pre + "kc"], g[pre + "vc"], g[pre + "do"], g[f"paged_{tag}_block_table"],
+        g[f"paged_{tag}_seq_lens"], int(g[f"paged_{tag}_block_size"]), name)
+    for label, a in (("o", o), ("dq", dq), ("dkc", dkc), ("dvc", dvc)):
+        np.testing.assert_allclose(a, g[pre + label], rtol=0, atol=1e-10)
+
+
+@pytest.mark.parametrize("name", NORMS)
+def test_config1_fp32_matches_reference(golden, name):
+    """BASELINE config 1 in float32 on the reference's seed; sampled rows + sums."""
+    g = golden("config1")
+    torch.manual_seed(0)
+    q, k, v = (torch.randn(2, 8, 512, 128) for _ in range(3))
+    o_shape = q.shape
+    gr = torch.randn(o_shape)
+    o, dq, dk, dv = oracle.attention_backward(q.numpy(), k.numpy(), v.numpy(), gr.numpy(), name,
+                                              scale=1 / np.sqrt(128), causal=True, dtype=np.float32)
+    for label, a in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        ref = g[f"config1_{name}_{label}_rows"]
+        np.testing.assert_allclose(a[:, :, ::61, :], ref, rtol=0, atol=2e-5)
+        assert abs(a.astype(np.float64).sum() - float(g[f"config1_{name}_{label}_sum"])) < 1e-2
