@@ -1,0 +1,144 @@
+// Shared device helpers: element conversion, warp reductions, the exact
+// threshold (tau) solver used by sparsemax / entmax15, and the kernel-side
+// parameter blocks.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/hfan.h"
+
+namespace hfan {
+
+constexpr float kNegInf = -__builtin_huge_valf();
+constexpr float kPosInf = __builtin_huge_valf();
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------------------
+// element <-> float
+// ---------------------------------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Exact threshold solve.
+//
+// Both sparse normalizers are p_i = (z_i - tau)_+^a with sum_i p_i = 1, a = 1
+// (sparsemax, z = s) or a = 2 (entmax15, z = s / 2).  The reference finds tau by
+// sorting each row (vutils/entmax.py:35-133).  Here tau is found from a
+// bracket and the closed form on the support:
+//
+//   * any row has tau >= zmax - 1, because the top entry alone has
+//     (zmax - tau)^a <= 1; so keys with z <= zmax - 1 are never in the support.
+//   * given a lower bound t <= tau, one sweep over the row gathers, over the
+//     candidate set S = {z > t}: cnt = |S|, s1 = sum (z - t), s2 = sum (z - t)^2
+//     and zmin = min_S z.  The closed-form threshold of S is
+//         sparsemax:  tc = t + (s1 - 1) / cnt
+//         entmax15:   tc = t + (s1 - sqrt(s1^2 - cnt (s2 - 1))) / cnt
+//     (the entmax root is the vutils formula mean - sqrt((1 - ss)/rho) written
+//     around t).  If zmin >= tc the candidate set is exactly the support and
+//     tc is the exact threshold.  Otherwise the row is refined with a Newton
+//     step on f(t) = sum (z - t)_+^a - 1 (convex and decreasing, so Newton from
+//     the left never overshoots): sparsemax t <- tc (Michelot's iteration),
+//     entmax15 t <- t + (s2 - 1) / (2 s1).
+// ---------------------------------------------------------------------------
+struct TauStats {
+  float cnt, s1, s2, zmin;
+};
+
+__device__ __forceinline__ void tau_accumulate(TauStats& st, float z, float t) {
+  if (z > t) {
+    float d = z - t;
+    st.cnt += 1.f;
+    st.s1 += d;
+    st.s2 += d * d;
+    st.zmin = fminf(st.zmin, z);
+  }
+}
+
+// Returns true when t is resolved; writes the exact threshold to *tau.  On
+// false, *t holds the refined lower bound for the next sweep and *tau the
+// current closed-form estimate.
+__device__ __forceinline__ bool tau_step(int norm, const TauStats& st, float* t, float* tau) {
+  float cnt = fmaxf(st.cnt, 1.f);
+  float tc;
+  if (norm == HFAN_SPARSEMAX) {
+    tc = *t + (st.s1 - 1.f) / cnt;
+  } else {
+    float disc = fmaxf(st.s1 * st.s1 - cnt * (st.s2 - 1.f), 0.f);
+    tc = *t + (st.s1 - sqrtf(disc)) / cnt;
+  }
+  *tau = tc;
+  if (st.zmin >= tc) return true;
+  float nt = (norm == HFAN_SPARSEMAX) ? tc : *t + (st.s2 - 1.f) / (2.f * fmaxf(st.s1, 1e-30f));
+  // Guard against a rounding stall: the next bound must strictly grow.
+  *t = fmaxf(nt, nextafterf(*t, kPosInf));
+  return false;
+}
+
+__device__ __forceinline__ float sparse_prob(int norm, float z, float tau) {
+  float d = fmaxf(z - tau, 0.f);
+  return norm == HFAN_SPARSEMAX ? d : d * d;
+}
+// g = 1[p>0] (sparsemax) or sqrt(p) (entmax15): the diagonal of the inverse
+// Hessian used by both closed-form backwards (vutils/entmax.py:148-157, 175-183).
+__device__ __forceinline__ float sparse_g(int norm, float z, float tau) {
+  float d = z - tau;
+  if (!(d > 0.f)) return 0.f;
+  return norm == HFAN_SPARSEMAX ? 1.f : d;
+}
+
+// ---------------------------------------------------------------------------
+// Sequence geometry shared by the attention kernels.
+// ---------------------------------------------------------------------------
+struct Geometry {
+  int q_start, q_len;   // first packed row / number of query rows of this sequence
+  int k_start, k_len;   // first packed key / number of keys
+};
+
+__device__ __forceinline__ bool key_visible(int i, int j, const Geometry& g, int causal,
+                                            int window_left) {
+  if (j >= g.k_len) return false;
+  int limit = i + g.k_len - g.q_len;
+  if (causal && j > limit) return false;
+  if (window_left > 0 && j <= limit - window_left) return false;
+  return true;
+}
+
+// Device-side status word: kernels record the first error they detect
+// (out-of-range page id, bounded wait expired) instead of trapping.
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevBadPage = 1,
+  kDevWaitTimeout = 2,
+};
+
+}  // namespace hfan

@@ -1,0 +1,97 @@
+// Kernel-side parameter block shared by every attention kernel (dense, varlen
+// and paged layouts) plus the address arithmetic for each layout.
+#pragma once
+
+#include "common.cuh"
+
+namespace hfan {
+
+struct AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  const void* dout;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* stats;  // [2][hq][rows_total]
+  float* corr;   // [hq][rows_total]
+
+  int64_t q_sb, q_sh, q_st;
+  int64_t k_sb, k_sh, k_st;
+  int64_t v_sb, v_sh, v_st;
+  int64_t o_sb, o_sh, o_st;
+  int64_t do_sb, do_sh, do_st;
+  int64_t dq_sb, dq_sh, dq_st;
+  int64_t dk_sb, dk_sh, dk_st;
+  int64_t dv_sb, dv_sh, dv_st;
+
+  int batch, hq, hkv, d;
+  int len_q, len_k;      // dense lengths; varlen/paged maxima
+  int rows_total;        // stats rows per head
+  const int* cu_q;       // varlen
+  const int* cu_k;
+  const int* block_table;  // paged
+  const int* seq_lens;
+  int page_size, max_blocks;
+  int64_t num_cache_tokens;
+  int paged;
+
+  float scale;
+  int causal, window_left, norm;
+  int grad_f32;          // dq/dk/dv element type is float32 (else the input type)
+  int* dev_status;       // first device-side error, see DeviceError
+};
+
+__device__ __forceinline__ Geometry geometry(const AttnParams& p, int b) {
+  Geometry g;
+  if (p.cu_q != nullptr) {
+    g.q_start = p.cu_q[b];
+    g.q_len = p.cu_q[b + 1] - g.q_start;
+    g.k_start = p.cu_k[b];
+    g.k_len = p.cu_k[b + 1] - g.k_start;
+  } else {
+    g.q_start = b * p.len_q;
+    g.q_len = p.len_q;
+    g.k_start = 0;
+    g.k_len = p.paged ? p.seq_lens[b] : p.len_k;
+  }
+  return g;
+}
+
+// Element offset of query-side row i (q, o, do, dq share the indexing scheme).
+__device__ __forceinline__ int64_t qrow_off(const AttnParams& p, const Geometry& g, int b, int h,
+                                            int i, int64_t sb, int64_t sh, int64_t st) {
+  int64_t tok = p.cu_q != nullptr ? (int64_t)(g.q_start + i) : (int64_t)i;
+  return (int64_t)b * sb + (int64_t)h * sh + tok * st;
+}
+
+// Token index of key j of sequence b inside the K/V storage.  For the paged
+// layout this is the physical cache row; -1 flags a page id outside the
+// cache (recorded in the device status word, the row reads as zeros).
+__device__ __forceinline__ int64_t key_token(const AttnParams& p, const Geometry& g, int b, int j) {
+  if (p.paged) {
+    int page = p.block_table[(int64_t)b * p.max_blocks + j / p.page_size];
+    int64_t tok = (int64_t)page * p.page_size + (j % p.page_size);
+    if (page < 0 || tok >= p.num_cache_tokens) {
+      if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevBadPage);
+      return -1;
+    }
+    return tok;
+  }
+  return p.cu_k != nullptr ? (int64_t)(g.k_start + j) : (int64_t)j;
+}
+
+__device__ __forceinline__ int64_t key_off(const AttnParams& p, int b, int kvh, int64_t tok,
+                                           int64_t sb, int64_t sh, int64_t st) {
+  // Paged caches and packed varlen tensors have no batch stride.
+  int64_t bo = (p.paged || p.cu_k != nullptr) ? 0 : (int64_t)b * sb;
+  return bo + (int64_t)kvh * sh + tok * st;
+}
+
+__device__ __forceinline__ int64_t stat_index(const AttnParams& p, const Geometry& g, int h, int i) {
+  return (int64_t)h * p.rows_total + g.q_start + i;
+}
+
+}  // namespace hfan

@@ -1,0 +1,380 @@
+"""torch.library custom ops over the native library, with fake (meta) kernels
+for ``torch.compile(fullgraph=True)`` and autograd formulas.
+
+Ops (namespace ``hfan``):
+  attn_fwd / attn_bwd       dense [B, H, S, D] attention
+  varlen_fwd / varlen_bwd   packed [T, H, D] attention with cu_seqlens
+  paged_fwd / paged_bwd     paged KV cache + block_table
+  rownorm_fwd / rownorm_bwd row normalizers on a materialised matrix
+
+Every op launches on the current CUDA stream of its inputs' device; CPU
+tensors raise (the engine has no CPU path).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.FLOAT32, torch.float16: N.FLOAT16, torch.bfloat16: N.BFLOAT16}
+
+
+def dtype_id(t: Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16") from None
+
+
+def _require_cuda(*ts: Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("hfan attention requires CUDA tensors.")
+
+
+def _inner_contig(t: Tensor) -> Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _t4(t: Optional[Tensor]) -> N.HfanTensor:
+    """[B, H, S, D] view -> hfan_tensor."""
+    if t is None:
+        return N.HfanTensor(None, 0, 0, 0)
+    return N.HfanTensor(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def _t3(t: Optional[Tensor]) -> N.HfanTensor:
+    """Packed [T, H, D] (or cache [P, H, D]) view -> hfan_tensor (no batch stride)."""
+    if t is None:
+        return N.HfanTensor(None, 0, 0, 0)
+    return N.HfanTensor(t.data_ptr(), 0, t.stride(1), t.stride(0))
+
+
+def _stream(t: Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: Optional[Tensor]) -> ctypes.c_void_p:
+    return ctypes.c_void_p(None if t is None else t.data_ptr())
+
+
+# ---------------------------------------------------------------------------
+# dense
+# ---------------------------------------------------------------------------
+def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None) -> N.AttnDesc:
+    b, hq, lq, d = q.shape
+    return N.AttnDesc(
+        dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=k.shape[1],
+        head_dim=d, len_q=lq, len_k=k.shape[2], total_q=b * lq, cu_seqlens_q=None,
+        cu_seqlens_k=None, scale=float(scale), causal=int(bool(causal)),
+        window_left=int(window_left), grad_dtype=dtype_id(q) if grad_dtype is None else grad_dtype)
+
+
+def _new_out(q: Tensor, out_bshd: bool) -> Tensor:
+    b, h, s, d = q.shape
+    if out_bshd:
+        return torch.empty((b, s, h, d), dtype=q.dtype, device=q.device)
+    return torch.empty_like(q, memory_format=torch.contiguous_format)
+
+
+def _as_bhsd(o: Tensor, out_bshd: bool) -> Tensor:
+    return o.transpose(1, 2) if out_bshd else o
+
+
+@torch.library.custom_op("hfan::attn_fwd", mutates_args=())
+def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, causal: bool,
+             window_left: int, out_bshd: bool) -> tuple[Tensor, Tensor]:
+    _require_cuda(q, k, v)
+    q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
+    o = _new_out(q, out_bshd)
+    b, hq, lq, _ = q.shape
+    stats = torch.empty((2, hq, b * lq), dtype=torch.float32, device=q.device)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(_as_bhsd(o, out_bshd)),
+                                      _ptr(stats), _stream(q)), "hfan_attn_fwd")
+    return o, stats
+
+
+@attn_fwd.register_fake
+def _(q, k, v, normalizer, scale, causal, window_left, out_bshd):
+    b, hq, lq, d = q.shape
+    o = _new_out(q, out_bshd)
+    return o, q.new_empty((2, hq, b * lq), dtype=torch.float32)
+
+
+@torch.library.custom_op("hfan::attn_bwd", mutates_args=())
+def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, normalizer: int,
+             scale: float, causal: bool, window_left: int) -> tuple[Tensor, Tensor, Tensor]:
+    _require_cuda(do, q, k, v, o)
+    do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
+    dq = torch.empty_like(q, memory_format=torch.contiguous_format)
+    dk = torch.empty_like(k, memory_format=torch.contiguous_format)
+    dv = torch.empty_like(v, memory_format=torch.contiguous_format)
+    b, hq, lq, _ = q.shape
+    corr = torch.empty((hq, b * lq), dtype=torch.float32, device=q.device)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
+                                      _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
+                "hfan_attn_bwd")
+    return dq, dk, dv
+
+
+@attn_bwd.register_fake
+def _(do, q, k, v, o, stats, normalizer, scale, causal, window_left):
+    return (torch.empty_like(q, memory_format=torch.contiguous_format),
+            torch.empty_like(k, memory_format=torch.contiguous_format),
+            torch.empty_like(v, memory_format=torch.contiguous_format))
+
+
+def _attn_setup(ctx, inputs, output):
+    q, k, v, normalizer, scale, causal, window_left, out_bshd = inputs
+    o, stats = output
+    ctx.save_for_backward(q, k, v, o, stats)
+    ctx.args = (normalizer, scale, causal, window_left, out_bshd)
+    ctx.mark_non_differentiable(stats)
+
+
+def _attn_backward(ctx, do, dstats):
+    q, k, v, o, stats = ctx.saved_tensors
+    normalizer, scale, causal, window_left, out_bshd = ctx.args
+    dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, normalizer,
+                          scale, causal, window_left)
+    return dq, dk, dv, None, None, None, None, None
+
+
+torch.library.register_autograd("hfan::attn_fwd", _attn_backward, setup_context=_attn_setup)
+
+
+# ---------------------------------------------------------------------------
+# varlen
+# ---------------------------------------------------------------------------
+def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal) -> N.AttnDesc:
+    return N.AttnDesc(
+        dtype=dtype_id(q), normalizer=normalizer, batch=cu_q.numel() - 1, heads_q=q.shape[1],
+        heads_kv=k.shape[1], head_dim=q.shape[2], len_q=int(max_q), len_k=int(max_k),
+        total_q=q.shape[0], cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=cu_k.data_ptr(),
+        scale=float(scale), causal=int(bool(causal)), window_left=0, grad_dtype=dtype_id(q))
+
+
+@torch.library.custom_op("hfan::varlen_fwd", mutates_args=())
+def varlen_fwd(q: Tensor, k: Tensor, v: Tensor, cu_q: Tensor, cu_k: Tensor, max_q: int, max_k: int,
+               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor]:
+    _require_cuda(q, k, v, cu_q, cu_k)
+    q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
+    cu_q = cu_q.to(torch.int32).contiguous()
+    cu_k = cu_k.to(torch.int32).contiguous()
+    o = torch.empty_like(q, memory_format=torch.contiguous_format)
+    stats = torch.empty((2, q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _ptr(stats),
+                                      _stream(q)), "hfan_attn_fwd(varlen)")
+    return o, stats
+
+
+@varlen_fwd.register_fake
+def _(q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
+    return (torch.empty_like(q, memory_format=torch.contiguous_format),
+            q.new_empty((2, q.shape[1], q.shape[0]), dtype=torch.float32))
+
+
+@torch.library.custom_op("hfan::varlen_bwd", mutates_args=())
+def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, cu_q: Tensor,
+               cu_k: Tensor, max_q: int, max_k: int, normalizer: int, scale: float,
+               causal: bool) -> tuple[Tensor, Tensor, Tensor]:
+    _require_cuda(do, q, k, v, o)
+    do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
+    cu_q = cu_q.to(torch.int32).contiguous()
+    cu_k = cu_k.to(torch.int32).contiguous()
+    dq = torch.zeros_like(q, memory_format=torch.contiguous_format)
+    dk = torch.zeros_like(k, memory_format=torch.contiguous_format)
+    dv = torch.zeros_like(v, memory_format=torch.contiguous_format)
+    corr = torch.empty((q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _t3(do),
+                                      _ptr(stats), _ptr(corr), _t3(dq), _t3(dk), _t3(dv), _stream(q)),
+                "hfan_attn_bwd(varlen)")
+    return dq, dk, dv
+
+
+@varlen_bwd.register_fake
+def _(do, q, k, v, o, stats, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
+    return (torch.empty_like(q, memory_format=torch.contiguous_format),
+            torch.empty_like(k, memory_format=torch.contiguous_format),
+            torch.empty_like(v, memory_format=torch.contiguous_format))
+
+
+def _varlen_setup(ctx, inputs, output):
+    q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal = inputs
+    o, stats = output
+    ctx.save_for_backward(q, k, v, o, stats, cu_q, cu_k)
+    ctx.args = (max_q, max_k, normalizer, scale, causal)
+    ctx.mark_non_differentiable(stats)
+
+
+def _varlen_backward(ctx, do, dstats):
+    q, k, v, o, stats, cu_q, cu_k = ctx.saved_tensors
+    max_q, max_k, normalizer, scale, causal = ctx.args
+    dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    return dq, dk, dv, None, None, None, None, None, None, None
+
+
+torch.library.register_autograd("hfan::varlen_fwd", _varlen_backward, setup_context=_varlen_setup)
+
+
+# ---------------------------------------------------------------------------
+# paged
+# ---------------------------------------------------------------------------
+def _paged_desc(q, kc, block_table, seq_lens, page_size, max_len_k, normalizer, scale, causal) -> N.PagedDesc:
+    b, hq, lq, d = q.shape
+    return N.PagedDesc(
+        dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=kc.shape[1], head_dim=d,
+        len_q=lq, page_size=int(page_size), max_blocks=block_table.shape[1], max_len_k=int(max_len_k),
+        num_cache_tokens=kc.shape[0], block_table=block_table.data_ptr(), seq_lens=seq_lens.data_ptr(),
+        scale=float(scale), causal=int(bool(causal)), grad_dtype=N.FLOAT32)
+
+
+@torch.library.custom_op("hfan::paged_fwd", mutates_args=())
+def paged_fwd(q: Tensor, key_cache: Tensor, value_cache: Tensor, block_table: Tensor, seq_lens: Tensor,
+              page_size: int, max_len_k: int, normalizer: int, scale: float,
+              causal: bool) -> tuple[Tensor, Tensor]:
+    _require_cuda(q, key_cache, value_cache, block_table, seq_lens)
+    q, kc, vc = _inner_contig(q), _inner_contig(key_cache), _inner_contig(value_cache)
+    bt = block_table.to(torch.int32).contiguous()
+    sl = seq_lens.to(torch.int32).contiguous()
+    o = torch.empty_like(q, memory_format=torch.contiguous_format)
+    b, hq, lq, _ = q.shape
+    stats = torch.empty((2, hq, b * lq), dtype=torch.float32, device=q.device)
+    desc = _paged_desc(q, kc, bt, sl, page_size, max_len_k, normalizer, scale, causal)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_paged_fwd(ctypes.byref(desc), _t4(q), _t3(kc), _t3(vc), _t4(o), _ptr(stats),
+                                       _stream(q)), "hfan_paged_fwd")
+    return o, stats
+
+
+@paged_fwd.register_fake
+def _(q, key_cache, value_cache, block_table, seq_lens, page_size, max_len_k, normalizer, scale, causal):
+    b, hq, lq, _ = q.shape
+    return (torch.empty_like(q, memory_format=torch.contiguous_format),
+            q.new_empty((2, hq, b * lq), dtype=torch.float32))
+
+
+@torch.library.custom_op("hfan::paged_bwd", mutates_args=())
+def paged_bwd(do: Tensor, q: Tensor, key_cache: Tensor, value_cache: Tensor, o: Tensor, stats: Tensor,
+              block_table: Tensor, seq_lens: Tensor, page_size: int, max_len_k: int, normalizer: int,
+              scale: float, causal: bool) -> tuple[Tensor, Tensor, Tensor]:
+    _require_cuda(do, q, key_cache, value_cache, o)
+    do, q, kc, vc, o = (_inner_contig(t) for t in (do, q, key_cache, value_cache, o))
+    bt = block_table.to(torch.int32).contiguous()
+    sl = seq_lens.to(torch.int32).contiguous()
+    dq = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    dkc = torch.zeros(kc.shape, dtype=torch.float32, device=q.device)
+    dvc = torch.zeros(vc.shape, dtype=torch.float32, device=q.device)
+    b, hq, lq, _ = q.shape
+    corr = torch.empty((hq, b * lq), dtype=torch.float32, device=q.device)
+    desc = _paged_desc(q, kc, bt, sl, page_size, max_len_k, normalizer, scale, causal)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_paged_bwd(ctypes.byref(desc), _t4(q), _t3(kc), _t3(vc), _t4(o), _t4(do),
+                                       _ptr(stats), _ptr(corr), _t4(dq), _t3(dkc), _t3(dvc), _stream(q)),
+                "hfan_paged_bwd")
+    return dq.to(q.dtype), dkc.to(key_cache.dtype), dvc.to(value_cache.dtype)
+
+
+@paged_bwd.register_fake
+def _(do, q, key_cache, value_cache, o, stats, block_table, seq_lens, page_size, max_len_k, normalizer,
+      scale, causal):
+    return (torch.empty_like(q, memory_format=torch.contiguous_format),
+            torch.empty_like(key_cache, memory_format=torch.contiguous_format),
+            torch.empty_like(value_cache, memory_format=torch.contiguous_format))
+
+
+def _paged_setup(ctx, inputs, output):
+    q, kc, vc, bt, sl, page_size, max_len_k, normalizer, scale, causal = inputs
+    o, stats = output
+    ctx.save_for_backward(q, kc, vc, o, stats, bt, sl)
+    ctx.args = (page_size, max_len_k, normalizer, scale, causal)
+    ctx.mark_non_differentiable(stats)
+
+
+def _paged_backward(ctx, do, dstats):
+    q, kc, vc, o, stats, bt, sl = ctx.saved_tensors
+    page_size, max_len_k, normalizer, scale, causal = ctx.args
+    dq, dkc, dvc = paged_bwd(do, q, kc, vc, o, stats, bt, sl, page_size, max_len_k, normalizer, scale, causal)
+    return dq, dkc, dvc, None, None, None, None, None, None, None
+
+
+torch.library.register_autograd("hfan::paged_fwd", _paged_backward, setup_context=_paged_setup)
+
+
+# ---------------------------------------------------------------------------
+# row normalizers
+# ---------------------------------------------------------------------------
+def _rows(x: Tensor):
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    if x2.stride(-1) != 1 or (x2.shape[0] > 1 and x2.stride(0) < x2.shape[1]):
+        x2 = x2.contiguous()
+    return x2
+
+
+@torch.library.custom_op("hfan::rownorm_fwd", mutates_args=())
+def rownorm_fwd(x: Tensor, normalizer: int) -> Tensor:
+    _require_cuda(x)
+    x2 = _rows(x)
+    y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        N.check(N.lib().hfan_rownorm_fwd(normalizer, dtype_id(x), x2.shape[0], x2.shape[1], _ptr(x2),
+                                         max(x2.stride(0), x2.shape[1]), _ptr(y), x2.shape[1], _stream(x)),
+                "hfan_rownorm_fwd")
+    return y
+
+
+@rownorm_fwd.register_fake
+def _(x, normalizer):
+    return torch.empty(x.shape, dtype=x.dtype, device=x.device)
+
+
+@torch.library.custom_op("hfan::rownorm_bwd", mutates_args=())
+def rownorm_bwd(y: Tensor, dy: Tensor, normalizer: int) -> Tensor:
+    _require_cuda(y, dy)
+    y2 = y.reshape(-1, y.shape[-1]).contiguous()
+    dy2 = dy.reshape(-1, dy.shape[-1]).contiguous().to(y.dtype)
+    dx = torch.empty(y.shape, dtype=y.dtype, device=y.device)
+    with torch.cuda.device(y.device):
+        N.check(N.lib().hfan_rownorm_bwd(normalizer, dtype_id(y), y2.shape[0], y2.shape[1], _ptr(y2), y2.shape[1],
+                                         _ptr(dy2), dy2.shape[1], _ptr(dx), y2.shape[1], _stream(y)),
+                "hfan_rownorm_bwd")
+    return dx
+
+
+@rownorm_bwd.register_fake
+def _(y, dy, normalizer):
+    return torch.empty(y.shape, dtype=y.dtype, device=y.device)
+
+
+def _rownorm_setup(ctx, inputs, output):
+    ctx.save_for_backward(output)
+    ctx.normalizer = inputs[1]
+
+
+def _rownorm_backward(ctx, dy):
+    (y,) = ctx.saved_tensors
+    return rownorm_bwd(y, dy, ctx.normalizer), None
+
+
+torch.library.register_autograd("hfan::rownorm_fwd", _rownorm_backward, setup_context=_rownorm_setup)
+
+
+def row_normalize(x: Tensor, normalizer: str, dim: int = -1) -> Tensor:
+    """Apply a normalizer along ``dim`` with the CUDA row kernels."""
+    nid = N.NORMALIZER_IDS[normalizer]
+    if dim != -1 and dim != x.dim() - 1:
+        return rownorm_fwd(x.movedim(dim, -1).contiguous(), nid).movedim(-1, dim)
+    return rownorm_fwd(x, nid)

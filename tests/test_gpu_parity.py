@@ -1,0 +1,277 @@
+"""GPU parity of the CUDA kernels against the numpy oracle and the golden
+vectors generated from the reference.
+
+Tolerances (the bar of the engine's target):
+  * float32 inputs: |kernel - oracle| <= 1e-5 * max(1, max|oracle|) elementwise.
+  * bfloat16: max|kernel - oracle| <= 2e-2 * max|oracle|; float16: 1e-2.
+  * every 16-bit case also keeps the reference tests' own bar, mean |err| < 1e-3
+    (scaled by max|oracle| for gradients larger than one).
+  * sparse thresholds: |tau_kernel - tau_oracle| <= 1e-5 (1 + |tau|) in float32,
+    so the zero pattern agrees except for entries within ~1e-5 of tau.
+The oracle runs in float64 on the same (dtype-rounded) inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from hf_attention_normalizers_b200 import kernels, ops, varlen
+import hf_attention_normalizers_b200 as H
+from hf_attention_normalizers_b200 import _native as N
+
+pytestmark = pytest.mark.gpu
+
+NORMS = ("softmax1", "sparsemax", "entmax15")
+KERNELS = {
+    "softmax1": kernels.hopper_softmax1_attention,
+    "sparsemax": kernels.hopper_sparsemax_attention,
+    "entmax15": kernels.hopper_entmax15_attention,
+}
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 1e-2}
+
+
+def _np(t):
+    return t.detach().double().cpu().numpy()
+
+
+def assert_close(actual, expected, dtype, what=""):
+    a = _np(actual) if isinstance(actual, torch.Tensor) else np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    assert a.shape == e.shape, (what, a.shape, e.shape)
+    assert np.isfinite(a).all(), f"{what}: non-finite values"
+    scale = max(1.0, float(np.abs(e).max())) if dtype == torch.float32 else float(np.abs(e).max()) + 1e-12
+    err = np.abs(a - e)
+    assert err.max() <= TOL[dtype] * scale, f"{what}: max err {err.max():.3e} vs tol {TOL[dtype] * scale:.3e}"
+    if dtype != torch.float32:
+        assert err.mean() < 1e-3 * max(1.0, scale), f"{what}: mean err {err.mean():.3e}"
+
+
+def _inputs(shape_q, shape_kv, dtype, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(shape_q, generator=g).to(dtype).cuda()
+    k = torch.randn(shape_kv, generator=g).to(dtype).cuda()
+    v = torch.randn(shape_kv, generator=g).to(dtype).cuda()
+    do = torch.randn(shape_q, generator=g).to(dtype).cuda()
+    return q, k, v, do
+
+
+def _run_dense(norm, q, k, v, do, causal=True, window=None):
+    qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
+    o = KERNELS[norm](qr, kr, vr, is_causal=causal, window_left=window)
+    o.backward(do)
+    torch.cuda.synchronize()
+    return o, qr.grad, kr.grad, vr.grad
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("tag", ["mha", "gqa"])
+@pytest.mark.parametrize("norm", NORMS)
+def test_dense_matches_reference_golden(golden, norm, tag, dtype):
+    """Golden vectors from the reference's eager attention (tests/test_hopper_attention.py shapes)."""
+    g = golden("dense")
+    q, k, v, do = (torch.tensor(g[f"dense_{tag}_{x}"]).to(dtype).cuda() for x in ("q", "k", "v", "do"))
+    out = _run_dense(norm, q, k, v, do)
+    if dtype == torch.float32:
+        for label, a in zip(("o", "dq", "dk", "dv"), out):
+            assert_close(a, g[f"dense_{tag}_{norm}_{label}"], dtype, f"{norm}/{tag}/{label}")
+    else:
+        ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), norm, causal=True)
+        for label, a, e in zip(("o", "dq", "dk", "dv"), out, ref):
+            assert_close(a, e, dtype, f"{norm}/{tag}/{label}")
+
+
+DENSE_CASES = [
+    # (B, Hq, Hkv, Lq, Lk, D, causal)
+    (2, 4, 2, 200, 200, 64, True),
+    (1, 8, 2, 300, 300, 128, True),
+    (1, 4, 4, 77, 190, 128, True),     # bottom-right causal with Lq < Lk
+    (2, 2, 1, 65, 65, 48, False),
+    (1, 4, 1, 1, 513, 128, True),      # decode-like single row
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("case", DENSE_CASES)
+@pytest.mark.parametrize("norm", NORMS)
+def test_dense_random_matches_oracle(norm, case, dtype):
+    b, hq, hkv, lq, lk, d, causal = case
+    q, k, v, do = _inputs((b, hq, lq, d), (b, hkv, lk, d), dtype, seed=10 * DENSE_CASES.index(case) + NORMS.index(norm))
+    out = _run_dense(norm, q, k, v, do, causal=causal)
+    ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), norm, causal=causal)
+    for label, a, e in zip(("o", "dq", "dk", "dv"), out, ref):
+        assert_close(a, e, dtype, f"{norm}/{case}/{label}")
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_sliding_window_matches_oracle(norm):
+    q, k, v, do = _inputs((1, 4, 150, 64), (1, 2, 150, 64), torch.bfloat16, seed=3)
+    out = _run_dense(norm, q, k, v, do, causal=True, window=20)
+    ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), norm, causal=True, window_left=20)
+    for label, a, e in zip(("o", "dq", "dk", "dv"), out, ref):
+        assert_close(a, e, torch.bfloat16, f"{norm}/window/{label}")
+
+
+@pytest.mark.parametrize("norm", ("sparsemax", "entmax15"))
+def test_sparse_threshold_matches_oracle_fp32(norm):
+    """The saved tau equals the oracle's sort-based tau (zero-pattern check)."""
+    q, k, v, _ = _inputs((1, 2, 96, 64), (1, 2, 96, 64), torch.float32, seed=11)
+    o, stats = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], 64 ** -0.5, True, -1, False)
+    _, p, s = oracle.attention_forward(_np(q), _np(k), _np(v), norm, causal=True, return_probs=True)
+    half = 1.0 if norm == "sparsemax" else 0.5
+    with np.errstate(all="ignore"):
+        z = (s - s.max(-1, keepdims=True)) * half
+        if norm == "sparsemax":
+            tau_rel, _ = oracle.normalizers.sparsemax_threshold(z)
+        else:
+            tau_rel, _ = oracle.normalizers.entmax_threshold(z)
+    tau_abs = tau_rel[..., 0] + s.max(-1) * half
+    tau_k = stats[0].reshape(1, 2, 96).double().cpu().numpy()
+    assert np.all(np.abs(tau_k - tau_abs) <= 1e-5 * (1 + np.abs(tau_abs)))
+    support = stats[1].reshape(1, 2, 96).cpu().numpy()
+    diff = np.abs(support - (p > 0).sum(-1))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.95
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_varlen_matches_reference_golden(golden, norm):
+    g = golden("varlen")
+    cu_q = torch.tensor(g["varlen_cu_q"]).cuda()
+    cu_k = torch.tensor(g["varlen_cu_k"]).cuda()
+    for dtype in (torch.float32, torch.float16):
+        q, k, v = (torch.tensor(g[f"varlen_{norm}_{x}"]).to(dtype).cuda().requires_grad_(True) for x in "qkv")
+        do = torch.tensor(g[f"varlen_{norm}_do"]).to(dtype).cuda()
+        o = varlen.varlen_hopper_attention(q, k, v, cu_q, cu_k, norm, max_seqlen_q=8, max_seqlen_k=10)
+        o.backward(do)
+        if dtype == torch.float32:
+            refs = [g[f"varlen_{norm}_{x}"] for x in ("o", "dq", "dk", "dv")]
+        else:
+            refs = oracle.varlen_backward(_np(q), _np(k), _np(v), _np(do), g["varlen_cu_q"], g["varlen_cu_k"], norm)
+        for label, a, e in zip(("o", "dq", "dk", "dv"), (o, q.grad, k.grad, v.grad), refs):
+            assert_close(a, e, dtype, f"varlen/{norm}/{label}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("norm", NORMS)
+def test_varlen_random_gqa_matches_oracle(norm, dtype):
+    gen = torch.Generator().manual_seed(5)
+    lens_q = torch.randint(1, 200, (5,), generator=gen)
+    lens_k = lens_q + torch.randint(0, 40, (5,), generator=gen)
+    cu_q = torch.cat([torch.zeros(1, dtype=torch.long), lens_q.cumsum(0)])
+    cu_k = torch.cat([torch.zeros(1, dtype=torch.long), lens_k.cumsum(0)])
+    tq, tk = int(cu_q[-1]), int(cu_k[-1])
+    q = torch.randn(tq, 8, 128, generator=gen).to(dtype).cuda().requires_grad_(True)
+    k = torch.randn(tk, 2, 128, generator=gen).to(dtype).cuda().requires_grad_(True)
+    v = torch.randn(tk, 2, 128, generator=gen).to(dtype).cuda().requires_grad_(True)
+    do = torch.randn(tq, 8, 128, generator=gen).to(dtype).cuda()
+    o = varlen.varlen_hopper_attention(q, k, v, cu_q.cuda().int(), cu_k.cuda().int(), norm)
+    o.backward(do)
+    refs = oracle.varlen_backward(_np(q), _np(k), _np(v), _np(do), cu_q.numpy(), cu_k.numpy(), norm)
+    for label, a, e in zip(("o", "dq", "dk", "dv"), (o, q.grad, k.grad, v.grad), refs):
+        assert_close(a, e, dtype, f"varlen-rand/{norm}/{label}")
+
+
+@pytest.mark.parametrize("tag", ["unique", "shared", "decode"])
+@pytest.mark.parametrize("norm", NORMS)
+def test_paged_matches_reference_golden(golden, norm, tag):
+    g = golden("paged")
+    pre = f"paged_{tag}_{norm}_"
+    bt = torch.tensor(g[f"paged_{tag}_block_table"]).cuda()
+    sl = torch.tensor(g[f"paged_{tag}_seq_lens"]).cuda()
+    bs = int(g[f"paged_{tag}_block_size"])
+    for dtype in (torch.float32, torch.float16):
+        q, kc, vc = (torch.tensor(g[pre + x]).to(dtype).cuda().requires_grad_(True) for x in ("q", "kc", "vc"))
+        do = torch.tensor(g[pre + "do"]).to(dtype).cuda()
+        o = H.paged_attention(q, kc, vc, bt, sl, block_size=bs, normalizer=norm)
+        o.backward(do)
+        if dtype == torch.float32:
+            refs = [g[pre + x] for x in ("o", "dq", "dkc", "dvc")]
+        else:
+            refs = oracle.paged_backward(_np(q), _np(kc), _np(vc), _np(do), bt.cpu().numpy(), sl.cpu().numpy(), bs, norm)
+        for label, a, e in zip(("o", "dq", "dkc", "dvc"), (o, q.grad, kc.grad, vc.grad), refs):
+            assert_close(a, e, dtype, f"paged/{tag}/{norm}/{label}")
+
+
+def test_paged_rejects_out_of_range_block_table():
+    q = torch.randn(1, 2, 1, 32, device="cuda")
+    kc = torch.randn(16, 1, 32, device="cuda")
+    with pytest.raises(ValueError, match="outside the physical cache"):
+        H.paged_attention(q, kc, kc, torch.tensor([[0, 9]], device="cuda"), torch.tensor([8], device="cuda"), 4)
+
+
+@pytest.mark.parametrize("label", ["plain", "masked"])
+@pytest.mark.parametrize("norm", NORMS)
+def test_row_normalizers_match_reference_golden(golden, norm, label):
+    from hf_attention_normalizers_b200 import vutils
+
+    g = golden("normalizers")
+    fn = {"softmax1": vutils.softmax_1, "sparsemax": vutils.sparsemax, "entmax15": vutils.entmax15}[norm]
+    x = torch.tensor(g[f"norm_{label}_f32_x"]).cuda().requires_grad_(True)
+    dy = torch.tensor(g[f"norm_{label}_f32_dy"]).cuda()
+    y = fn(x, dim=-1)
+    y.backward(dy)
+    assert_close(y, g[f"norm_{label}_f32_{norm}_y"], torch.float32, f"rownorm/{norm}/y")
+    assert_close(x.grad, g[f"norm_{label}_f32_{norm}_dx"], torch.float32, f"rownorm/{norm}/dx")
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_config1_fp32_matches_reference(golden, norm):
+    """BASELINE config 1 (fp32, B=2 H=8 S=512 D=128, seed 0) against the reference's own outputs."""
+    g = golden("config1")
+    torch.manual_seed(0)
+    q, k, v = (torch.randn(2, 8, 512, 128) for _ in range(3))
+    gr = torch.randn(2, 8, 512, 128)
+    q, k, v = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = KERNELS[norm](q, k, v, is_causal=True)
+    (o * gr.cuda()).sum().backward()
+    for label, a in (("o", o), ("dq", q.grad), ("dk", k.grad), ("dv", v.grad)):
+        rows = g[f"config1_{norm}_{label}_rows"]
+        assert_close(a[:, :, ::61, :], rows, torch.float32, f"config1/{norm}/{label}")
+        assert abs(float(a.double().sum()) - float(g[f"config1_{norm}_{label}_sum"])) < 1e-2
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_long_key_row_beyond_old_single_block_limit(norm):
+    q = torch.randn(1, 1, 2, 64, device="cuda", dtype=torch.float16, requires_grad=True)
+    k = torch.randn(1, 1, 8192, 64, device="cuda", dtype=torch.float16, requires_grad=True)
+    v = torch.randn_like(k, requires_grad=True)
+    o = KERNELS[norm](q, k, v, is_causal=True)
+    o.float().square().mean().backward()
+    ref = oracle.attention_forward(_np(q), _np(k), _np(v), norm, causal=True)
+    assert_close(o, ref, torch.float16, "long-row")
+    assert all(torch.isfinite(t).all() for t in (q.grad, k.grad, v.grad))
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_torch_compile_fullgraph_bf16(norm):
+    def attention(q, k, v):
+        return KERNELS[norm](q, k, v, is_causal=True)
+
+    compiled = torch.compile(attention, fullgraph=True)
+    q = torch.randn(1, 2, 16, 32, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn_like(q, requires_grad=True)
+    v = torch.randn_like(q, requires_grad=True)
+    out = compiled(q, k, v)
+    out.float().square().mean().backward()
+    assert torch.isfinite(out).all()
+    assert all(torch.isfinite(x.grad).all() for x in (q, k, v))
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_hf_qwen3_backend_matches_materialised_path(norm):
+    from transformers.models.qwen3 import Qwen3Config, Qwen3ForCausalLM
+
+    config = Qwen3Config(vocab_size=128, hidden_size=64, intermediate_size=128, num_hidden_layers=1,
+                         num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=64)
+    torch.manual_seed(0)
+    model = Qwen3ForCausalLM(config).to(device="cuda", dtype=torch.float32).train()
+    ids = torch.randint(0, config.vocab_size, (2, 16), device="cuda")
+    H.set_softmax_attention_backend(model, base_backend="flash_attention_3", softmax_fn=norm, mode="strict")
+    assert model.config._attn_implementation == f"{norm}_flash_attention_3"
+    fused = model(ids).logits
+    fused.float().square().mean().backward()
+    assert all(p.grad is None or torch.isfinite(p.grad).all() for p in model.parameters())
+    H.set_softmax_attention_backend(model, base_backend="eager", softmax_fn=norm, mode="strict")
+    assert model.config._attn_implementation == f"{norm}_eager"
+    eager = model(ids).logits
+    assert_close(fused, _np(eager), torch.float32, f"qwen3/{norm}")
