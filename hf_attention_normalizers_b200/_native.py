@@ -41,6 +41,7 @@ class AttnDesc(ctypes.Structure):
         ("len_q", ctypes.c_int32),
         ("len_k", ctypes.c_int32),
         ("total_q", ctypes.c_int32),
+        ("total_k", ctypes.c_int32),
         ("cu_seqlens_q", ctypes.c_void_p),
         ("cu_seqlens_k", ctypes.c_void_p),
         ("scale", ctypes.c_float),

@@ -123,6 +123,7 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   p.cu_q = desc->cu_seqlens_q;
   p.cu_k = desc->cu_seqlens_k;
   p.rows_total = desc->cu_seqlens_q ? desc->total_q : desc->batch * desc->len_q;
+  p.rows_k = desc->cu_seqlens_q ? desc->total_k : desc->len_k;
   p.scale = desc->scale;
   p.causal = desc->causal ? 1 : 0;
   p.window_left = desc->window_left;
@@ -218,9 +219,9 @@ int hfan_attn_bwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan
   p.corr = corr;
   if (desc->len_q == 0 || desc->len_k == 0 || p.rows_total == 0) return HFAN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = tc_supported(desc->dtype, p)
-                      ? tc_attention_bwd(desc->dtype, p, desc->len_q, desc->len_k, s)
-                      : simt_attention_bwd(desc->dtype, p, desc->len_q, desc->len_k, s);
+  cudaError_t e = tc_supported(desc->dtype, p) ? tc_attention_bwd(desc->dtype, p, desc->len_q, desc->len_k, s)
+                                                : cudaErrorNotSupported;
+  if (e == cudaErrorNotSupported) e = simt_attention_bwd(desc->dtype, p, desc->len_q, desc->len_k, s);
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_attn_bwd");
 }
 

@@ -30,6 +30,7 @@ struct AttnParams {
   int batch, hq, hkv, d;
   int len_q, len_k;      // dense lengths; varlen/paged maxima
   int rows_total;        // stats rows per head
+  int64_t rows_k;        // varlen: packed key rows
   const int* cu_q;       // varlen
   const int* cu_k;
   const int* block_table;  // paged

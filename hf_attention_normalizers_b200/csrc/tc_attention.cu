@@ -1,9 +1,643 @@
-// Tensor-core (tcgen05 + TMA) attention kernels for 16-bit inputs.
+// Tensor-core fused attention forward for 16-bit inputs on sm_100a.
+//
+// One CTA computes 128 query rows of one (batch, query head) against all
+// visible keys of its KV head, in key tiles of 128:
+//
+//   warp 4      TMA producer: Q once, then K (and V) tiles into 2-stage rings
+//   warp 5      MMA issuer:   S = Q K^T into a double-buffered TMEM tile,
+//                             O += P V into a TMEM accumulator
+//   warps 0-3   normalizer:   thread i owns query row i (TMEM lane i); reads
+//                             S with tcgen05.ld, writes P (16-bit, 128-byte
+//                             swizzled, K-major) to shared memory, finalises O
+//
+// softmax1 runs one pass with an online max / denominator seeded with the
+// implicit zero logit (m = 0, l = 1; reference kernels/softmax1_hopper.py:80-83);
+// the O accumulator is rescaled lazily, only when a row max grows by more
+// than 2^8.
+//
+// sparsemax / entmax15 need the row threshold tau before any probability is
+// known, so they run a scan pass first (S only, no V): each row keeps the
+// running top-64 scores above (running max - 1) in shared memory; the exact
+// sort-based formula of vutils/entmax.py:35-133 applied to that short list
+// gives tau whenever the support is shorter than the list.  Rows whose
+// support may be longer continue with exact bracket sweeps (common.cuh,
+// tau_step).  The final pass then forms p = (z - tau)_+^a and P V; the output
+// needs no normalisation.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "params.cuh"
+#include "tc_ptx.cuh"
 
 namespace hfan {
-bool tc_supported(int dtype, const AttnParams& p) { (void)dtype; (void)p; return false; }
-cudaError_t tc_attention_fwd(int, const AttnParams&, int, cudaStream_t) { return cudaErrorNotSupported; }
+namespace {
+
+using namespace tc;
+
+constexpr int kBM = 128;           // query rows per CTA
+constexpr int kBN = 128;           // keys per tile
+constexpr int kStages = 2;         // K and V ring depth
+constexpr int kTopC = 64;          // top-k list length per row (scan pass)
+constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
+constexpr uint32_t kHalf = 128u * 128u;  // one 128-row x 128-byte swizzled half tile
+constexpr int kThreads = 192;
+constexpr float kRescaleLog2 = 8.f;
+
+enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2 };
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t p_full, pv_done, ctrl;
+};
+
+struct Ctl {
+  uint32_t tmem_base;
+  int abort;
+  int next_pass;
+  int any_pending;
+};
+
+template <int HD>
+struct Layout {
+  static constexpr int NH = HD / 64;
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t K = Q + NH * kHalf;
+  static constexpr uint32_t V = K + kStages * NH * kHalf;
+  static constexpr uint32_t P = V + kStages * NH * kHalf;
+  static constexpr uint32_t BARS = P + 2 * kHalf;
+  static constexpr uint32_t CTL = BARS + sizeof(Bars);
+  static constexpr uint32_t TOTAL = CTL + sizeof(Ctl) + 1024;  // + alignment slack
+};
+
+// Wait whose outcome is uniform across the warp, so that the warp-collective
+// tcgen05.ld / tcgen05.st that follow are executed by all 32 lanes or none.
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
+  ctl->abort = 1;
+  if (p.dev_status) atomicCAS(p.dev_status, kDevOk, code);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// ------------------------------------------------------------------ top-k
+// The list of one row lives in column `row` of L[kTopC][128], sorted
+// descending.  mrun_m1 = list[0] - 1; thr = the admission threshold.
+struct TopState {
+  int n;
+  bool overflow;
+  float mrun_m1;  // running max - 1 (z units)
+  float thr;      // values <= thr are not inserted
+};
+
+__device__ __noinline__ void topc_insert(float* L, int row, TopState& s, float z) {
+  if (s.n == kTopC) {
+    float last = L[(kTopC - 1) * 128 + row];
+    float new_m1 = fmaxf(s.mrun_m1, z - 1.f);
+    if (last > new_m1) s.overflow = true;  // evicting a still-relevant value
+    s.n = kTopC - 1;
+  }
+  int i = s.n - 1;
+  while (i >= 0) {
+    float e = L[i * 128 + row];
+    if (e >= z) break;
+    L[(i + 1) * 128 + row] = e;
+    --i;
+  }
+  L[(i + 1) * 128 + row] = z;
+  s.n += 1;
+  s.mrun_m1 = L[row] - 1.f;
+  s.thr = s.n == kTopC ? fmaxf(s.mrun_m1, L[(kTopC - 1) * 128 + row]) : s.mrun_m1;
+}
+
+__device__ __forceinline__ void topc_push(float* L, int row, TopState& s, float z) {
+  if (z <= s.thr) {
+    if (z > s.mrun_m1) s.overflow = true;  // relevant but no room
+    return;
+  }
+  topc_insert(L, row, s, z);
+}
+
+// Exact tau from the sorted list (vutils sort formulas, shifted by the top
+// value for conditioning).  Returns true when the list provably contains the
+// whole support; *lower receives a valid lower bound otherwise.
+template <int NORM>
+__device__ bool topc_tau(const float* L, int row, const TopState& s, float* tau, float* lower) {
+  const float z1 = L[row];
+  float s1 = 0.f, s2 = 0.f, tau_rel = 0.f, last_rel = 0.f;
+  int kstar = 0;
+  for (int i = 0; i < s.n; ++i) {
+    float y = L[i * 128 + row] - z1;
+    s1 += y;
+    float k = (float)(i + 1);
+    float t;
+    bool in;
+    if (NORM == HFAN_SPARSEMAX) {
+      t = (s1 - 1.f) / k;
+      in = k * y > s1 - 1.f;
+    } else {
+      s2 += y * y;
+      float mean = s1 / k;
+      float ss = s2 - s1 * mean;
+      float delta = (1.f - ss) / k;
+      t = mean - sqrtf(fmaxf(delta, 0.f));
+      in = t <= y;
+    }
+    if (in) {
+      kstar = i + 1;
+      tau_rel = t;
+    }
+    last_rel = t;
+  }
+  *tau = z1 + tau_rel;
+  *lower = fmaxf(z1 + last_rel, z1 - 1.f);
+  return kstar < s.n || !s.overflow;
+}
+
+// ------------------------------------------------------------------ kernel
+template <int HD, bool BF16, int NORM>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  using L = Layout<HD>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int NH = L::NH;
+  constexpr uint32_t KV_BYTES = NH * kHalf;
+  constexpr uint32_t IDESC_QK = idesc_f16(BF16, kBM, kBN, false, false);
+  constexpr uint32_t IDESC_PV = idesc_f16(BF16, kBM, HD, false, true);
+  constexpr bool SPARSE = NORM != HFAN_SOFTMAX1;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + L::BARS);
+  Ctl* ctl = reinterpret_cast<Ctl*>(smem + L::CTL);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const Geometry g = geometry(p, b);
+  const int q0 = qt * kBM;
+  if (q0 >= g.q_len) return;
+  const int kvh = h / (p.hq / p.hkv);
+  const bool varlen = p.cu_q != nullptr;
+  const int qtok = varlen ? g.q_start + q0 : q0;
+  const int ktok0 = varlen ? g.k_start : 0;
+  const int bcoord = varlen ? 0 : b;
+
+  const int last_row = min(q0 + kBM - 1, g.q_len - 1);
+  int k_hi = g.k_len;
+  if (p.causal) k_hi = min(k_hi, last_row + g.k_len - g.q_len + 1);
+  int k_lo = 0;
+  if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
+  k_lo = (k_lo / kBN) * kBN;
+  const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kBN - 1) / kBN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->s_empty[s], 128);
+    }
+    mbar_init(&bars->p_full, 128);
+    mbar_init(&bars->pv_done, 1);
+    mbar_init(&bars->ctrl, 1);
+    ctl->abort = 0;
+    ctl->next_pass = kPassFinal;
+    ctl->any_pending = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(&ctl->tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const uint32_t tmem_o = tmem + 256;
+  volatile int* abort_flag = &ctl->abort;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_tiles > 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      mbar_arrive_expect_tx(&bars->q_full, NH * kHalf);
+      for (int hh = 0; hh < NH; ++hh)
+        tma_load_4d(smem + L::Q + hh * kHalf, &tm_q, &bars->q_full, 64 * hh, qtok, h, bcoord);
+      uint32_t kc = 0, vc = 0, ctrl_phase = 0;
+      int pass = SPARSE ? kPassTopC : kPassFinal;
+      bool ok = true;
+      while (ok) {
+        const bool fin = pass == kPassFinal;
+        for (int t = 0; t < n_tiles && ok; ++t) {
+          const int kb = k_lo + t * kBN;
+          const int s = kc % kStages;
+          if (!(ok = mbar_wait(&bars->k_empty[s], ((kc / kStages) & 1) ^ 1, abort_flag))) break;
+          mbar_arrive_expect_tx(&bars->k_full[s], KV_BYTES);
+          for (int hh = 0; hh < NH; ++hh)
+            tma_load_4d(smem + L::K + s * KV_BYTES + hh * kHalf, &tm_k, &bars->k_full[s], 64 * hh,
+                        ktok0 + kb, kvh, bcoord);
+          ++kc;
+          if (fin) {
+            const int vs = vc % kStages;
+            if (!(ok = mbar_wait(&bars->v_empty[vs], ((vc / kStages) & 1) ^ 1, abort_flag))) break;
+            mbar_arrive_expect_tx(&bars->v_full[vs], KV_BYTES);
+            for (int hh = 0; hh < NH; ++hh)
+              tma_load_4d(smem + L::V + vs * KV_BYTES + hh * kHalf, &tm_v, &bars->v_full[vs], 64 * hh,
+                          ktok0 + kb, kvh, bcoord);
+            ++vc;
+          }
+        }
+        if (!ok || fin) break;
+        if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
+        ctrl_phase ^= 1;
+        pass = ctl->next_pass;
+      }
+      if (!ok) record_error(p, ctl, kDevWaitTimeout);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t q_base = smem_u32(smem + L::Q);
+      const uint32_t k_base = smem_u32(smem + L::K);
+      const uint32_t v_base = smem_u32(smem + L::V);
+      const uint32_t p_base = smem_u32(smem + L::P);
+      uint32_t kc = 0, vc = 0, sc = 0, pc = 0, ctrl_phase = 0;
+      int pass = SPARSE ? kPassTopC : kPassFinal;
+      bool ok = mbar_wait(&bars->q_full, 0, abort_flag);
+      auto issue_pv = [&](int t) -> bool {
+        const int vs = vc % kStages;
+        if (!mbar_wait(&bars->v_full[vs], (vc / kStages) & 1, abort_flag)) return false;
+        if (!mbar_wait(&bars->p_full, pc & 1, abort_flag)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // A = P [128 x 128 keys], K-major, two 64-key halves; B = V tile,
+          // MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
+          const uint64_t a = sw128_desc(p_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(v_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
+          mma_f16_ss(tmem_o, a, bd, IDESC_PV, t > 0 || kk > 0);
+        }
+        mma_commit(&bars->v_empty[vs]);
+        mma_commit(&bars->pv_done);
+        ++vc;
+        ++pc;
+        return true;
+      };
+      while (ok) {
+        const bool fin = pass == kPassFinal;
+        for (int t = 0; t < n_tiles && ok; ++t) {
+          const int s = kc % kStages;
+          const int sb = sc & 1;
+          if (!(ok = mbar_wait(&bars->k_full[s], (kc / kStages) & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint64_t a = sw128_desc(q_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(k_base + s * KV_BYTES + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+            mma_f16_ss(tmem + sb * 128, a, bd, IDESC_QK, kk > 0);
+          }
+          mma_commit(&bars->s_full[sb]);
+          mma_commit(&bars->k_empty[s]);
+          ++kc;
+          ++sc;
+          if (fin && t >= 1) ok = issue_pv(t - 1);
+        }
+        if (!ok) break;
+        if (fin) {
+          ok = issue_pv(n_tiles - 1);
+          break;
+        }
+        if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
+        ctrl_phase ^= 1;
+        pass = ctl->next_pass;
+      }
+      if (!ok) record_error(p, ctl, kDevWaitTimeout);
+    }
+  } else {
+    // ------------------------------------------------------------ normalizer
+    const int row = threadIdx.x;  // 0..127 == TMEM lane
+    const int i = q0 + row;       // query row within the sequence
+    const bool row_ok = i < g.q_len;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const int limit = i + g.k_len - g.q_len;
+    // visible keys of this row: [vis_lo, vis_hi)
+    int vis_hi = row_ok ? g.k_len : 0;
+    if (p.causal) vis_hi = min(vis_hi, limit + 1);
+    int vis_lo = 0;
+    if (p.window_left > 0) vis_lo = limit - p.window_left + 1;
+    const float zs = NORM == HFAN_SOFTMAX1 ? p.scale * kLog2e
+                                           : (NORM == HFAN_SPARSEMAX ? p.scale : 0.5f * p.scale);
+    float* topl = reinterpret_cast<float*>(smem + L::P);
+    uint8_t* sP = smem + L::P;
+
+    uint32_t sc = 0, pc = 0;
+    bool ok = true;
+    float sreg[kBN];
+    auto load_s = [&](int t) -> bool {
+      const int sb = sc & 1;
+      if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + c * 32, r[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars->s_empty[sb]);
+      ++sc;
+      const int kb = k_lo + t * kBN;
+      const int lo = vis_lo - kb, hi = vis_hi - kb;
+#pragma unroll
+      for (int j = 0; j < kBN; ++j)
+        sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) * zs : kNegInf;
+      return true;
+    };
+
+    // ---- threshold (sparse normalizers)
+    float tau = kPosInf;
+    bool empty_row = false;
+    if (SPARSE) {
+      TopState ts{0, false, kNegInf, kNegInf};
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        if (!(ok = load_s(t))) break;
+#pragma unroll
+        for (int j = 0; j < kBN; ++j) topc_push(topl, row, ts, sreg[j]);
+      }
+      float lower = kNegInf;
+      bool pending = false;
+      if (ts.n == 0) {
+        empty_row = true;
+      } else {
+        pending = !topc_tau<NORM>(topl, row, ts, &tau, &lower);
+      }
+      for (int sweep = 0;; ++sweep) {
+        // CTA-wide decision (uniform across the 128 normalizer threads):
+        // another bracket sweep, or the final pass.
+        named_bar_sync(1, 128);
+        if (row == 0) ctl->any_pending = 0;
+        named_bar_sync(1, 128);
+        if (pending) ctl->any_pending = 1;
+        if (!ok) ctl->abort = 1;
+        named_bar_sync(1, 128);
+        if (row == 0) {
+          const bool more_ = ctl->any_pending != 0 && sweep < kMaxSweeps && ctl->abort == 0;
+          ctl->next_pass = more_ ? kPassSweep : kPassFinal;
+          mbar_arrive(&bars->ctrl);
+        }
+        named_bar_sync(1, 128);
+        if (ctl->next_pass != kPassSweep) break;
+        TauStats st{0.f, 0.f, 0.f, kPosInf};
+        for (int t = 0; t < n_tiles && ok; ++t) {
+          if (!(ok = load_s(t))) break;
+          if (pending) {
+#pragma unroll
+            for (int j = 0; j < kBN; ++j) tau_accumulate(st, sreg[j], lower);
+          }
+        }
+        if (pending && ok) pending = !tau_step(NORM, st, &lower, &tau);
+      }
+    }
+
+    // ---- final pass: P and O
+    float m_ref = 0.f, l = 1.f, support = 0.f;
+    for (int t = 0; t < n_tiles && ok; ++t) {
+      if (!(ok = load_s(t))) break;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (!SPARSE) {
+        float tmax = kNegInf;
+#pragma unroll
+        for (int j = 0; j < kBN; ++j) tmax = fmaxf(tmax, sreg[j]);
+        if (tmax > m_ref + kRescaleLog2) {
+          alpha = exp2f(m_ref - tmax);
+          m_ref = tmax;
+          l *= alpha;
+          rescale = t > 0;
+        }
+        float lsum = 0.f;
+#pragma unroll
+        for (int j = 0; j < kBN; ++j) {
+          float e = exp2f(sreg[j] - m_ref);  // exp2(-inf) = 0 for masked keys
+          sreg[j] = e;
+          lsum += e;
+        }
+        l += lsum;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kBN; ++j) {
+          float pj = empty_row ? 0.f : sparse_prob(NORM, sreg[j], tau);
+          support += pj > 0.f ? 1.f : 0.f;
+          sreg[j] = pj;
+        }
+      }
+      // P buffer and O are free once the previous P V has completed.
+      if (t > 0) {
+        if (!(ok = wait_warp(&bars->pv_done, (pc - 1) & 1, abort_flag))) break;
+        tc_fence_after();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // warp-collective: lanes without a rescale multiply by one
+        const float f = rescale ? alpha : 1.f;
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          tmem_ld32(tmem_o + lane_addr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
+          tmem_st32(tmem_o + lane_addr + c * 32, r);
+        }
+        tmem_wait_st();
+      }
+      // P row -> shared memory, 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
+#pragma unroll
+      for (int c = 0; c < kBN / 8; ++c) {
+        const int hh = c >> 3, cc = c & 7;
+        uint4 v;
+        v.x = pack2<BF16>(sreg[c * 8 + 0], sreg[c * 8 + 1]);
+        v.y = pack2<BF16>(sreg[c * 8 + 2], sreg[c * 8 + 3]);
+        v.z = pack2<BF16>(sreg[c * 8 + 4], sreg[c * 8 + 5]);
+        v.w = pack2<BF16>(sreg[c * 8 + 6], sreg[c * 8 + 7]);
+        *reinterpret_cast<uint4*>(sP + hh * kHalf + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full);
+      ++pc;
+    }
+    if (ok && n_tiles > 0) {
+      ok = wait_warp(&bars->pv_done, (pc - 1) & 1, abort_flag);
+      tc_fence_after();
+    }
+    if (!ok) record_error(p, ctl, kDevWaitTimeout);
+
+    // ---- epilogue: O row -> global, row statistics.  The TMEM loads are
+    // warp-collective, so every lane loads; only valid rows store.
+    {
+      const float inv = SPARSE ? 1.f : 1.f / l;
+      T* orow = static_cast<T*>(p.o) + qrow_off(p, g, b, h, row_ok ? i : 0, p.o_sb, p.o_sh, p.o_st);
+      uint32_t r[32];
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        if (n_tiles > 0) {
+          tmem_ld32(tmem_o + lane_addr + c * 32, r);
+          tmem_wait_ld();
+        }
+        if (n_tiles == 0 || !ok) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 v;
+            v.x = pack2<BF16>(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
+            v.y = pack2<BF16>(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+            v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
+            v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + j) = v;
+          }
+        }
+      }
+    }
+    if (row_ok) {
+      const int64_t si = stat_index(p, g, h, i);
+      if (SPARSE) {
+        p.stats[si] = empty_row ? kPosInf : tau;
+        p.stats[(int64_t)p.hq * p.rows_total + si] = support;
+      } else {
+        p.stats[si] = m_ref;
+        p.stats[(int64_t)p.hq * p.rows_total + si] = l;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 4-D map (dim, token, head, batch) with a 64 x 128 x 1 x 1 box, 128-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t tokens, int heads, int batch,
+              int64_t st, int64_t sh, int64_t sb) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+bool stride_ok(int64_t s) { return s > 0 && (s % 8) == 0 && s < ((int64_t)1 << 38); }
+
+template <int HD, bool BF16>
+cudaError_t launch_fwd(const AttnParams& p, int max_q, cudaStream_t stream) {
+  const bool varlen = p.cu_q != nullptr;
+  CUtensorMap tq, tk, tv;
+  // Token extent: dense maps cover one sequence (rows past it read as zero);
+  // packed varlen maps cover all packed rows.
+  const int64_t tq_n = varlen ? p.rows_total : p.len_q;
+  const int64_t tk_n = varlen ? p.rows_k : p.len_k;
+  const int batch = varlen ? 1 : p.batch;
+  const int64_t q_sb = varlen ? tq_n * p.q_st : p.q_sb;
+  const int64_t k_sb = varlen ? tk_n * p.k_st : p.k_sb;
+  const int64_t v_sb = varlen ? tk_n * p.v_st : p.v_sb;
+  if (!make_map(&tq, p.q, BF16, HD, tq_n, p.hq, batch, p.q_st, p.q_sh, q_sb) ||
+      !make_map(&tk, p.k, BF16, HD, tk_n, p.hkv, batch, p.k_st, p.k_sh, k_sb) ||
+      !make_map(&tv, p.v, BF16, HD, tk_n, p.hkv, batch, p.v_st, p.v_sh, v_sb))
+    return cudaErrorInvalidValue;
+  const size_t smem = Layout<HD>::TOTAL;
+  dim3 grid((max_q + kBM - 1) / kBM, p.hq, p.batch);
+  cudaError_t e;
+  switch (p.norm) {
+    case HFAN_SOFTMAX1:
+      e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+      break;
+    case HFAN_SPARSEMAX:
+      e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+      break;
+    default:
+      e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_supported(int dtype, const AttnParams& p) {
+  if (dtype != HFAN_BFLOAT16 && dtype != HFAN_FLOAT16) return false;
+  if (p.paged) return false;
+  if (p.d != 64 && p.d != 128) return false;
+  if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v) || !aligned16(p.o)) return false;
+  if (!stride_ok(p.q_st) || !stride_ok(p.q_sh) || !stride_ok(p.k_st) || !stride_ok(p.k_sh) ||
+      !stride_ok(p.v_st) || !stride_ok(p.v_sh) || (p.o_st % 8) != 0 || (p.o_sh % 8) != 0)
+    return false;
+  if (p.cu_q == nullptr) {
+    if ((p.batch > 1) && (!stride_ok(p.q_sb) || !stride_ok(p.k_sb) || !stride_ok(p.v_sb))) return false;
+    if (p.batch > 1 && (p.o_sb % 8) != 0) return false;
+  } else {
+    if (p.rows_k <= 0) return false;  // packed key rows bound the K/V maps
+  }
+  return true;
+}
+
+cudaError_t tc_attention_fwd(int dtype, const AttnParams& p, int max_q, cudaStream_t s) {
+  const bool bf16 = dtype == HFAN_BFLOAT16;
+  if (p.d == 128) return bf16 ? launch_fwd<128, true>(p, max_q, s) : launch_fwd<128, false>(p, max_q, s);
+  return bf16 ? launch_fwd<64, true>(p, max_q, s) : launch_fwd<64, false>(p, max_q, s);
+}
+
 cudaError_t tc_attention_bwd(int, const AttnParams&, int, int, cudaStream_t) { return cudaErrorNotSupported; }
+
 }  // namespace hfan

@@ -70,7 +70,7 @@ def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None) -
     b, hq, lq, d = q.shape
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=k.shape[1],
-        head_dim=d, len_q=lq, len_k=k.shape[2], total_q=b * lq, cu_seqlens_q=None,
+        head_dim=d, len_q=lq, len_k=k.shape[2], total_q=b * lq, total_k=k.shape[0] * k.shape[2], cu_seqlens_q=None,
         cu_seqlens_k=None, scale=float(scale), causal=int(bool(causal)),
         window_left=int(window_left), grad_dtype=dtype_id(q) if grad_dtype is None else grad_dtype)
 
@@ -159,7 +159,7 @@ def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal) -> N
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=cu_q.numel() - 1, heads_q=q.shape[1],
         heads_kv=k.shape[1], head_dim=q.shape[2], len_q=int(max_q), len_k=int(max_k),
-        total_q=q.shape[0], cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=cu_k.data_ptr(),
+        total_q=q.shape[0], total_k=k.shape[0], cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=cu_k.data_ptr(),
         scale=float(scale), causal=int(bool(causal)), window_left=0, grad_dtype=dtype_id(q))
 
 

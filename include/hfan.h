@@ -85,6 +85,7 @@ typedef struct hfan_attn_desc {
   int32_t len_q;        /* dense: query length; varlen: max query length              */
   int32_t len_k;        /* dense: key length;   varlen: max key length                */
   int32_t total_q;      /* varlen: packed query tokens (rows of q); dense: ignored    */
+  int32_t total_k;      /* varlen: packed key tokens (rows of k, v); dense: ignored   */
   const int32_t* cu_seqlens_q; /* varlen: [batch+1] device offsets, else NULL         */
   const int32_t* cu_seqlens_k; /* varlen: [batch+1] device offsets, else NULL         */
   float scale;
