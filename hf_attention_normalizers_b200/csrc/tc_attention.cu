@@ -16,13 +16,13 @@
 // than 2^8.
 //
 // sparsemax / entmax15 need the row threshold tau before any probability is
-// known, so they run a scan pass first (S only, no V): each row keeps the
-// running top-64 scores above (running max - 1) in shared memory; the exact
-// sort-based formula of vutils/entmax.py:35-133 applied to that short list
-// gives tau whenever the support is shorter than the list.  Rows whose
-// support may be longer continue with exact bracket sweeps (common.cuh,
-// tau_step).  The final pass then forms p = (z - tau)_+^a and P V; the output
-// needs no normalisation.
+// known, so they run a scan pass first (S only, no V).  Each row appends the
+// scores above a rising lower bound of tau to a shared-memory candidate
+// buffer (see Cand below); solving the threshold equation on that buffer gives
+// the exact tau of vutils/entmax.py:35-133 without sorting.  Rows whose
+// candidates outgrow the buffer continue with exact bracket sweeps over the
+// whole row (common.cuh, tau_step).  The final pass then forms
+// p = (z - tau)_+^a and P V; the output needs no normalisation.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,7 +38,6 @@ using namespace tc;
 constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kStages = 2;         // K and V ring depth
-constexpr int kTopC = 64;          // top-k list length per row (scan pass)
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
 constexpr uint32_t kHalf = 128u * 128u;  // one 128-row x 128-byte swizzled half tile
 constexpr int kThreads = 192;
@@ -96,78 +95,59 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-// ------------------------------------------------------------------ top-k
-// The list of one row lives in column `row` of L[kTopC][128], sorted
-// descending.  mrun_m1 = list[0] - 1; thr = the admission threshold.
-struct TopState {
-  int n;
-  bool overflow;
-  float mrun_m1;  // running max - 1 (z units)
-  float thr;      // values <= thr are not inserted
+// ------------------------------------------------------------------ candidates
+// Scan-pass state of one row.  Scores above the admission threshold `thr`
+// (z units) are appended, unsorted, to the row's column of a shared-memory
+// buffer buf[cap][128].  thr only rises and is always a lower bound of tau:
+// it starts at (running max - 1) and is lifted to the exact threshold of the
+// buffered candidates alone, whose f_A(t) = sum_A (z - t)_+^a never exceeds
+// the row's f(t).  Every score above the final thr is therefore in the
+// buffer, and the threshold solved on the buffer is the row's exact tau.
+struct Cand {
+  int n;          // buffered entries (some may be <= thr: dead, ignored)
+  bool overflow;  // more live candidates than the buffer holds
+  float thr;      // admission threshold, z units
+  float thr_s;    // the same threshold in raw-score units (thr / zs)
 };
 
-__device__ __noinline__ void topc_insert(float* L, int row, TopState& s, float z) {
-  if (s.n == kTopC) {
-    float last = L[(kTopC - 1) * 128 + row];
-    float new_m1 = fmaxf(s.mrun_m1, z - 1.f);
-    if (last > new_m1) s.overflow = true;  // evicting a still-relevant value
-    s.n = kTopC - 1;
-  }
-  int i = s.n - 1;
-  while (i >= 0) {
-    float e = L[i * 128 + row];
-    if (e >= z) break;
-    L[(i + 1) * 128 + row] = e;
-    --i;
-  }
-  L[(i + 1) * 128 + row] = z;
-  s.n += 1;
-  s.mrun_m1 = L[row] - 1.f;
-  s.thr = s.n == kTopC ? fmaxf(s.mrun_m1, L[(kTopC - 1) * 128 + row]) : s.mrun_m1;
-}
-
-__device__ __forceinline__ void topc_push(float* L, int row, TopState& s, float z) {
-  if (z <= s.thr) {
-    if (z > s.mrun_m1) s.overflow = true;  // relevant but no room
-    return;
-  }
-  topc_insert(L, row, s, z);
-}
-
-// Exact tau from the sorted list (vutils sort formulas, shifted by the top
-// value for conditioning).  Returns true when the list provably contains the
-// whole support; *lower receives a valid lower bound otherwise.
+// Solve f_A(t) = 1 on the buffered candidates starting from the lower bound
+// t0 (exact bracket + closed form of common.cuh).  Returns the root (or the
+// best lower bound after `max_iter` steps) and its support size.
 template <int NORM>
-__device__ bool topc_tau(const float* L, int row, const TopState& s, float* tau, float* lower) {
-  const float z1 = L[row];
-  float s1 = 0.f, s2 = 0.f, tau_rel = 0.f, last_rel = 0.f;
-  int kstar = 0;
-  for (int i = 0; i < s.n; ++i) {
-    float y = L[i * 128 + row] - z1;
-    s1 += y;
-    float k = (float)(i + 1);
-    float t;
-    bool in;
-    if (NORM == HFAN_SPARSEMAX) {
-      t = (s1 - 1.f) / k;
-      in = k * y > s1 - 1.f;
-    } else {
-      s2 += y * y;
-      float mean = s1 / k;
-      float ss = s2 - s1 * mean;
-      float delta = (1.f - ss) / k;
-      t = mean - sqrtf(fmaxf(delta, 0.f));
-      in = t <= y;
+__device__ float buffer_solve(const float* buf, int row, int n, float t0, int max_iter, bool* exact,
+                              float* support) {
+  float t = t0, tau = t0;
+  *exact = false;
+  for (int it = 0; it < max_iter; ++it) {
+    TauStats st{0.f, 0.f, 0.f, kPosInf};
+    for (int e = 0; e < n; ++e) tau_accumulate(st, buf[e * 128 + row], t);
+    *support = st.cnt;
+    if (st.cnt == 0.f) break;
+    if (tau_step(NORM, st, &t, &tau)) {
+      *exact = true;
+      return tau;
     }
-    if (in) {
-      kstar = i + 1;
-      tau_rel = t;
-    }
-    last_rel = t;
   }
-  *tau = z1 + tau_rel;
-  *lower = fmaxf(z1 + last_rel, z1 - 1.f);
-  return kstar < s.n || !s.overflow;
+  return t;
+}
+
+// Raise thr to the buffer's own threshold and drop dead entries.
+template <int NORM>
+__device__ __noinline__ void buffer_compact(float* buf, int row, Cand& c, int cap, float zs) {
+  bool exact;
+  float sup;
+  float root = buffer_solve<NORM>(buf, row, c.n, c.thr, 8, &exact, &sup);
+  if (root > c.thr) {
+    c.thr = root;
+    c.thr_s = root / zs;
+  }
+  int live = 0;
+  for (int e = 0; e < c.n; ++e) {
+    float z = buf[e * 128 + row];
+    if (z > c.thr) buf[live++ * 128 + row] = z;
+  }
+  c.n = live;
+  if (live > (3 * cap) / 4) c.overflow = true;
 }
 
 // ------------------------------------------------------------------ kernel
@@ -350,12 +330,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.window_left > 0) vis_lo = limit - p.window_left + 1;
     const float zs = NORM == HFAN_SOFTMAX1 ? p.scale * kLog2e
                                            : (NORM == HFAN_SPARSEMAX ? p.scale : 0.5f * p.scale);
-    float* topl = reinterpret_cast<float*>(smem + L::P);
+    // During the scan passes the V ring and the P buffer are idle; they hold
+    // the candidate buffer (the producer loads V only in the final pass).
+    float* cbuf = reinterpret_cast<float*>(smem + L::V);
+    constexpr int CAP = (int)((kStages * NH * kHalf + 2 * kHalf) / (128 * 4));
     uint8_t* sP = smem + L::P;
 
     uint32_t sc = 0, pc = 0;
     bool ok = true;
-    float sreg[kBN];
+    float sreg[kBN];  // raw scores s = q.k of the current tile (masked: -inf)
     auto load_s = [&](int t) -> bool {
       const int sb = sc & 1;
       if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
@@ -369,28 +352,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++sc;
       const int kb = k_lo + t * kBN;
       const int lo = vis_lo - kb, hi = vis_hi - kb;
+      if (__all_sync(0xffffffffu, lo <= 0 && hi >= kBN)) {
 #pragma unroll
-      for (int j = 0; j < kBN; ++j)
-        sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) * zs : kNegInf;
+        for (int j = 0; j < kBN; ++j) sreg[j] = __uint_as_float(r[j >> 5][j & 31]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kBN; ++j) sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) : kNegInf;
+      }
       return true;
     };
 
     // ---- threshold (sparse normalizers)
-    float tau = kPosInf;
-    bool empty_row = false;
+    float tau = kPosInf, support = 0.f;
     if (SPARSE) {
-      TopState ts{0, false, kNegInf, kNegInf};
+      Cand cd{0, false, kNegInf, kNegInf};
+      float zmax = kNegInf;
       for (int t = 0; t < n_tiles && ok; ++t) {
         if (!(ok = load_s(t))) break;
+        float tm = kNegInf;
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) topc_push(topl, row, ts, sreg[j]);
+        for (int j = 0; j < kBN; ++j) tm = fmaxf(tm, sreg[j]);
+        zmax = fmaxf(zmax, tm * zs);
+        if (zmax - 1.f > cd.thr) {
+          cd.thr = zmax - 1.f;
+          cd.thr_s = cd.thr / zs;
+        }
+        if (!cd.overflow && tm > cd.thr_s) {
+#pragma unroll
+          for (int j = 0; j < kBN; ++j) {
+            if (sreg[j] > cd.thr_s) {
+              if (cd.n == CAP) buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
+              if (!cd.overflow) cbuf[cd.n++ * 128 + row] = sreg[j] * zs;
+            }
+          }
+        }
+        if (__any_sync(0xffffffffu, cd.n > CAP / 2 && !cd.overflow)) {
+          if (cd.n > CAP / 4 && !cd.overflow) buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
+        }
       }
-      float lower = kNegInf;
+      // exact threshold from the buffer, or a lower bound for bracket sweeps
+      float lower = cd.thr;
       bool pending = false;
-      if (ts.n == 0) {
-        empty_row = true;
+      if (!(zmax > kNegInf)) {
+        tau = kPosInf;  // no visible key: zero row
+      } else if (!cd.overflow) {
+        bool exact;
+        float t_or_root = buffer_solve<NORM>(cbuf, row, cd.n, cd.thr, 64, &exact, &support);
+        if (exact) {
+          tau = t_or_root;
+        } else {
+          pending = true;
+          lower = t_or_root;
+        }
       } else {
-        pending = !topc_tau<NORM>(topl, row, ts, &tau, &lower);
+        pending = true;
       }
       for (int sweep = 0;; ++sweep) {
         // CTA-wide decision (uniform across the 128 normalizer threads):
@@ -413,33 +428,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = load_s(t))) break;
           if (pending) {
 #pragma unroll
-            for (int j = 0; j < kBN; ++j) tau_accumulate(st, sreg[j], lower);
+            for (int j = 0; j < kBN; ++j) tau_accumulate(st, sreg[j] * zs, lower);
           }
         }
-        if (pending && ok) pending = !tau_step(NORM, st, &lower, &tau);
+        if (pending && ok) {
+          support = st.cnt;
+          pending = !tau_step(NORM, st, &lower, &tau);
+        }
       }
     }
 
     // ---- final pass: P and O
-    float m_ref = 0.f, l = 1.f, support = 0.f;
+    float m_ref = 0.f, l = 1.f;
+    const float ntau = -tau;
     for (int t = 0; t < n_tiles && ok; ++t) {
       if (!(ok = load_s(t))) break;
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
+        // log2 units: x = s * scale * log2(e)
         float tmax = kNegInf;
 #pragma unroll
         for (int j = 0; j < kBN; ++j) tmax = fmaxf(tmax, sreg[j]);
+        tmax *= zs;
         if (tmax > m_ref + kRescaleLog2) {
           alpha = exp2f(m_ref - tmax);
           m_ref = tmax;
           l *= alpha;
           rescale = t > 0;
         }
+        const float nm = -m_ref;
         float lsum = 0.f;
 #pragma unroll
         for (int j = 0; j < kBN; ++j) {
-          float e = exp2f(sreg[j] - m_ref);  // exp2(-inf) = 0 for masked keys
+          float e = exp2f(fmaf(sreg[j], zs, nm));  // exp2(-inf) = 0 for masked keys
           sreg[j] = e;
           lsum += e;
         }
@@ -447,9 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
 #pragma unroll
         for (int j = 0; j < kBN; ++j) {
-          float pj = empty_row ? 0.f : sparse_prob(NORM, sreg[j], tau);
-          support += pj > 0.f ? 1.f : 0.f;
-          sreg[j] = pj;
+          float d = fmaxf(fmaf(sreg[j], zs, ntau), 0.f);
+          sreg[j] = NORM == HFAN_SPARSEMAX ? d : d * d;
         }
       }
       // P buffer and O are free once the previous P V has completed.
@@ -525,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (row_ok) {
       const int64_t si = stat_index(p, g, h, i);
       if (SPARSE) {
-        p.stats[si] = empty_row ? kPosInf : tau;
+        p.stats[si] = tau;
         p.stats[(int64_t)p.hq * p.rows_total + si] = support;
       } else {
         p.stats[si] = m_ref;
