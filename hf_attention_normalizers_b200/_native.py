@@ -11,7 +11,7 @@ import ctypes
 import os
 import threading
 
-_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libhfan.so")
+_LIB_PATH = os.environ.get("HFAN_LIBRARY") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libhfan.so")
 _lock = threading.Lock()
 _lib = None
 

@@ -131,9 +131,10 @@ __device__ float buffer_solve(const float* buf, int row, int n, float t0, int ma
   return t;
 }
 
-// Raise thr to the buffer's own threshold and drop dead entries.
+// Raise thr to the buffer's own threshold and drop dead entries.  State is
+// passed by value so that callers keep it in registers.
 template <int NORM>
-__device__ __noinline__ void buffer_compact(float* buf, int row, Cand& c, int cap, float zs) {
+__device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap, float zs) {
   bool exact;
   float sup;
   float root = buffer_solve<NORM>(buf, row, c.n, c.thr, 8, &exact, &sup);
@@ -148,6 +149,7 @@ __device__ __noinline__ void buffer_compact(float* buf, int row, Cand& c, int ca
   }
   c.n = live;
   if (live > (3 * cap) / 4) c.overflow = true;
+  return c;
 }
 
 // ------------------------------------------------------------------ kernel
@@ -162,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC_QK = idesc_f16(BF16, kBM, kBN, false, false);
   constexpr uint32_t IDESC_PV = idesc_f16(BF16, kBM, HD, false, true);
   constexpr bool SPARSE = NORM != HFAN_SOFTMAX1;
+#ifndef HFAN_EXP
+#define HFAN_EXP 0
+#endif
+  constexpr bool SCAN = SPARSE && HFAN_EXP != 2;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -226,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int hh = 0; hh < NH; ++hh)
         tma_load_4d(smem + L::Q + hh * kHalf, &tm_q, &bars->q_full, 64 * hh, qtok, h, bcoord);
       uint32_t kc = 0, vc = 0, ctrl_phase = 0;
-      int pass = SPARSE ? kPassTopC : kPassFinal;
+      int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = true;
       while (ok) {
         const bool fin = pass == kPassFinal;
@@ -264,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t v_base = smem_u32(smem + L::V);
       const uint32_t p_base = smem_u32(smem + L::P);
       uint32_t kc = 0, vc = 0, sc = 0, pc = 0, ctrl_phase = 0;
-      int pass = SPARSE ? kPassTopC : kPassFinal;
+      int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = mbar_wait(&bars->q_full, 0, abort_flag);
       auto issue_pv = [&](int t) -> bool {
         const int vs = vc % kStages;
@@ -364,30 +370,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- threshold (sparse normalizers)
     float tau = kPosInf, support = 0.f;
-    if (SPARSE) {
+    if (SCAN) {
       Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
       for (int t = 0; t < n_tiles && ok; ++t) {
         if (!(ok = load_s(t))) break;
+        // chunk maxima (8 keys each) gate the candidate appends
+        float cm[kBN / 8];
         float tm = kNegInf;
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) tm = fmaxf(tm, sreg[j]);
+        for (int c = 0; c < kBN / 8; ++c) {
+          float m8 = sreg[c * 8];
+#pragma unroll
+          for (int e = 1; e < 8; ++e) m8 = fmaxf(m8, sreg[c * 8 + e]);
+          cm[c] = m8;
+          tm = fmaxf(tm, m8);
+        }
         zmax = fmaxf(zmax, tm * zs);
         if (zmax - 1.f > cd.thr) {
           cd.thr = zmax - 1.f;
           cd.thr_s = cd.thr / zs;
         }
-        if (!cd.overflow && tm > cd.thr_s) {
+        if (HFAN_EXP != 1 && !cd.overflow && tm > cd.thr_s) {
 #pragma unroll
-          for (int j = 0; j < kBN; ++j) {
-            if (sreg[j] > cd.thr_s) {
-              if (cd.n == CAP) buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
-              if (!cd.overflow) cbuf[cd.n++ * 128 + row] = sreg[j] * zs;
+          for (int c = 0; c < kBN / 8; ++c) {
+            if (!cd.overflow && cm[c] > cd.thr_s) {
+              if (cd.n > CAP - 8) cd = buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
+              if (!cd.overflow) {
+                // predicated appends: every value is written at slot n, and n
+                // only advances past the candidates
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float x = sreg[c * 8 + e];
+                  cbuf[cd.n * 128 + row] = x * zs;
+                  cd.n += x > cd.thr_s ? 1 : 0;
+                }
+              }
             }
           }
         }
         if (__any_sync(0xffffffffu, cd.n > CAP / 2 && !cd.overflow)) {
-          if (cd.n > CAP / 4 && !cd.overflow) buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
+          if (cd.n > CAP / 4 && !cd.overflow) cd = buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
         }
       }
       // exact threshold from the buffer, or a lower bound for bracket sweeps
