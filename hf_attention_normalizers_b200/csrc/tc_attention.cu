@@ -29,6 +29,7 @@
 #include "common.cuh"
 #include "params.cuh"
 #include "tc_ptx.cuh"
+#include "tc_common.cuh"
 
 namespace hfan {
 namespace {
@@ -39,7 +40,6 @@ constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kStages = 2;         // K and V ring depth
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
-constexpr uint32_t kHalf = 128u * 128u;  // one 128-row x 128-byte swizzled half tile
 constexpr int kThreads = 192;
 constexpr float kRescaleLog2 = 8.f;
 
@@ -72,27 +72,9 @@ struct Layout {
   static constexpr uint32_t TOTAL = CTL + sizeof(Ctl) + 1024;  // + alignment slack
 };
 
-// Wait whose outcome is uniform across the warp, so that the warp-collective
-// tcgen05.ld / tcgen05.st that follow are executed by all 32 lanes or none.
-__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  bool ok = mbar_wait(bar, parity, abort);
-  return __all_sync(0xffffffffu, ok);
-}
-
 __device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
   ctl->abort = 1;
   if (p.dev_status) atomicCAS(p.dev_status, kDevOk, code);
-}
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if (BF16) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-  } else {
-    __half2 v = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
 }
 
 // ------------------------------------------------------------------ candidates
@@ -588,36 +570,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-// 4-D map (dim, token, head, batch) with a 64 x 128 x 1 x 1 box, 128-byte swizzle.
-bool make_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t tokens, int heads, int batch,
-              int64_t st, int64_t sh, int64_t sb) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)batch};
-  cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
-bool stride_ok(int64_t s) { return s > 0 && (s % 8) == 0 && s < ((int64_t)1 << 38); }
-
 template <int HD, bool BF16>
 cudaError_t launch_fwd(const AttnParams& p, int max_q, cudaStream_t stream) {
   const bool varlen = p.cu_q != nullptr;
@@ -682,6 +634,5 @@ cudaError_t tc_attention_fwd(int dtype, const AttnParams& p, int max_q, cudaStre
   return bf16 ? launch_fwd<64, true>(p, max_q, s) : launch_fwd<64, false>(p, max_q, s);
 }
 
-cudaError_t tc_attention_bwd(int, const AttnParams&, int, int, cudaStream_t) { return cudaErrorNotSupported; }
 
 }  // namespace hfan

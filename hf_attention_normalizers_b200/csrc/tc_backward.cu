@@ -1,0 +1,746 @@
+// Tensor-core fused attention backward for 16-bit inputs on sm_100a.
+//
+// Two kernels, both with the forward's warp roles (warp 4: TMA producer,
+// warp 5: MMA issuer, warps 0-3: one tile row per thread, TMEM lane == row):
+//
+// dq kernel  (one CTA per 128 query rows of one (batch, query head))
+//     per key tile:  S = Q K^T, dP = dO V^T          (TMEM, f32)
+//                    dS = w (dP - c)                  (registers -> smem, 16-bit)
+//                    dQ += dS K                       (TMEM, K reused as an MN-major operand)
+//     w = p for softmax1 (p = exp2(s log2e scale - m) / l from the saved row
+//     statistics) and w = 1[p>0] (sparsemax) or sqrt(p) (entmax15): the
+//     closed-form backwards of vutils/entmax.py:148-157 and :175-183 and the
+//     softmax Jacobian.  The row correction c is sum_j w dP / sum_j w for the
+//     sparse normalizers (a first pass over the key tiles) and O . dO for
+//     softmax1 (the implicit sink has value 0).  c is saved for the dk/dv
+//     kernel.
+//
+// dk/dv kernel  (one CTA per 128 keys of one (batch, KV head); it walks every
+//                query head of the KV group, so GQA needs no atomics)
+//     per query tile:  S^T = K Q^T, dP^T = V dO^T      (TMEM)
+//                      P^T, dS^T                        (registers -> smem)
+//                      dV += P^T dO,  dK += dS^T Q      (TMEM accumulators)
+//
+// Gradients are written in the input dtype; dK carries the softmax scale.
+#include "common.cuh"
+#include "params.cuh"
+#include "tc_common.cuh"
+#include "tc_ptx.cuh"
+
+namespace hfan {
+namespace {
+
+using namespace tc;
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kThreads = 192;
+
+template <int NORM> __device__ __forceinline__ float zscale(float scale) {
+  return NORM == HFAN_SOFTMAX1 ? scale * kLog2e : (NORM == HFAN_SPARSEMAX ? scale : 0.5f * scale);
+}
+
+// Weight w and probability p of one score (z units) given the row statistics.
+template <int NORM>
+__device__ __forceinline__ void weight(float z, float st0, float inv_l, float* w, float* pr) {
+  if (NORM == HFAN_SOFTMAX1) {
+    float e = exp2f(z - st0) * inv_l;
+    *w = e;
+    *pr = e;
+  } else {
+    float d = z - st0;
+    if (d > 0.f) {
+      *w = NORM == HFAN_SPARSEMAX ? 1.f : d;
+      *pr = NORM == HFAN_SPARSEMAX ? d : d * d;
+    } else {
+      *w = 0.f;
+      *pr = 0.f;
+    }
+  }
+}
+
+// =========================================================== dq kernel
+struct QBars {
+  uint64_t qd_full;
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t sdp_full, sdp_empty, ds_full, ds_empty, dq_done;
+};
+
+template <int HD>
+struct QLayout {
+  static constexpr int NH = HD / 64;
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t DO = Q + NH * kHalf;
+  static constexpr uint32_t K = DO + NH * kHalf;
+  static constexpr uint32_t V = K + 2 * NH * kHalf;
+  static constexpr uint32_t DS = V + 2 * NH * kHalf;
+  static constexpr uint32_t BARS = DS + 2 * kHalf;
+  static constexpr uint32_t CTL = BARS + sizeof(QBars);
+  static constexpr uint32_t TOTAL = CTL + 16 + 1024;
+};
+
+template <int HD, bool BF16, int NORM>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                     const AttnParams p) {
+  using L = QLayout<HD>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int NH = L::NH;
+  constexpr uint32_t TILE = NH * kHalf;
+  constexpr bool SPARSE = NORM != HFAN_SOFTMAX1;
+  constexpr int NPASS = SPARSE ? 2 : 1;
+  constexpr uint32_t IDESC_S = idesc_f16(BF16, kBM, kBN, false, false);
+  constexpr uint32_t IDESC_DQ = idesc_f16(BF16, kBM, HD, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  QBars* bars = reinterpret_cast<QBars*>(smem + L::BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::CTL);
+  int* abort_ptr = reinterpret_cast<int*>(smem + L::CTL + 4);
+  volatile int* abort_flag = abort_ptr;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int qt = gridDim.x - 1 - blockIdx.x;
+  const Geometry g = geometry(p, b);
+  const int q0 = qt * kBM;
+  if (q0 >= g.q_len) return;
+  const int kvh = h / (p.hq / p.hkv);
+  const bool varlen = p.cu_q != nullptr;
+  const int qtok = varlen ? g.q_start + q0 : q0;
+  const int ktok0 = varlen ? g.k_start : 0;
+  const int bcoord = varlen ? 0 : b;
+
+  const int last_row = min(q0 + kBM - 1, g.q_len - 1);
+  int k_hi = g.k_len;
+  if (p.causal) k_hi = min(k_hi, last_row + g.k_len - g.q_len + 1);
+  int k_lo = 0;
+  if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
+  k_lo = (k_lo / kBN) * kBN;
+  const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kBN - 1) / kBN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->qd_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    mbar_init(&bars->sdp_full, 1);
+    mbar_init(&bars->sdp_empty, 128);
+    mbar_init(&bars->ds_full, 128);
+    mbar_init(&bars->ds_empty, 1);
+    mbar_init(&bars->dq_done, 1);
+    *abort_ptr = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dq = tmem + 256;
+
+  if (warp == 4) {
+    if (lane == 0 && n_tiles > 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_do);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      mbar_arrive_expect_tx(&bars->qd_full, 2 * TILE);
+      for (int hh = 0; hh < NH; ++hh) {
+        tma_load_4d(smem + L::Q + hh * kHalf, &tm_q, &bars->qd_full, 64 * hh, qtok, h, bcoord);
+        tma_load_4d(smem + L::DO + hh * kHalf, &tm_do, &bars->qd_full, 64 * hh, qtok, h, bcoord);
+      }
+      bool ok = true;
+      uint32_t kc = 0;
+      for (int pass = 0; pass < NPASS && ok; ++pass) {
+        for (int t = 0; t < n_tiles && ok; ++t) {
+          const int kb = k_lo + t * kBN;
+          const int s = kc & 1;
+          const uint32_t ph = ((kc >> 1) & 1) ^ 1;
+          if (!(ok = mbar_wait(&bars->k_empty[s], ph, abort_flag))) break;
+          mbar_arrive_expect_tx(&bars->k_full[s], TILE);
+          for (int hh = 0; hh < NH; ++hh)
+            tma_load_4d(smem + L::K + s * TILE + hh * kHalf, &tm_k, &bars->k_full[s], 64 * hh, ktok0 + kb, kvh, bcoord);
+          if (!(ok = mbar_wait(&bars->v_empty[s], ph, abort_flag))) break;
+          mbar_arrive_expect_tx(&bars->v_full[s], TILE);
+          for (int hh = 0; hh < NH; ++hh)
+            tma_load_4d(smem + L::V + s * TILE + hh * kHalf, &tm_v, &bars->v_full[s], 64 * hh, ktok0 + kb, kvh, bcoord);
+          ++kc;
+        }
+      }
+      if (!ok) {
+        *abort_ptr = 1;
+        if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
+      const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
+      const uint32_t ds_base = smem_u32(smem + L::DS);
+      bool ok = mbar_wait(&bars->qd_full, 0, abort_flag);
+      uint32_t kc = 0, sdc = 0, dsc = 0;
+      auto issue_dq = [&](int s, int t) -> bool {
+        if (!mbar_wait(&bars->ds_full, dsc & 1, abort_flag)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t a = sw128_desc(ds_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(k_base + s * TILE + kk * 16 * 128, kHalf, 1024);
+          mma_f16_ss(tmem_dq, a, bd, IDESC_DQ, t > 0 || kk > 0);
+        }
+        mma_commit(&bars->k_empty[s]);
+        mma_commit(&bars->ds_empty);
+        ++dsc;
+        return true;
+      };
+      for (int pass = 0; pass < NPASS && ok; ++pass) {
+        const bool last = pass == NPASS - 1;
+        int prev_s = 0;
+        for (int t = 0; t < n_tiles && ok; ++t) {
+          const int s = kc & 1;
+          const uint32_t ph = (kc >> 1) & 1;
+          if (!(ok = mbar_wait(&bars->k_full[s], ph, abort_flag))) break;
+          if (!(ok = mbar_wait(&bars->v_full[s], ph, abort_flag))) break;
+          if (!(ok = mbar_wait(&bars->sdp_empty, (sdc & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+            mma_f16_ss(tmem_s, sw128_desc(q_base + off, 16, 1024), sw128_desc(k_base + s * TILE + off, 16, 1024),
+                       IDESC_S, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+            mma_f16_ss(tmem_dp, sw128_desc(do_base + off, 16, 1024), sw128_desc(v_base + s * TILE + off, 16, 1024),
+                       IDESC_S, kk > 0);
+          }
+          mma_commit(&bars->sdp_full);
+          mma_commit(&bars->v_empty[s]);
+          ++sdc;
+          if (!last) {
+            mma_commit(&bars->k_empty[s]);
+          } else {
+            if (t > 0) ok = issue_dq(prev_s, t - 1);
+            prev_s = s;
+          }
+          ++kc;
+        }
+        if (ok && last) {
+          ok = issue_dq(prev_s, n_tiles - 1);
+          mma_commit(&bars->dq_done);
+        }
+      }
+      if (!ok) {
+        *abort_ptr = 1;
+        if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+      }
+    }
+  } else {
+    const int row = threadIdx.x;
+    const int i = q0 + row;
+    const bool row_ok = i < g.q_len;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const int limit = i + g.k_len - g.q_len;
+    int vis_hi = row_ok ? g.k_len : 0;
+    if (p.causal) vis_hi = min(vis_hi, limit + 1);
+    int vis_lo = 0;
+    if (p.window_left > 0) vis_lo = limit - p.window_left + 1;
+    const float zs = zscale<NORM>(p.scale);
+    float st0 = 0.f, inv_l = 1.f, c = 0.f;
+    int64_t si = 0;
+    if (row_ok) {
+      si = stat_index(p, g, h, i);
+      st0 = p.stats[si];
+      inv_l = NORM == HFAN_SOFTMAX1 ? 1.f / p.stats[(int64_t)p.hq * p.rows_total + si] : 1.f;
+    }
+    if (NORM == HFAN_SOFTMAX1 && row_ok) {
+      // c = O . dO (the implicit sink carries no value)
+      const T* orow = static_cast<const T*>(p.o) + qrow_off(p, g, b, h, i, p.o_sb, p.o_sh, p.o_st);
+      const T* drow = static_cast<const T*>(p.dout) + qrow_off(p, g, b, h, i, p.do_sb, p.do_sh, p.do_st);
+      float acc = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < HD; d += 8) {
+        uint4 ov = *reinterpret_cast<const uint4*>(orow + d);
+        uint4 dv = *reinterpret_cast<const uint4*>(drow + d);
+        const T* oe = reinterpret_cast<const T*>(&ov);
+        const T* de = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(to_f32<T>(oe[e]), to_f32<T>(de[e]), acc);
+      }
+      c = acc;
+    }
+    bool ok = true;
+    uint32_t sdc = 0;
+
+    // Loads one 32-column chunk of S and dP; applies the visibility mask.
+    auto chunk = [&](int t, int cidx, float (&sv)[32], float (&dv)[32]) {
+      uint32_t rs[32], rd[32];
+      tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
+      tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
+      tmem_wait_ld();
+      const int kb = k_lo + t * kBN + cidx * 32;
+      const int lo = vis_lo - kb, hi = vis_hi - kb;
+      const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= 32);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        sv[j] = (full || (j >= lo && j < hi)) ? __uint_as_float(rs[j]) * zs : kNegInf;
+        dv[j] = __uint_as_float(rd[j]);
+      }
+    };
+
+    if (SPARSE) {
+      float num = 0.f, den = 0.f;
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int cidx = 0; cidx < 4; ++cidx) {
+          float sv[32], dv[32];
+          chunk(t, cidx, sv, dv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float w, pr;
+            weight<NORM>(sv[j], st0, inv_l, &w, &pr);
+            num = fmaf(w, dv[j], num);
+            den += w;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->sdp_empty);
+        ++sdc;
+      }
+      c = den > 0.f ? num / den : 0.f;
+    }
+    if (row_ok) p.corr[si] = c;
+
+    for (int t = 0; t < n_tiles && ok; ++t) {
+      if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
+      tc_fence_after();
+      uint32_t pk[64];
+#pragma unroll
+      for (int cidx = 0; cidx < 4; ++cidx) {
+        float sv[32], dv[32];
+        chunk(t, cidx, sv, dv);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float w0, w1, p0, p1;
+          weight<NORM>(sv[j], st0, inv_l, &w0, &p0);
+          weight<NORM>(sv[j + 1], st0, inv_l, &w1, &p1);
+          pk[cidx * 16 + j / 2] = pack2<BF16>(w0 * (dv[j] - c), w1 * (dv[j + 1] - c));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->sdp_empty);
+      ++sdc;
+      if (t > 0) {
+        if (!(ok = wait_warp(&bars->ds_empty, (t - 1) & 1, abort_flag))) break;
+      }
+      store_row_sw128(smem + L::DS, row, pk);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->ds_full);
+    }
+    if (ok && n_tiles > 0) {
+      ok = wait_warp(&bars->dq_done, 0, abort_flag);
+      tc_fence_after();
+    }
+    if (!ok) {
+      *abort_ptr = 1;
+      if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+    }
+    T* dqrow = static_cast<T*>(p.dq) + qrow_off(p, g, b, h, row_ok ? i : 0, p.dq_sb, p.dq_sh, p.dq_st);
+#pragma unroll
+    for (int cidx = 0; cidx < HD / 32; ++cidx) {
+      uint32_t r[32];
+      if (n_tiles > 0) {
+        tmem_ld32(tmem_dq + lane_addr + cidx * 32, r);
+        tmem_wait_ld();
+      }
+      if (n_tiles == 0 || !ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 v;
+          v.x = pack2<BF16>(__uint_as_float(r[j + 0]) * p.scale, __uint_as_float(r[j + 1]) * p.scale);
+          v.y = pack2<BF16>(__uint_as_float(r[j + 2]) * p.scale, __uint_as_float(r[j + 3]) * p.scale);
+          v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * p.scale, __uint_as_float(r[j + 5]) * p.scale);
+          v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * p.scale, __uint_as_float(r[j + 7]) * p.scale);
+          *reinterpret_cast<uint4*>(dqrow + cidx * 32 + j) = v;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =========================================================== dk/dv kernel
+struct KBars {
+  uint64_t kv_full;
+  uint64_t qd_full[2], qd_empty[2];
+  uint64_t sdp_full, sdp_empty, pb_full, pb_empty, done;
+};
+
+template <int HD>
+struct KLayout {
+  static constexpr int NH = HD / 64;
+  static constexpr uint32_t K = 0;
+  static constexpr uint32_t V = K + NH * kHalf;
+  static constexpr uint32_t Q = V + NH * kHalf;        // 2 stages
+  static constexpr uint32_t DO = Q + 2 * NH * kHalf;   // 2 stages
+  static constexpr uint32_t PB = DO + 2 * NH * kHalf;  // P^T, then dS^T
+  static constexpr uint32_t STATS = PB + 2 * kHalf;    // 3 x 128 floats
+  static constexpr uint32_t BARS = STATS + 3 * 128 * 4;
+  static constexpr uint32_t CTL = BARS + sizeof(KBars);
+  static constexpr uint32_t TOTAL = CTL + 16 + 1024;
+};
+
+template <int HD, bool BF16, int NORM>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                       const AttnParams p) {
+  using L = KLayout<HD>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int NH = L::NH;
+  constexpr uint32_t TILE = NH * kHalf;
+  constexpr uint32_t IDESC_S = idesc_f16(BF16, kBM, kBN, false, false);
+  constexpr uint32_t IDESC_ACC = idesc_f16(BF16, kBM, HD, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  KBars* bars = reinterpret_cast<KBars*>(smem + L::BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::CTL);
+  int* abort_ptr = reinterpret_cast<int*>(smem + L::CTL + 4);
+  volatile int* abort_flag = abort_ptr;
+  float* st0s = reinterpret_cast<float*>(smem + L::STATS);
+  float* st1s = st0s + 128;
+  float* crs = st1s + 128;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, kvh = blockIdx.y;
+  const Geometry g = geometry(p, b);
+  const int k0 = blockIdx.x * kBN;
+  if (k0 >= g.k_len) return;
+  const int groups = p.hq / p.hkv;
+  const bool varlen = p.cu_q != nullptr;
+  const int qtok0 = varlen ? g.q_start : 0;
+  const int ktok = varlen ? g.k_start + k0 : k0;
+  const int bcoord = varlen ? 0 : b;
+
+  // query rows that see any key of this tile
+  const int off = g.k_len - g.q_len;
+  int i_lo = 0;
+  if (p.causal) i_lo = max(0, k0 - off);
+  int i_hi = g.q_len;
+  if (p.window_left > 0) i_hi = min(i_hi, min(k0 + kBN, g.k_len) - 1 - off + p.window_left);
+  const int m_lo = i_lo / kBM;
+  const int m_hi = i_hi > i_lo ? (i_hi + kBM - 1) / kBM : m_lo;
+  const int n_m = m_hi - m_lo;
+  const int n_units = groups * n_m;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->qd_full[s], 1);
+      mbar_init(&bars->qd_empty[s], 1);
+    }
+    mbar_init(&bars->sdp_full, 1);
+    mbar_init(&bars->sdp_empty, 128);
+    mbar_init(&bars->pb_full, 128);
+    mbar_init(&bars->pb_empty, 1);
+    mbar_init(&bars->done, 1);
+    *abort_ptr = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dv = tmem + 256, tmem_dk = tmem + 256 + HD;
+
+  if (warp == 4) {
+    if (lane == 0 && n_units > 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_do);
+      prefetch_tmap(&tm_k);
+      prefetch_tmap(&tm_v);
+      mbar_arrive_expect_tx(&bars->kv_full, 2 * TILE);
+      for (int hh = 0; hh < NH; ++hh) {
+        tma_load_4d(smem + L::K + hh * kHalf, &tm_k, &bars->kv_full, 64 * hh, ktok, kvh, bcoord);
+        tma_load_4d(smem + L::V + hh * kHalf, &tm_v, &bars->kv_full, 64 * hh, ktok, kvh, bcoord);
+      }
+      bool ok = true;
+      for (int u = 0; u < n_units && ok; ++u) {
+        const int hq = kvh * groups + u / n_m;
+        const int m = m_lo + u % n_m;
+        const int s = u & 1;
+        if (!(ok = mbar_wait(&bars->qd_empty[s], ((u >> 1) & 1) ^ 1, abort_flag))) break;
+        mbar_arrive_expect_tx(&bars->qd_full[s], 2 * TILE);
+        for (int hh = 0; hh < NH; ++hh) {
+          tma_load_4d(smem + L::Q + s * TILE + hh * kHalf, &tm_q, &bars->qd_full[s], 64 * hh, qtok0 + m * kBM, hq, bcoord);
+          tma_load_4d(smem + L::DO + s * TILE + hh * kHalf, &tm_do, &bars->qd_full[s], 64 * hh, qtok0 + m * kBM, hq, bcoord);
+        }
+      }
+      if (!ok) {
+        *abort_ptr = 1;
+        if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && n_units > 0) {
+      const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
+      const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
+      const uint32_t pb_base = smem_u32(smem + L::PB);
+      bool ok = mbar_wait(&bars->kv_full, 0, abort_flag);
+      uint32_t pbc = 0;
+      // dV += P^T dO and dK += dS^T Q for unit u (stage s)
+      auto issue_acc = [&](int u, int s) -> bool {
+        for (int which = 0; which < 2; ++which) {
+          if (!mbar_wait(&bars->pb_full, pbc & 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t bsrc = (which == 0 ? do_base : q_base) + s * TILE;
+          const uint32_t dst = which == 0 ? tmem_dv : tmem_dk;
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk) {
+            const uint64_t a = sw128_desc(pb_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(bsrc + kk * 16 * 128, kHalf, 1024);
+            mma_f16_ss(dst, a, bd, IDESC_ACC, u > 0 || kk > 0);
+          }
+          mma_commit(&bars->pb_empty);
+          ++pbc;
+        }
+        mma_commit(&bars->qd_empty[s]);
+        return true;
+      };
+      for (int u = 0; u < n_units && ok; ++u) {
+        const int s = u & 1;
+        if (!(ok = mbar_wait(&bars->qd_full[s], (u >> 1) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(&bars->sdp_empty, (u & 1) ^ 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * kHalf + (kk & 3) * 32;
+          mma_f16_ss(tmem_s, sw128_desc(k_base + o, 16, 1024), sw128_desc(q_base + s * TILE + o, 16, 1024),
+                     IDESC_S, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * kHalf + (kk & 3) * 32;
+          mma_f16_ss(tmem_dp, sw128_desc(v_base + o, 16, 1024), sw128_desc(do_base + s * TILE + o, 16, 1024),
+                     IDESC_S, kk > 0);
+        }
+        mma_commit(&bars->sdp_full);
+        if (u > 0) ok = issue_acc(u - 1, (u - 1) & 1);
+      }
+      if (ok) {
+        ok = issue_acc(n_units - 1, (n_units - 1) & 1);
+        mma_commit(&bars->done);
+      }
+      if (!ok) {
+        *abort_ptr = 1;
+        if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+      }
+    }
+  } else {
+    const int row = threadIdx.x;  // key within the tile
+    const int j = k0 + row;
+    const bool key_ok = j < g.k_len;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const float zs = zscale<NORM>(p.scale);
+    bool ok = true;
+    uint32_t pbc = 0;
+    // The named barriers run on every iteration, even after a timeout, so that
+    // no warp waits for one that has left the loop.
+    for (int u = 0; u < n_units; ++u) {
+      const int hq = kvh * groups + u / n_m;
+      const int m = m_lo + u % n_m;
+      const int qbase = m * kBM;
+      // stage the statistics of this tile's 128 query rows
+      named_bar_sync(1, 128);
+      {
+        const int iq = qbase + row;
+        float a = kPosInf, bb = 1.f, cc = 0.f;
+        if (iq < g.q_len) {
+          const int64_t si = stat_index(p, g, hq, iq);
+          a = p.stats[si];
+          bb = p.stats[(int64_t)p.hq * p.rows_total + si];
+          cc = p.corr[si];
+        }
+        if (NORM == HFAN_SOFTMAX1 && !(iq < g.q_len)) a = kPosInf;
+        st0s[row] = a;
+        st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / bb : 1.f;
+        crs[row] = cc;
+      }
+      named_bar_sync(1, 128);
+      if (!ok) continue;
+      if (!(ok = wait_warp(&bars->sdp_full, u & 1, abort_flag))) continue;
+      tc_fence_after();
+      // visible queries of this key: [c_lo, c_hi) relative to qbase
+      const int jl = j - off;  // causal: query i sees key j iff i >= j - off
+      int c_lo = p.causal ? jl - qbase : -1 << 30;
+      int c_hi = key_ok ? g.q_len - qbase : -(1 << 30);
+      if (p.window_left > 0) c_hi = min(c_hi, jl + p.window_left - qbase);
+      uint32_t ppk[64], dpk[64];
+#pragma unroll
+      for (int cidx = 0; cidx < 4; ++cidx) {
+        uint32_t rs[32], rd[32];
+        tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
+        tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
+        tmem_wait_ld();
+        const int lo = c_lo - cidx * 32, hi = c_hi - cidx * 32;
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int col = cidx * 32 + e + x;
+            const bool vis = (e + x) >= lo && (e + x) < hi;
+            float w = 0.f, pr = 0.f;
+            if (vis) weight<NORM>(__uint_as_float(rs[e + x]) * zs, st0s[col], st1s[col], &w, &pr);
+            pv[x] = pr;
+            dsv[x] = w * (__uint_as_float(rd[e + x]) - crs[col]);
+          }
+          ppk[cidx * 16 + e / 2] = pack2<BF16>(pv[0], pv[1]);
+          dpk[cidx * 16 + e / 2] = pack2<BF16>(dsv[0], dsv[1]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->sdp_empty);
+      // P^T, then dS^T, through the shared buffer
+      for (int which = 0; which < 2 && ok; ++which) {
+        if (pbc > 0) {
+          if (!(ok = wait_warp(&bars->pb_empty, (pbc - 1) & 1, abort_flag))) break;
+        }
+        store_row_sw128(smem + L::PB, row, which == 0 ? ppk : dpk);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars->pb_full);
+        ++pbc;
+      }
+    }
+    if (ok && n_units > 0) {
+      ok = wait_warp(&bars->done, 0, abort_flag);
+      tc_fence_after();
+    }
+    if (!ok) {
+      *abort_ptr = 1;
+      if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+    }
+    const int64_t kt = varlen ? (int64_t)g.k_start + (key_ok ? j : 0) : (key_ok ? j : 0);
+    const int64_t boff = varlen ? 0 : (int64_t)b;
+    T* dkrow = static_cast<T*>(p.dk) + boff * p.dk_sb + (int64_t)kvh * p.dk_sh + kt * p.dk_st;
+    T* dvrow = static_cast<T*>(p.dv) + boff * p.dv_sb + (int64_t)kvh * p.dv_sh + kt * p.dv_st;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const uint32_t src = which == 0 ? tmem_dv : tmem_dk;
+      const float f = which == 0 ? 1.f : p.scale;
+      T* dst = which == 0 ? dvrow : dkrow;
+#pragma unroll
+      for (int cidx = 0; cidx < HD / 32; ++cidx) {
+        uint32_t r[32];
+        if (n_units > 0) {
+          tmem_ld32(src + lane_addr + cidx * 32, r);
+          tmem_wait_ld();
+        }
+        if (n_units == 0 || !ok) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) r[x] = 0u;
+        }
+        if (key_ok) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 8) {
+            uint4 v;
+            v.x = pack2<BF16>(__uint_as_float(r[x + 0]) * f, __uint_as_float(r[x + 1]) * f);
+            v.y = pack2<BF16>(__uint_as_float(r[x + 2]) * f, __uint_as_float(r[x + 3]) * f);
+            v.z = pack2<BF16>(__uint_as_float(r[x + 4]) * f, __uint_as_float(r[x + 5]) * f);
+            v.w = pack2<BF16>(__uint_as_float(r[x + 6]) * f, __uint_as_float(r[x + 7]) * f);
+            *reinterpret_cast<uint4*>(dst + cidx * 32 + x) = v;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =========================================================== host
+template <typename K>
+cudaError_t launch_k(K kernel, dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap& a,
+                     const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d, const AttnParams& p) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kernel<<<grid, kThreads, smem, s>>>(a, b, c, d, p);
+  return cudaGetLastError();
+}
+
+template <int HD, bool BF16, int NORM>
+cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t s) {
+  const bool varlen = p.cu_q != nullptr;
+  const int64_t tq = varlen ? p.rows_total : p.len_q;
+  const int64_t tk = varlen ? p.rows_k : p.len_k;
+  const int batch = varlen ? 1 : p.batch;
+  CUtensorMap mq, mdo, mk, mv;
+  if (!make_map(&mq, p.q, BF16, HD, tq, p.hq, batch, p.q_st, p.q_sh, varlen ? tq * p.q_st : p.q_sb) ||
+      !make_map(&mdo, p.dout, BF16, HD, tq, p.hq, batch, p.do_st, p.do_sh, varlen ? tq * p.do_st : p.do_sb) ||
+      !make_map(&mk, p.k, BF16, HD, tk, p.hkv, batch, p.k_st, p.k_sh, varlen ? tk * p.k_st : p.k_sb) ||
+      !make_map(&mv, p.v, BF16, HD, tk, p.hkv, batch, p.v_st, p.v_sh, varlen ? tk * p.v_st : p.v_sb))
+    return cudaErrorInvalidValue;
+  cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
+                           QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+  if (e != cudaSuccess) return e;
+  return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
+                  KLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+}
+
+template <int HD, bool BF16>
+cudaError_t launch_bwd(const AttnParams& p, int max_q, int max_k, cudaStream_t s) {
+  switch (p.norm) {
+    case HFAN_SOFTMAX1: return launch_bwd_t<HD, BF16, HFAN_SOFTMAX1>(p, max_q, max_k, s);
+    case HFAN_SPARSEMAX: return launch_bwd_t<HD, BF16, HFAN_SPARSEMAX>(p, max_q, max_k, s);
+    default: return launch_bwd_t<HD, BF16, HFAN_ENTMAX15>(p, max_q, max_k, s);
+  }
+}
+
+}  // namespace
+
+cudaError_t tc_attention_bwd(int dtype, const AttnParams& p, int max_q, int max_k, cudaStream_t s) {
+  // Gradients in the input dtype only; float32 gradient requests use the
+  // general kernels.
+  if (p.grad_f32) return cudaErrorNotSupported;
+  if (!tc::aligned16(p.dout) || !tc::aligned16(p.dq) || !tc::aligned16(p.dk) || !tc::aligned16(p.dv) ||
+      !tc::stride_ok(p.do_st) || !tc::stride_ok(p.do_sh) || (p.dq_st % 8) || (p.dq_sh % 8) ||
+      (p.dk_st % 8) || (p.dk_sh % 8) || (p.dv_st % 8) || (p.dv_sh % 8))
+    return cudaErrorNotSupported;
+  if (p.cu_q == nullptr && p.batch > 1 &&
+      (!tc::stride_ok(p.do_sb) || (p.dq_sb % 8) || (p.dk_sb % 8) || (p.dv_sb % 8)))
+    return cudaErrorNotSupported;
+  const bool bf16 = dtype == HFAN_BFLOAT16;
+  if (p.d == 128) return bf16 ? launch_bwd<128, true>(p, max_q, max_k, s) : launch_bwd<128, false>(p, max_q, max_k, s);
+  return bf16 ? launch_bwd<64, true>(p, max_q, max_k, s) : launch_bwd<64, false>(p, max_q, max_k, s);
+}
+
+}  // namespace hfan

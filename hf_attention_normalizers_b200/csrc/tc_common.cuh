@@ -1,0 +1,80 @@
+// Helpers shared by the tensor-core forward and backward kernels: warp-uniform
+// bounded waits, 16-bit packing, and host-side TMA tensor-map construction.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "params.cuh"
+#include "tc_ptx.cuh"
+
+namespace hfan {
+namespace tc {
+
+constexpr uint32_t kHalf = 128u * 128u;  // one 128-row x 128-byte swizzled half tile
+
+// Wait whose outcome is uniform across the warp, so that the warp-collective
+// tcgen05.ld / tcgen05.st that follow are executed by all 32 lanes or none.
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// P (or dS) row r of a 128 x 128 16-bit tile -> shared memory, K-major with
+// 128-byte swizzle: two 64-column halves kHalf apart; 16-byte chunk c of row
+// r sits at chunk position c ^ (r & 7).  `pk` holds the row as 64 packed pairs.
+__device__ __forceinline__ void store_row_sw128(uint8_t* base, int row, const uint32_t (&pk)[64]) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const int hh = c >> 3, cc = c & 7;
+    uint4 v = make_uint4(pk[c * 4 + 0], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+    *reinterpret_cast<uint4*>(base + hh * kHalf + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+  }
+}
+
+// ------------------------------------------------------------------ host
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 4-D map (dim, token, head, batch) with a 64 x 128 x 1 x 1 box, 128-byte swizzle.
+inline bool make_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t tokens, int heads, int batch,
+              int64_t st, int64_t sh, int64_t sb) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+inline bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+inline bool stride_ok(int64_t s) { return s > 0 && (s % 8) == 0 && s < ((int64_t)1 << 38); }
+
+
+}  // namespace tc
+}  // namespace hfan
