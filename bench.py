@@ -165,6 +165,8 @@ def run_ours(args, rank, world, local_rank):
             step()
         e1.record()
         barrier()
+    if args.profile_case:
+        return None
     ms = e0.elapsed_time(e1) / args.steps
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -260,9 +262,63 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": args.steps * len(NORMS) * 3,
         "clocks": sampler.summary(),
     }
+    if args.decode:
+        line["paged_decode"] = bench_decode(dev, hbm)
     if args.cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
     return line
+
+
+def bench_decode(dev, hbm_peak, bsz=256, norms=("softmax1", "sparsemax", "entmax15")):
+    """paged decode, batch 256, contexts U[1024, 32768]
+    (seed 0), 32-token pages in a randomly permuted pool (seed 1), 32 query /
+    8 KV heads, D=128, bf16, one query token per sequence.  Reported as
+    algorithmic GB/s: every valid page's K and V bytes plus q, o and the block
+    table, divided by the device time of one call."""
+    import torch
+
+    from hf_attention_normalizers_b200 import _native as N
+    from hf_attention_normalizers_b200 import ops
+
+    page, hq, hkv, d = 32, 32, 8, 128
+    lens = torch.randint(1024, 32769, (bsz,), generator=torch.Generator().manual_seed(0))
+    npages = [(int(x) + page - 1) // page for x in lens]
+    pool = sum(npages)
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(1)).int()
+    table = torch.zeros(bsz, 1024, dtype=torch.int32)
+    off = 0
+    for i, n in enumerate(npages):
+        table[i, :n] = perm[off:off + n]
+        off += n
+    gen = torch.Generator(device=dev).manual_seed(2)
+    kc = torch.randn(pool * page, hkv, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    vc = torch.randn(pool * page, hkv, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    q = torch.randn(bsz, hq, 1, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    table_d, lens_d = table.to(dev), lens.int().to(dev)
+    max_len = int(lens.max())
+    kv_bytes = pool * page * hkv * d * 2 * 2
+    alg = kv_bytes + 2 * q.numel() * 2 + table.numel() * 4 + bsz * 4
+    out = {"config": "BASELINE configs[3]" if bsz == 256 else f"configs[3] shape, batch {bsz}",
+           "kv_gb": round(kv_bytes / 1e9, 3)}
+    for name in norms:
+        nid = N.NORMALIZER_IDS[name]
+        f = lambda: ops.paged_fwd(q, kc, vc, table_d, lens_d, page, max_len, nid, d ** -0.5, True)
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            f()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        gbs = alg / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 3), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 3)}
+    out["note"] = ("sparsemax/entmax15 read V only for keys in the support, so their algorithmic GB/s "
+                   "can exceed the DRAM bandwidth")
+    return out
 
 
 # --------------------------------------------------------------------------- CPU
@@ -341,8 +397,26 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--no-decode", dest="decode", action="store_false",
+                    help="skip the paged-decode measurement (BASELINE configs[3])")
+    ap.add_argument("--decode-only", type=int, default=0, metavar="BATCH",
+                    help="only run the paged-decode measurement with this many sequences (profiling)")
+    ap.add_argument("--decode-norms", default="softmax1,sparsemax,entmax15")
+    ap.add_argument("--shape", default=None,
+                    help="B,S,HQ,HKV override for small profiling cases (default: the BASELINE config)")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="run warmup+steps of the step only (no e2e, no phases): for ncu captures")
     args = ap.parse_args()
+    if args.shape:
+        global B, S, HQ, HKV
+        B, S, HQ, HKV = (int(x) for x in args.shape.split(","))
 
+    if args.decode_only:
+        import torch
+
+        print(json.dumps(bench_decode(torch.device("cuda", 0), peaks()[2], args.decode_only,
+                                      tuple(args.decode_norms.split(",")))), flush=True)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -355,7 +429,8 @@ def main():
 
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-        args.cpu_baseline = args.cpu_baseline and rank == 0 and world == 1
+        args.cpu_baseline = args.cpu_baseline and rank == 0 and world == 1 and not args.shape
+        args.decode = args.decode and world == 1 and not args.shape
         line = run_ours(args, rank, world, local_rank)
         if world > 1:
             import torch.distributed as dist

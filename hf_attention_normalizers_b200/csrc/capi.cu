@@ -18,6 +18,10 @@ cudaError_t rownorm_bwd(int norm, int dtype, int64_t rows, int64_t n, const void
                         const void* dy, int64_t lddy, void* dx, int64_t lddx, cudaStream_t s);
 // Tensor-core (tcgen05 / TMA) kernels for 16-bit dense and varlen requests.
 bool tc_supported(int dtype, const AttnParams& p);
+// Split-KV paged decode (paged_decode.cu).
+bool decode_supported(int dtype, const AttnParams& p, int max_len);
+size_t decode_workspace_bytes(const AttnParams& p, int max_len);
+cudaError_t decode_run(int dtype, const AttnParams& p, int max_len, void* ws, cudaStream_t s);
 cudaError_t tc_attention_fwd(int dtype, const AttnParams& p, int max_q, cudaStream_t s);
 cudaError_t tc_attention_bwd(int dtype, const AttnParams& p, int max_q, int max_k, cudaStream_t s);
 }  // namespace hfan
@@ -252,6 +256,32 @@ int hfan_paged_bwd(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = simt_attention_bwd(desc->dtype, p, desc->len_q, desc->max_len_k, s);
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_paged_bwd");
+}
+
+int64_t hfan_paged_decode_workspace_bytes(const hfan_paged_desc* desc) {
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (fill_paged(desc, p) != HFAN_OK) return -1;
+  return (int64_t)decode_workspace_bytes(p, desc->max_len_k);
+}
+
+int hfan_paged_decode(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_cache, hfan_tensor value_cache,
+                      hfan_tensor o, float* stats, void* workspace, int64_t workspace_bytes, void* stream) {
+  AttnParams p = base_params(q, key_cache, value_cache, o);
+  int rc = fill_paged(desc, p);
+  if (rc != HFAN_OK) return rc;
+  if (stats == nullptr) return fail(HFAN_ERR_INVALID, "stats buffer is required");
+  p.stats = stats;
+  if (!decode_supported(desc->dtype, p, desc->max_len_k))
+    return fail(HFAN_ERR_UNSUPPORTED, "paged decode: shape outside the split-KV kernel's envelope");
+  const size_t need = decode_workspace_bytes(p, desc->max_len_k);
+  if (workspace == nullptr || workspace_bytes < (int64_t)need)
+    return fail(HFAN_ERR_INVALID, "paged decode: workspace of %zu bytes required", need);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(HFAN_ERR_INVALID, "paged decode: workspace must be 256-byte aligned");
+  if (desc->max_len_k == 0) return HFAN_OK;
+  cudaError_t e = decode_run(desc->dtype, p, desc->max_len_k, workspace, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_paged_decode");
 }
 
 int hfan_rownorm_fwd(int32_t normalizer, int32_t dtype, int64_t rows, int64_t n, const void* x,

@@ -255,6 +255,16 @@ def paged_fwd(q: Tensor, key_cache: Tensor, value_cache: Tensor, block_table: Te
     stats = torch.empty((2, hq, b * lq), dtype=torch.float32, device=q.device)
     desc = _paged_desc(q, kc, bt, sl, page_size, max_len_k, normalizer, scale, causal)
     with torch.cuda.device(q.device):
+        if lq == 1:
+            # serving fast path: split-KV decode with a workspace from the caching allocator
+            nbytes = N.lib().hfan_paged_decode_workspace_bytes(ctypes.byref(desc))
+            if nbytes > 0:
+                ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+                rc = N.lib().hfan_paged_decode(ctypes.byref(desc), _t4(q), _t3(kc), _t3(vc), _t4(o), _ptr(stats),
+                                               _ptr(ws), nbytes, _stream(q))
+                if rc != 2:  # 2 = shape outside the decode kernel's envelope
+                    N.check(rc, "hfan_paged_decode")
+                    return o, stats
         N.check(N.lib().hfan_paged_fwd(ctypes.byref(desc), _t4(q), _t3(kc), _t3(vc), _t4(o), _ptr(stats),
                                        _stream(q)), "hfan_paged_fwd")
     return o, stats

@@ -140,6 +140,20 @@ int hfan_paged_bwd(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_c
                    hfan_tensor value_cache, hfan_tensor o, hfan_tensor d_o, const float* stats,
                    float* corr, hfan_tensor dq, hfan_tensor dk, hfan_tensor dv, void* stream);
 
+/* Split-KV paged decode (len_q == 1), the serving fast path of hfan_paged_fwd.
+ * Same semantics, inputs, outputs and statistics as hfan_paged_fwd; scratch
+ * (per-split partial outputs and, for sparsemax/entmax15, the score rows) lives
+ * in a caller-provided device workspace, 256-byte aligned, of at least
+ * hfan_paged_decode_workspace_bytes(desc) bytes.  Returns HFAN_ERR_UNSUPPORTED
+ * (nothing launched) for shapes outside the kernel's envelope: 16-bit cache,
+ * head_dim 64/128, heads_q/heads_kv in {1,2,4,8}, max_len_k <= 32768.
+ * Replaces _paged_softmax1_forward (kernels/paged_softmax1_hopper.py:17-83) and
+ * _paged_sparse_forward (kernels/paged_sparse_entmax_hopper.py:52-185) for decode. */
+int64_t hfan_paged_decode_workspace_bytes(const hfan_paged_desc* desc);
+int hfan_paged_decode(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_cache,
+                      hfan_tensor value_cache, hfan_tensor o, float* stats, void* workspace,
+                      int64_t workspace_bytes, void* stream);
+
 /* Row normalizers over the last axis of a [rows, n] matrix with row stride
  * ld (elements, unit column stride).  y/dx have the dtype of x. */
 int hfan_rownorm_fwd(int32_t normalizer, int32_t dtype, int64_t rows, int64_t n,

@@ -275,3 +275,25 @@ def test_hf_qwen3_backend_matches_materialised_path(norm):
     assert model.config._attn_implementation == f"{norm}_eager"
     eager = model(ids).logits
     assert_close(fused, _np(eager), torch.float32, f"qwen3/{norm}")
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_paged_decode_serving_shape_matches_oracle(norm):
+    """Split-KV decode path: bf16, D=128, GQA 4:1, 32-token pages, permuted pages, long rows."""
+    gen = torch.Generator().manual_seed(21)
+    lens = torch.tensor([1, 31, 33, 1024, 1025, 3000, 5000], dtype=torch.long)
+    bs, hkv, g, d = 32, 2, 4, 128
+    pages = [(int(x) + bs - 1) // bs for x in lens]
+    perm = torch.randperm(sum(pages), generator=gen)
+    table = torch.zeros(len(lens), max(pages), dtype=torch.int32)
+    off = 0
+    for i, n in enumerate(pages):
+        table[i, :n] = perm[off:off + n].int()
+        off += n
+    kc = torch.randn(sum(pages) * bs, hkv, d, generator=gen).to(torch.bfloat16).cuda()
+    vc = torch.randn(sum(pages) * bs, hkv, d, generator=gen).to(torch.bfloat16).cuda()
+    q = torch.randn(len(lens), hkv * g, 1, d, generator=gen).to(torch.bfloat16).cuda()
+    o = H.paged_attention(q, kc, vc, table.cuda(), lens.cuda(), block_size=bs, normalizer=norm)
+    ref = oracle.paged_forward(_np(q), _np(kc), _np(vc), table.numpy(), lens.numpy(), bs, norm)
+    assert_close(o, ref, torch.bfloat16, f"decode/{norm}")
+    assert N.device_status(torch.cuda.current_stream().cuda_stream) == 0
