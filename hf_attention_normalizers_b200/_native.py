@@ -82,6 +82,7 @@ SIGNATURES = {
     "hfan_paged_bwd": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _T, _P, _P, _T, _T, _T, _P]),
     "hfan_paged_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(PagedDesc)]),
     "hfan_paged_decode": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _P, _P, ctypes.c_int64, _P]),
+    "hfan_paged_decode_static": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _P, _P]),
     "hfan_rownorm_fwd": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                                         _P, ctypes.c_int64, _P, ctypes.c_int64, _P]),
     "hfan_rownorm_bwd": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,

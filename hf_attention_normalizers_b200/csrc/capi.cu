@@ -22,6 +22,8 @@ bool tc_supported(int dtype, const AttnParams& p);
 bool decode_supported(int dtype, const AttnParams& p, int max_len);
 size_t decode_workspace_bytes(const AttnParams& p, int max_len);
 cudaError_t decode_run(int dtype, const AttnParams& p, int max_len, void* ws, cudaStream_t s);
+size_t decode_static_scratch_bytes();
+cudaError_t decode_static_scratch(void** out);
 cudaError_t tc_attention_fwd(int dtype, const AttnParams& p, int max_q, cudaStream_t s);
 cudaError_t tc_attention_bwd(int dtype, const AttnParams& p, int max_q, int max_k, cudaStream_t s);
 }  // namespace hfan
@@ -282,6 +284,30 @@ int hfan_paged_decode(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor ke
   if (desc->max_len_k == 0) return HFAN_OK;
   cudaError_t e = decode_run(desc->dtype, p, desc->max_len_k, workspace, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_paged_decode");
+}
+
+int hfan_paged_decode_static(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_cache,
+                             hfan_tensor value_cache, hfan_tensor o, float* stats, void* stream) {
+  AttnParams p = base_params(q, key_cache, value_cache, o);
+  int rc = fill_paged(desc, p);
+  if (rc != HFAN_OK) return rc;
+  if (stats == nullptr) return fail(HFAN_ERR_INVALID, "stats buffer is required");
+  p.stats = stats;
+  if (!decode_supported(desc->dtype, p, desc->max_len_k))
+    return fail(HFAN_ERR_UNSUPPORTED, "paged decode: shape outside the split-KV kernel's envelope");
+  const size_t need = decode_workspace_bytes(p, desc->max_len_k);
+  const size_t have = decode_static_scratch_bytes();
+  if (need > have)
+    return fail(HFAN_ERR_INVALID,
+                "hfan_paged_decode_static: this request needs %zu bytes of scratch but the built-in "
+                "scratch holds %zu bytes; use hfan_paged_decode with a caller workspace",
+                need, have);
+  void* ws = nullptr;
+  cudaError_t e = decode_static_scratch(&ws);
+  if (e != cudaSuccess) return cuda_fail(e, "hfan_paged_decode_static (scratch address)");
+  if (desc->max_len_k == 0) return HFAN_OK;
+  e = decode_run(desc->dtype, p, desc->max_len_k, ws, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_paged_decode_static");
 }
 
 int hfan_rownorm_fwd(int32_t normalizer, int32_t dtype, int64_t rows, int64_t n, const void* x,

@@ -26,6 +26,8 @@
 //
 // Row statistics use the same layout as the other attention kernels, so the
 // general paged backward can consume them.
+#include <mutex>
+
 #include "common.cuh"
 #include "params.cuh"
 
@@ -508,6 +510,40 @@ bool decode_supported(int dtype, const AttnParams& p, int max_len) {
 }
 
 size_t decode_workspace_bytes(const AttnParams& p, int max_len) { return ws_layout(p, max_len).total; }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory at the
+// point where they decode: code running inside a CUDA graph capture or on an
+// inference server's hot path, and embedders that own the GPU allocator and
+// forbid allocations behind their back.  For them the scratch lives in this
+// fixed device array instead of a caller workspace.  It is loaded with the
+// library and held by every GPU that loads it until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kStaticDecodeScratchBytes = (size_t)64 << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticDecodeScratchBytes];
+
+size_t decode_static_scratch_bytes() { return kStaticDecodeScratchBytes; }
+
+// Device address of g_decode_scratch for the current device.  In host code the
+// array name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+cudaError_t decode_static_scratch(void** out) {
+  static std::mutex mu;
+  static void* cache[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    if (e != cudaSuccess) return e;
+    cache[dev] = ptr;
+  }
+  *out = cache[dev];
+  return cudaSuccess;
+}
 
 cudaError_t decode_run(int dtype, const AttnParams& p, int max_len, void* ws, cudaStream_t s) {
   if (dtype == HFAN_BFLOAT16)

@@ -154,6 +154,26 @@ int hfan_paged_decode(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor ke
                       hfan_tensor value_cache, hfan_tensor o, float* stats, void* workspace,
                       int64_t workspace_bytes, void* stream);
 
+/* Allocation-free paged decode.  This entry point has no counterpart in the
+ * reference.  It is for callers that cannot allocate device memory when they
+ * decode: code being captured into a CUDA graph or running on a serving hot
+ * path, and embedders that own the GPU allocator.  It does exactly what
+ * hfan_paged_decode does, but its scratch is a fixed 64 MiB device array
+ * inside the library (every GPU that loads the library holds it until the
+ * process exits), so the caller passes only inputs and outputs.
+ *   - Requests needing more than 64 MiB of scratch (see
+ *     hfan_paged_decode_workspace_bytes) fail with HFAN_ERR_INVALID and a
+ *     message; nothing is launched.
+ *   - The first call on a device looks up the array's device address with
+ *     that device current; make that first call before any stream capture.
+ *   - All calls share the one array, and it keeps the previous call's
+ *     contents (every kernel overwrites the scratch it later reads, so nothing
+ *     needs clearing).  Calls that overlap on the GPU (different streams, or
+ *     different threads) race on it: serialise them.
+ *   - Nothing here calls cudaMalloc, cudaFree or an allocating library. */
+int hfan_paged_decode_static(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_cache,
+                             hfan_tensor value_cache, hfan_tensor o, float* stats, void* stream);
+
 /* Row normalizers over the last axis of a [rows, n] matrix with row stride
  * ld (elements, unit column stride).  y/dx have the dtype of x. */
 int hfan_rownorm_fwd(int32_t normalizer, int32_t dtype, int64_t rows, int64_t n,
