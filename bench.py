@@ -116,13 +116,13 @@ def run_ours(args, rank, world, local_rank):
 
     from hf_attention_normalizers_b200 import _native as N
     from hf_attention_normalizers_b200 import kernels, ops
+    from hf_attention_normalizers_b200.sharding import gather_heads, kv_group_shard
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if HKV % world:
-        raise SystemExit(f"--gpus must divide {HKV} KV heads")
-    hkv = HKV // world
-    hq = HQ // world
+    shard = kv_group_shard(HQ, HKV, world, rank)
+    hkv = shard.kv_hi - shard.kv_lo
+    hq = shard.q_hi - shard.q_lo
     scale = D ** -0.5
     gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
     host = {
@@ -138,8 +138,7 @@ def run_ours(args, rank, world, local_rank):
         if world == 1:
             return
         for x in tensors:
-            out = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
-            dist.all_gather_into_tensor(out, x.contiguous())
+            gather_heads(x, 1)
 
     def step():
         for name in NORMS:
