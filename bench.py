@@ -426,6 +426,7 @@ def main():
             import torch
             import torch.distributed as dist
 
+            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
         args.cpu_baseline = args.cpu_baseline and rank == 0 and world == 1 and not args.shape

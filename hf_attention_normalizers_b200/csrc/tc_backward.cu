@@ -34,7 +34,7 @@ using namespace tc;
 
 constexpr int kBM = 128;
 constexpr int kBN = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 2 row warpgroups (warps 0-7), TMA warp 8, MMA warp 9
 
 template <int NORM> __device__ __forceinline__ float zscale(float scale) {
   return NORM == HFAN_SOFTMAX1 ? scale * kLog2e : (NORM == HFAN_SPARSEMAX ? scale : 0.5f * scale);
@@ -129,21 +129,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, 128);
-    mbar_init(&bars->ds_full, 128);
+    mbar_init(&bars->sdp_empty, 256);
+    mbar_init(&bars->ds_full, 256);
     mbar_init(&bars->ds_empty, 1);
     mbar_init(&bars->dq_done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dq = tmem + 256;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0 && n_tiles > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
@@ -242,10 +242,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int row = threadIdx.x;
+    // Two warpgroups share each 128 x 128 tile: warpgroup wg owns key columns
+    // [64 wg, 64 wg + 64) of every row (TMEM lanes are reached through warp % 4).
+    const int wg = warp >> 2;
+    const int row = threadIdx.x & 127;
     const int i = q0 + row;
     const bool row_ok = i < g.q_len;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const int limit = i + g.k_len - g.q_len;
     int vis_hi = row_ok ? g.k_len : 0;
     if (p.causal) vis_hi = min(vis_hi, limit + 1);
@@ -300,9 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
-        for (int cidx = 0; cidx < 4; ++cidx) {
+        for (int cc = 0; cc < 2; ++cc) {
           float sv[32], dv[32];
-          chunk(t, cidx, sv, dv);
+          chunk(t, wg * 2 + cc, sv, dv);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float w, pr;
@@ -315,24 +318,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&bars->sdp_empty);
         ++sdc;
       }
+      // combine the two column halves (the dS buffer is idle until pass B)
+      float* xch = reinterpret_cast<float*>(smem + L::DS);
+      xch[(wg * 128 + row) * 2 + 0] = num;
+      xch[(wg * 128 + row) * 2 + 1] = den;
+      named_bar_sync(1, 256);
+      num = xch[row * 2] + xch[(128 + row) * 2];
+      den = xch[row * 2 + 1] + xch[(128 + row) * 2 + 1];
+      named_bar_sync(1, 256);
       c = den > 0.f ? num / den : 0.f;
     }
-    if (row_ok) p.corr[si] = c;
+    if (row_ok && wg == 0) p.corr[si] = c;
 
     for (int t = 0; t < n_tiles && ok; ++t) {
       if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
       tc_fence_after();
-      uint32_t pk[64];
+      uint32_t pk[32];
 #pragma unroll
-      for (int cidx = 0; cidx < 4; ++cidx) {
+      for (int cc = 0; cc < 2; ++cc) {
         float sv[32], dv[32];
-        chunk(t, cidx, sv, dv);
+        chunk(t, wg * 2 + cc, sv, dv);
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           float w0, w1, p0, p1;
           weight<NORM>(sv[j], st0, inv_l, &w0, &p0);
           weight<NORM>(sv[j + 1], st0, inv_l, &w1, &p1);
-          pk[cidx * 16 + j / 2] = pack2<BF16>(w0 * (dv[j] - c), w1 * (dv[j + 1] - c));
+          pk[cc * 16 + j / 2] = pack2<BF16>(w0 * (dv[j] - c), w1 * (dv[j + 1] - c));
         }
       }
       tc_fence_before();
@@ -341,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t > 0) {
         if (!(ok = wait_warp(&bars->ds_empty, (t - 1) & 1, abort_flag))) break;
       }
-      store_row_sw128(smem + L::DS, row, pk);
+      store_half_sw128(smem + L::DS, wg, row, pk);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ds_full);
@@ -356,7 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     T* dqrow = static_cast<T*>(p.dq) + qrow_off(p, g, b, h, row_ok ? i : 0, p.dq_sb, p.dq_sh, p.dq_st);
 #pragma unroll
-    for (int cidx = 0; cidx < HD / 32; ++cidx) {
+    for (int cc = 0; cc < HD / 64; ++cc) {
+      const int cidx = wg * (HD / 64) + cc;  // warpgroup wg stores half of the head dim
       uint32_t r[32];
       if (n_tiles > 0) {
         tmem_ld32(tmem_dq + lane_addr + cidx * 32, r);
@@ -382,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -461,21 +473,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->qd_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, 128);
-    mbar_init(&bars->pb_full, 128);
+    mbar_init(&bars->sdp_empty, 256);
+    mbar_init(&bars->pb_full, 256);
     mbar_init(&bars->pb_empty, 1);
     mbar_init(&bars->done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dv = tmem + 256, tmem_dk = tmem + 256 + HD;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0 && n_units > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
@@ -503,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0 && n_units > 0) {
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
@@ -559,10 +571,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int row = threadIdx.x;  // key within the tile
+    const int wg = warp >> 2;          // warpgroup wg owns query columns [64 wg, 64 wg + 64)
+    const int row = threadIdx.x & 127;  // key within the tile
     const int j = k0 + row;
     const bool key_ok = j < g.k_len;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const float zs = zscale<NORM>(p.scale);
     bool ok = true;
     uint32_t pbc = 0;
@@ -573,8 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m_lo + u % n_m;
       const int qbase = m * kBM;
       // stage the statistics of this tile's 128 query rows
-      named_bar_sync(1, 128);
-      {
+      named_bar_sync(1, 256);
+      if (wg == 0) {
         const int iq = qbase + row;
         float a = kPosInf, bb = 1.f, cc = 0.f;
         if (iq < g.q_len) {
@@ -588,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / bb : 1.f;
         crs[row] = cc;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (!ok) continue;
       if (!(ok = wait_warp(&bars->sdp_full, u & 1, abort_flag))) continue;
       tc_fence_after();
@@ -597,9 +610,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int c_lo = p.causal ? jl - qbase : -1 << 30;
       int c_hi = key_ok ? g.q_len - qbase : -(1 << 30);
       if (p.window_left > 0) c_hi = min(c_hi, jl + p.window_left - qbase);
-      uint32_t ppk[64], dpk[64];
+      uint32_t ppk[32], dpk[32];
 #pragma unroll
-      for (int cidx = 0; cidx < 4; ++cidx) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int cidx = wg * 2 + cc;
         uint32_t rs[32], rd[32];
         tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
         tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
@@ -617,8 +631,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             pv[x] = pr;
             dsv[x] = w * (__uint_as_float(rd[e + x]) - crs[col]);
           }
-          ppk[cidx * 16 + e / 2] = pack2<BF16>(pv[0], pv[1]);
-          dpk[cidx * 16 + e / 2] = pack2<BF16>(dsv[0], dsv[1]);
+          ppk[cc * 16 + e / 2] = pack2<BF16>(pv[0], pv[1]);
+          dpk[cc * 16 + e / 2] = pack2<BF16>(dsv[0], dsv[1]);
         }
       }
       tc_fence_before();
@@ -628,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (pbc > 0) {
           if (!(ok = wait_warp(&bars->pb_empty, (pbc - 1) & 1, abort_flag))) break;
         }
-        store_row_sw128(smem + L::PB, row, which == 0 ? ppk : dpk);
+        store_half_sw128(smem + L::PB, wg, row, which == 0 ? ppk : dpk);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars->pb_full);
@@ -647,8 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t boff = varlen ? 0 : (int64_t)b;
     T* dkrow = static_cast<T*>(p.dk) + boff * p.dk_sb + (int64_t)kvh * p.dk_sh + kt * p.dk_st;
     T* dvrow = static_cast<T*>(p.dv) + boff * p.dv_sb + (int64_t)kvh * p.dv_sh + kt * p.dv_st;
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
+    {
+      const int which = wg;  // warpgroup 0 stores dV, warpgroup 1 stores dK
       const uint32_t src = which == 0 ? tmem_dv : tmem_dk;
       const float f = which == 0 ? 1.f : p.scale;
       T* dst = which == 0 ? dvrow : dkrow;
@@ -680,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);

@@ -44,6 +44,15 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* base, int row, const ui
   }
 }
 
+// One 64-column half (hh = 0 or 1) of such a row: 32 packed pairs.
+__device__ __forceinline__ void store_half_sw128(uint8_t* base, int hh, int row, const uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 v = make_uint4(pk[c * 4 + 0], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+    *reinterpret_cast<uint4*>(base + hh * kHalf + row * 128 + ((c ^ (row & 7)) << 4)) = v;
+  }
+}
+
 // ------------------------------------------------------------------ host
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
