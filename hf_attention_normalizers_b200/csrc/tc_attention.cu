@@ -40,7 +40,7 @@ constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kStages = 2;         // K and V ring depth
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 2 row warpgroups (warps 0-7), TMA warp 8, MMA warp 9
 constexpr float kRescaleLog2 = 8.f;
 
 enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2 };
@@ -69,7 +69,8 @@ struct Layout {
   static constexpr uint32_t P = V + kStages * NH * kHalf;
   static constexpr uint32_t BARS = P + 2 * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(Bars);
-  static constexpr uint32_t TOTAL = CTL + sizeof(Ctl) + 1024;  // + alignment slack
+  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;  // warpgroup exchange, 8 KB
+  static constexpr uint32_t TOTAL = XCH + 8192 + 1024;                // + alignment slack
 };
 
 __device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
@@ -97,12 +98,13 @@ struct Cand {
 // best lower bound after `max_iter` steps) and its support size.
 template <int NORM>
 __device__ float buffer_solve(const float* buf, int row, int n, float t0, int max_iter, bool* exact,
-                              float* support) {
+                              float* support, const float* buf2 = nullptr, int n2 = 0) {
   float t = t0, tau = t0;
   *exact = false;
   for (int it = 0; it < max_iter; ++it) {
     TauStats st{0.f, 0.f, 0.f, kPosInf};
     for (int e = 0; e < n; ++e) tau_accumulate(st, buf[e * 128 + row], t);
+    for (int e = 0; e < n2; ++e) tau_accumulate(st, buf2[e * 128 + row], t);
     *support = st.cnt;
     if (st.cnt == 0.f) break;
     if (tau_step(NORM, st, &t, &tau)) {
@@ -186,9 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_empty[s], 128);
+      mbar_init(&bars->s_empty[s], 256);
     }
-    mbar_init(&bars->p_full, 128);
+    mbar_init(&bars->p_full, 256);
     mbar_init(&bars->pv_done, 1);
     mbar_init(&bars->ctrl, 1);
     ctl->abort = 0;
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ctl->any_pending = 0;
     fence_barrier_init();
   }
-  if (warp == 5) tmem_alloc(&ctl->tmem_base, 512);
+  if (warp == 9) tmem_alloc(&ctl->tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_o = tmem + 256;
   volatile int* abort_flag = &ctl->abort;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       prefetch_tmap(&tm_q);
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) record_error(p, ctl, kDevWaitTimeout);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q);
@@ -306,10 +308,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ normalizer
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const int i = q0 + row;       // query row within the sequence
+    // Two warpgroups share each 128-row tile: warpgroup wg owns key columns
+    // [64 wg, 64 wg + 64) of every S tile and head-dim columns
+    // [HD/2 wg, HD/2 (wg + 1)) of O.  Row-wide quantities (softmax1 max and
+    // denominator, the sparse threshold) are combined through shared memory.
+    const int wg = warp >> 2;
+    const int row = threadIdx.x & 127;  // TMEM lane
+    const int i = q0 + row;             // query row within the sequence
     const bool row_ok = i < g.q_len;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const int limit = i + g.k_len - g.q_len;
     // visible keys of this row: [vis_lo, vis_hi)
     int vis_hi = row_ok ? g.k_len : 0;
@@ -319,33 +326,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float zs = NORM == HFAN_SOFTMAX1 ? p.scale * kLog2e
                                            : (NORM == HFAN_SPARSEMAX ? p.scale : 0.5f * p.scale);
     // During the scan passes the V ring and the P buffer are idle; they hold
-    // the candidate buffer (the producer loads V only in the final pass).
-    float* cbuf = reinterpret_cast<float*>(smem + L::V);
-    constexpr int CAP = (int)((kStages * NH * kHalf + 2 * kHalf) / (128 * 4));
+    // the candidate buffers (the producer loads V only in the final pass),
+    // one half per warpgroup.
+    constexpr int CAPW = (int)((kStages * NH * kHalf + 2 * kHalf) / (128 * 4)) / 2;
+    float* cbuf0 = reinterpret_cast<float*>(smem + L::V);
+    float* cbuf = cbuf0 + wg * CAPW * 128;
+    float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [2048] floats
     uint8_t* sP = smem + L::P;
+    constexpr int HALF_COLS = kBN / 2;
 
     uint32_t sc = 0, pc = 0;
     bool ok = true;
-    float sreg[kBN];  // raw scores s = q.k of the current tile (masked: -inf)
+    float sreg[HALF_COLS];  // raw scores s = q.k of this warpgroup's 64 columns (masked: -inf)
     auto load_s = [&](int t) -> bool {
       const int sb = sc & 1;
       if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
-      uint32_t r[4][32];
+      uint32_t r[2][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + c * 32, r[c]);
+      for (int c = 0; c < 2; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + wg * HALF_COLS + c * 32, r[c]);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars->s_empty[sb]);
       ++sc;
-      const int kb = k_lo + t * kBN;
+      const int kb = k_lo + t * kBN + wg * HALF_COLS;
       const int lo = vis_lo - kb, hi = vis_hi - kb;
-      if (__all_sync(0xffffffffu, lo <= 0 && hi >= kBN)) {
+      if (__all_sync(0xffffffffu, lo <= 0 && hi >= HALF_COLS)) {
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) sreg[j] = __uint_as_float(r[j >> 5][j & 31]);
+        for (int j = 0; j < HALF_COLS; ++j) sreg[j] = __uint_as_float(r[j >> 5][j & 31]);
       } else {
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) : kNegInf;
+        for (int j = 0; j < HALF_COLS; ++j)
+          sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) : kNegInf;
       }
       return true;
     };
@@ -358,10 +370,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < n_tiles && ok; ++t) {
         if (!(ok = load_s(t))) break;
         // chunk maxima (8 keys each) gate the candidate appends
-        float cm[kBN / 8];
+        float cm[HALF_COLS / 8];
         float tm = kNegInf;
 #pragma unroll
-        for (int c = 0; c < kBN / 8; ++c) {
+        for (int c = 0; c < HALF_COLS / 8; ++c) {
           float m8 = sreg[c * 8];
 #pragma unroll
           for (int e = 1; e < 8; ++e) m8 = fmaxf(m8, sreg[c * 8 + e]);
@@ -375,9 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (HFAN_EXP != 1 && !cd.overflow && tm > cd.thr_s) {
 #pragma unroll
-          for (int c = 0; c < kBN / 8; ++c) {
+          for (int c = 0; c < HALF_COLS / 8; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
-              if (cd.n > CAP - 8) cd = buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
+              if (cd.n > CAPW - 8) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
               if (!cd.overflow) {
                 // predicated appends: every value is written at slot n, and n
                 // only advances past the candidates
@@ -391,71 +403,108 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (__any_sync(0xffffffffu, cd.n > CAP / 2 && !cd.overflow)) {
-          if (cd.n > CAP / 4 && !cd.overflow) cd = buffer_compact<NORM>(cbuf, row, cd, CAP, zs);
+        if (__any_sync(0xffffffffu, cd.n > CAPW / 2 && !cd.overflow)) {
+          if (cd.n > CAPW / 4 && !cd.overflow) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
         }
       }
-      // exact threshold from the buffer, or a lower bound for bracket sweeps
-      float lower = cd.thr;
-      bool pending = false;
-      if (!(zmax > kNegInf)) {
-        tau = kPosInf;  // no visible key: zero row
-      } else if (!cd.overflow) {
-        bool exact;
-        float t_or_root = buffer_solve<NORM>(cbuf, row, cd.n, cd.thr, 64, &exact, &support);
-        if (exact) {
-          tau = t_or_root;
+      // merge the two halves: warpgroup 0 solves tau on both buffers
+      float* xs = xch;  // [2 wg][128 rows][4]
+      xs[(wg * 128 + row) * 4 + 0] = zmax;
+      xs[(wg * 128 + row) * 4 + 1] = cd.thr;
+      xs[(wg * 128 + row) * 4 + 2] = cd.overflow ? 1.f : 0.f;
+      xs[(wg * 128 + row) * 4 + 3] = __int_as_float(cd.n);
+      named_bar_sync(1, 256);
+      float* bc = xch + 1024;  // [128 rows][4]: tau, support, pending, lower
+      if (wg == 0) {
+        const float* o = xs + (128 + row) * 4;
+        const float zrow = fmaxf(zmax, o[0]);
+        float lower = fmaxf(cd.thr, o[1]);
+        bool pending = false;
+        if (!(zrow > kNegInf)) {
+          tau = kPosInf;  // no visible key: zero row
+        } else if (!cd.overflow && o[2] == 0.f) {
+          bool exact;
+          const float r = buffer_solve<NORM>(cbuf0, row, cd.n, lower, 64, &exact, &support,
+                                             cbuf0 + CAPW * 128, __float_as_int(o[3]));
+          if (exact) {
+            tau = r;
+          } else {
+            pending = true;
+            lower = r;
+          }
         } else {
           pending = true;
-          lower = t_or_root;
         }
-      } else {
-        pending = true;
+        bc[row * 4 + 0] = tau;
+        bc[row * 4 + 1] = support;
+        bc[row * 4 + 2] = pending ? 1.f : 0.f;
+        bc[row * 4 + 3] = lower;
       }
+      named_bar_sync(1, 256);
+      tau = bc[row * 4 + 0];
+      support = bc[row * 4 + 1];
+      bool pending = bc[row * 4 + 2] != 0.f;
+      float lower = bc[row * 4 + 3];
       for (int sweep = 0;; ++sweep) {
-        // CTA-wide decision (uniform across the 128 normalizer threads):
-        // another bracket sweep, or the final pass.
-        named_bar_sync(1, 128);
-        if (row == 0) ctl->any_pending = 0;
-        named_bar_sync(1, 128);
+        // CTA-wide decision (uniform across the 256 row threads): another
+        // bracket sweep, or the final pass.
+        named_bar_sync(1, 256);
+        if (threadIdx.x == 0) ctl->any_pending = 0;
+        named_bar_sync(1, 256);
         if (pending) ctl->any_pending = 1;
         if (!ok) ctl->abort = 1;
-        named_bar_sync(1, 128);
-        if (row == 0) {
+        named_bar_sync(1, 256);
+        if (threadIdx.x == 0) {
           const bool more_ = ctl->any_pending != 0 && sweep < kMaxSweeps && ctl->abort == 0;
           ctl->next_pass = more_ ? kPassSweep : kPassFinal;
           mbar_arrive(&bars->ctrl);
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 256);
         if (ctl->next_pass != kPassSweep) break;
         TauStats st{0.f, 0.f, 0.f, kPosInf};
         for (int t = 0; t < n_tiles && ok; ++t) {
           if (!(ok = load_s(t))) break;
           if (pending) {
 #pragma unroll
-            for (int j = 0; j < kBN; ++j) tau_accumulate(st, sreg[j] * zs, lower);
+            for (int j = 0; j < HALF_COLS; ++j) tau_accumulate(st, sreg[j] * zs, lower);
           }
         }
+        // combine the halves' sums; both warpgroups then take the same step
+        float* xt = xch;  // [2 wg][128 rows][4], free again once the merge above was read
+        xt[(wg * 128 + row) * 4 + 0] = st.cnt;
+        xt[(wg * 128 + row) * 4 + 1] = st.s1;
+        xt[(wg * 128 + row) * 4 + 2] = st.s2;
+        xt[(wg * 128 + row) * 4 + 3] = st.zmin;
+        named_bar_sync(1, 256);
+        const float* o = xt + ((1 - wg) * 128 + row) * 4;
+        TauStats all{st.cnt + o[0], st.s1 + o[1], st.s2 + o[2], fminf(st.zmin, o[3])};
+        named_bar_sync(1, 256);
         if (pending && ok) {
-          support = st.cnt;
-          pending = !tau_step(NORM, st, &lower, &tau);
+          support = all.cnt;
+          pending = !tau_step(NORM, all, &lower, &tau);
         }
       }
     }
 
     // ---- final pass: P and O
-    float m_ref = 0.f, l = 1.f;
+    float m_ref = 0.f, l = wg == 0 ? 1.f : 0.f;  // the implicit zero logit counts once
     const float ntau = -tau;
-    for (int t = 0; t < n_tiles && ok; ++t) {
-      if (!(ok = load_s(t))) break;
+    // softmax1 meets a named barrier on every tile, so after a timeout the loop
+    // keeps running (with the work skipped) instead of leaving it.
+    for (int t = 0; t < n_tiles && (ok || !SPARSE); ++t) {
+      if (ok) ok = load_s(t);
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
-        // log2 units: x = s * scale * log2(e)
+        // log2 units: x = s * scale * log2(e); the row max of both halves
         float tmax = kNegInf;
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) tmax = fmaxf(tmax, sreg[j]);
+        for (int j = 0; j < HALF_COLS; ++j) tmax = fmaxf(tmax, sreg[j]);
         tmax *= zs;
+        float* xm = xch + (t & 1) * 256;  // double-buffered by tile parity: one barrier per tile
+        xm[wg * 128 + row] = tmax;
+        named_bar_sync(1, 256);
+        tmax = fmaxf(tmax, xm[(1 - wg) * 128 + row]);
         if (tmax > m_ref + kRescaleLog2) {
           alpha = exp2f(m_ref - tmax);
           m_ref = tmax;
@@ -465,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float nm = -m_ref;
         float lsum = 0.f;
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) {
+        for (int j = 0; j < HALF_COLS; ++j) {
           float e = exp2f(fmaf(sreg[j], zs, nm));  // exp2(-inf) = 0 for masked keys
           sreg[j] = e;
           lsum += e;
@@ -473,14 +522,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += lsum;
       } else {
 #pragma unroll
-        for (int j = 0; j < kBN; ++j) {
+        for (int j = 0; j < HALF_COLS; ++j) {
           float d = fmaxf(fmaf(sreg[j], zs, ntau), 0.f);
           sreg[j] = NORM == HFAN_SPARSEMAX ? d : d * d;
         }
       }
+      if (!ok) continue;
       // P buffer and O are free once the previous P V has completed.
       if (t > 0) {
-        if (!(ok = wait_warp(&bars->pv_done, (pc - 1) & 1, abort_flag))) break;
+        if (!(ok = wait_warp(&bars->pv_done, (pc - 1) & 1, abort_flag))) continue;
         tc_fence_after();
       }
       if (__any_sync(0xffffffffu, rescale)) {
@@ -488,26 +538,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float f = rescale ? alpha : 1.f;
         uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          tmem_ld32(tmem_o + lane_addr + c * 32, r);
+        for (int c = 0; c < HD / 64; ++c) {
+          const uint32_t col = wg * (HD / 2) + c * 32;
+          tmem_ld32(tmem_o + lane_addr + col, r);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
-          tmem_st32(tmem_o + lane_addr + c * 32, r);
+          tmem_st32(tmem_o + lane_addr + col, r);
         }
         tmem_wait_st();
       }
-      // P row -> shared memory, 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < kBN / 8; ++c) {
-        const int hh = c >> 3, cc = c & 7;
-        uint4 v;
-        v.x = pack2<BF16>(sreg[c * 8 + 0], sreg[c * 8 + 1]);
-        v.y = pack2<BF16>(sreg[c * 8 + 2], sreg[c * 8 + 3]);
-        v.z = pack2<BF16>(sreg[c * 8 + 4], sreg[c * 8 + 5]);
-        v.w = pack2<BF16>(sreg[c * 8 + 6], sreg[c * 8 + 7]);
-        *reinterpret_cast<uint4*>(sP + hh * kHalf + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
-      }
+      for (int j = 0; j < HALF_COLS; j += 2) pk[j / 2] = pack2<BF16>(sreg[j], sreg[j + 1]);
+      store_half_sw128(sP, wg, row, pk);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_full);
@@ -518,17 +562,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
     }
     if (!ok) record_error(p, ctl, kDevWaitTimeout);
+    if (!SPARSE) {
+      // total denominator of the row
+      float* xl = xch + 512;
+      xl[wg * 128 + row] = l;
+      named_bar_sync(1, 256);
+      l += xl[(1 - wg) * 128 + row];
+    }
 
-    // ---- epilogue: O row -> global, row statistics.  The TMEM loads are
-    // warp-collective, so every lane loads; only valid rows store.
+    // ---- epilogue: this warpgroup's half of the O row -> global, row statistics.
+    // The TMEM loads are warp-collective, so every lane loads; only valid rows store.
     {
       const float inv = SPARSE ? 1.f : 1.f / l;
       T* orow = static_cast<T*>(p.o) + qrow_off(p, g, b, h, row_ok ? i : 0, p.o_sb, p.o_sh, p.o_st);
       uint32_t r[32];
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = wg * (HD / 2) + c * 32;
         if (n_tiles > 0) {
-          tmem_ld32(tmem_o + lane_addr + c * 32, r);
+          tmem_ld32(tmem_o + lane_addr + col, r);
           tmem_wait_ld();
         }
         if (n_tiles == 0 || !ok) {
@@ -543,12 +595,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             v.y = pack2<BF16>(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
             v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
             v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + j) = v;
+            *reinterpret_cast<uint4*>(orow + col + j) = v;
           }
         }
       }
     }
-    if (row_ok) {
+    if (row_ok && wg == 0) {
       const int64_t si = stat_index(p, g, h, i);
       if (SPARSE) {
         p.stats[si] = tau;
@@ -562,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
