@@ -40,7 +40,15 @@ constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kStages = 2;         // K and V ring depth
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
-constexpr int kThreads = 320;  // 2 row warpgroups (warps 0-7), TMA warp 8, MMA warp 9
+// Row warpgroups per CTA: HD / 32 (each owns 128 / NWG key columns of a tile
+// and 32 head-dim columns of O), then one TMA warp and one MMA warp.
+template <int HD> struct Roles {
+  static constexpr int NWG = HD / 32;
+  static constexpr int ROW_THREADS = 128 * NWG;
+  static constexpr int TMA_WARP = 4 * NWG;
+  static constexpr int MMA_WARP = 4 * NWG + 1;
+  static constexpr int THREADS = 32 * (4 * NWG + 2);
+};
 constexpr float kRescaleLog2 = 8.f;
 
 enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2 };
@@ -69,8 +77,8 @@ struct Layout {
   static constexpr uint32_t P = V + kStages * NH * kHalf;
   static constexpr uint32_t BARS = P + 2 * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(Bars);
-  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;  // warpgroup exchange, 8 KB
-  static constexpr uint32_t TOTAL = XCH + 8192 + 1024;                // + alignment slack
+  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;  // warpgroup exchange, 16 KB
+  static constexpr uint32_t TOTAL = XCH + 16384 + 1024;               // + alignment slack
 };
 
 __device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
@@ -98,13 +106,60 @@ struct Cand {
 // best lower bound after `max_iter` steps) and its support size.
 template <int NORM>
 __device__ float buffer_solve(const float* buf, int row, int n, float t0, int max_iter, bool* exact,
-                              float* support, const float* buf2 = nullptr, int n2 = 0) {
+                              float* support) {
   float t = t0, tau = t0;
   *exact = false;
   for (int it = 0; it < max_iter; ++it) {
     TauStats st{0.f, 0.f, 0.f, kPosInf};
     for (int e = 0; e < n; ++e) tau_accumulate(st, buf[e * 128 + row], t);
-    for (int e = 0; e < n2; ++e) tau_accumulate(st, buf2[e * 128 + row], t);
+    *support = st.cnt;
+    if (st.cnt == 0.f) break;
+    if (tau_step(NORM, st, &t, &tau)) {
+      *exact = true;
+      return tau;
+    }
+  }
+  return t;
+}
+
+// Lower bound of tau from the four largest chunk maxima z1 >= z2 >= z3 >= z4
+// (z units, -inf when missing): any k distinct scores whose closed-form
+// threshold t_k lies at or below the smallest of them give f(t_k) >= 1,
+// hence t_k <= tau.  k = 1 is the zmax - 1 bound.
+template <int NORM>
+__device__ __forceinline__ float top4_bound(float z1, float z2, float z3, float z4) {
+  const float zz[4] = {z1, z2, z3, z4};
+  float best = z1 - 1.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int k = 1; k <= 4; ++k) {
+    const float y = zz[k - 1] - z1;
+    if (!(zz[k - 1] > kNegInf)) break;
+    s1 += y;
+    s2 += y * y;
+    float t;
+    if (NORM == HFAN_SPARSEMAX) {
+      t = (s1 - 1.f) / k;
+    } else {
+      const float mean = s1 / k;
+      t = mean - sqrtf(fmaxf((1.f - (s2 - s1 * mean)) / k, 0.f));
+    }
+    if (t <= y) best = fmaxf(best, z1 + t);
+  }
+  return best;
+}
+
+// The same solve over the NW per-warpgroup buffers of one row (buffer w holds
+// ns[w] entries starting at entry w * capw).
+template <int NORM, int NW>
+__device__ float buffer_solve_multi(const float* buf0, int capw, int row, const int (&ns)[NW], float t0,
+                                    int max_iter, bool* exact, float* support) {
+  float t = t0, tau = t0;
+  *exact = false;
+  for (int it = 0; it < max_iter; ++it) {
+    TauStats st{0.f, 0.f, 0.f, kPosInf};
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+      for (int e = 0; e < ns[w]; ++e) tau_accumulate(st, buf0[(w * capw + e) * 128 + row], t);
     *support = st.cnt;
     if (st.cnt == 0.f) break;
     if (tau_step(NORM, st, &t, &tau)) {
@@ -132,13 +187,13 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
     if (z > c.thr) buf[live++ * 128 + row] = z;
   }
   c.n = live;
-  if (live > (3 * cap) / 4) c.overflow = true;
+  if (live > cap - 12) c.overflow = true;  // compaction no longer frees room for a chunk of appends
   return c;
 }
 
 // ------------------------------------------------------------------ kernel
 template <int HD, bool BF16, int NORM>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   using L = Layout<HD>;
@@ -188,9 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_empty[s], 256);
+      mbar_init(&bars->s_empty[s], Roles<HD>::ROW_THREADS);
     }
-    mbar_init(&bars->p_full, 256);
+    mbar_init(&bars->p_full, Roles<HD>::ROW_THREADS);
     mbar_init(&bars->pv_done, 1);
     mbar_init(&bars->ctrl, 1);
     ctl->abort = 0;
@@ -198,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ctl->any_pending = 0;
     fence_barrier_init();
   }
-  if (warp == 9) tmem_alloc(&ctl->tmem_base, 512);
+  if (warp == Roles<HD>::MMA_WARP) tmem_alloc(&ctl->tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -206,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_o = tmem + 256;
   volatile int* abort_flag = &ctl->abort;
 
-  if (warp == 8) {
+  if (warp == Roles<HD>::TMA_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       prefetch_tmap(&tm_q);
@@ -246,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) record_error(p, ctl, kDevWaitTimeout);
     }
-  } else if (warp == 9) {
+  } else if (warp == Roles<HD>::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q);
@@ -308,10 +363,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ normalizer
-    // Two warpgroups share each 128-row tile: warpgroup wg owns key columns
-    // [64 wg, 64 wg + 64) of every S tile and head-dim columns
-    // [HD/2 wg, HD/2 (wg + 1)) of O.  Row-wide quantities (softmax1 max and
+    // NWG warpgroups share each 128-row tile: warpgroup wg owns key columns
+    // [COLS wg, COLS (wg + 1)) of every S tile and head-dim columns
+    // [32 wg, 32 wg + 32) of O.  Row-wide quantities (softmax1 max and
     // denominator, the sparse threshold) are combined through shared memory.
+    constexpr int NWG = Roles<HD>::NWG;
+    constexpr int NT = Roles<HD>::ROW_THREADS;
+    constexpr int COLS = kBN / NWG;
     const int wg = warp >> 2;
     const int row = threadIdx.x & 127;  // TMEM lane
     const int i = q0 + row;             // query row within the sequence
@@ -327,37 +385,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            : (NORM == HFAN_SPARSEMAX ? p.scale : 0.5f * p.scale);
     // During the scan passes the V ring and the P buffer are idle; they hold
     // the candidate buffers (the producer loads V only in the final pass),
-    // one half per warpgroup.
-    constexpr int CAPW = (int)((kStages * NH * kHalf + 2 * kHalf) / (128 * 4)) / 2;
+    // one slice per warpgroup.
+    constexpr int CAPW = (int)((kStages * NH * kHalf + 2 * kHalf) / (128 * 4)) / NWG;
     float* cbuf0 = reinterpret_cast<float*>(smem + L::V);
     float* cbuf = cbuf0 + wg * CAPW * 128;
-    float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [2048] floats
+    float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [4096] floats
     uint8_t* sP = smem + L::P;
-    constexpr int HALF_COLS = kBN / 2;
 
     uint32_t sc = 0, pc = 0;
     bool ok = true;
-    float sreg[HALF_COLS];  // raw scores s = q.k of this warpgroup's 64 columns (masked: -inf)
+    float sreg[COLS];  // raw scores s = q.k of this warpgroup's columns (masked: -inf)
     auto load_s = [&](int t) -> bool {
       const int sb = sc & 1;
       if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
-      uint32_t r[2][32];
+      uint32_t r[COLS / 32][32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + wg * HALF_COLS + c * 32, r[c]);
+      for (int c = 0; c < COLS / 32; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + wg * COLS + c * 32, r[c]);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars->s_empty[sb]);
       ++sc;
-      const int kb = k_lo + t * kBN + wg * HALF_COLS;
+      const int kb = k_lo + t * kBN + wg * COLS;
       const int lo = vis_lo - kb, hi = vis_hi - kb;
-      if (__all_sync(0xffffffffu, lo <= 0 && hi >= HALF_COLS)) {
+      if (__all_sync(0xffffffffu, lo <= 0 && hi >= COLS)) {
 #pragma unroll
-        for (int j = 0; j < HALF_COLS; ++j) sreg[j] = __uint_as_float(r[j >> 5][j & 31]);
+        for (int j = 0; j < COLS; ++j) sreg[j] = __uint_as_float(r[j >> 5][j & 31]);
       } else {
 #pragma unroll
-        for (int j = 0; j < HALF_COLS; ++j)
-          sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) : kNegInf;
+        for (int j = 0; j < COLS; ++j) sreg[j] = (j >= lo && j < hi) ? __uint_as_float(r[j >> 5][j & 31]) : kNegInf;
       }
       return true;
     };
@@ -367,27 +423,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (SCAN) {
       Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
+      float t1 = kNegInf, t2 = kNegInf, t3 = kNegInf, t4 = kNegInf;  // top-4 chunk maxima (raw)
+      // Every warpgroup's bound is a lower bound of the row's tau, so they
+      // publish it and adopt the largest (a stale read is still a valid bound).
+      volatile float* xb = xch + 3072;  // [NWG][128]
+      xb[wg * 128 + row] = kNegInf;
+      named_bar_sync(1, NT);
       for (int t = 0; t < n_tiles && ok; ++t) {
         if (!(ok = load_s(t))) break;
         // chunk maxima (8 keys each) gate the candidate appends
-        float cm[HALF_COLS / 8];
+        float cm[COLS / 8];
         float tm = kNegInf;
 #pragma unroll
-        for (int c = 0; c < HALF_COLS / 8; ++c) {
+        for (int c = 0; c < COLS / 8; ++c) {
           float m8 = sreg[c * 8];
 #pragma unroll
           for (int e = 1; e < 8; ++e) m8 = fmaxf(m8, sreg[c * 8 + e]);
           cm[c] = m8;
           tm = fmaxf(tm, m8);
+          float x = m8, n1;
+          n1 = fmaxf(t1, x); x = fminf(t1, x); t1 = n1;
+          n1 = fmaxf(t2, x); x = fminf(t2, x); t2 = n1;
+          n1 = fmaxf(t3, x); x = fminf(t3, x); t3 = n1;
+          t4 = fmaxf(t4, x);
         }
         zmax = fmaxf(zmax, tm * zs);
-        if (zmax - 1.f > cd.thr) {
-          cd.thr = zmax - 1.f;
-          cd.thr_s = cd.thr / zs;
+        {
+          float lb = t1 > kNegInf ? top4_bound<NORM>(t1 * zs, t2 * zs, t3 * zs, t4 * zs) : kNegInf;
+#pragma unroll
+          for (int w = 0; w < NWG; ++w) lb = fmaxf(lb, xb[w * 128 + row]);
+          if (lb > cd.thr) {
+            cd.thr = lb;
+            cd.thr_s = lb / zs;
+          }
         }
         if (HFAN_EXP != 1 && !cd.overflow && tm > cd.thr_s) {
 #pragma unroll
-          for (int c = 0; c < HALF_COLS / 8; ++c) {
+          for (int c = 0; c < COLS / 8; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
               if (cd.n > CAPW - 8) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
               if (!cd.overflow) {
@@ -403,29 +475,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (__any_sync(0xffffffffu, cd.n > CAPW / 2 && !cd.overflow)) {
-          if (cd.n > CAPW / 4 && !cd.overflow) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
+        // warp-uniform compaction once a lane nears capacity (lanes over half full join)
+        if (__any_sync(0xffffffffu, cd.n > CAPW - 12 && !cd.overflow)) {
+          if (cd.n > CAPW / 2 && !cd.overflow) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
         }
+        xb[wg * 128 + row] = cd.thr;
       }
-      // merge the two halves: warpgroup 0 solves tau on both buffers
-      float* xs = xch;  // [2 wg][128 rows][4]
+      // merge the warpgroups: warpgroup 0 solves tau on all buffers of the row
+      float* xs = xch;  // [NWG][128 rows][4]
       xs[(wg * 128 + row) * 4 + 0] = zmax;
       xs[(wg * 128 + row) * 4 + 1] = cd.thr;
       xs[(wg * 128 + row) * 4 + 2] = cd.overflow ? 1.f : 0.f;
       xs[(wg * 128 + row) * 4 + 3] = __int_as_float(cd.n);
-      named_bar_sync(1, 256);
-      float* bc = xch + 1024;  // [128 rows][4]: tau, support, pending, lower
+      named_bar_sync(1, NT);
+      float* bc = xch + NWG * 512;  // [128 rows][4]: tau, support, pending, lower
       if (wg == 0) {
-        const float* o = xs + (128 + row) * 4;
-        const float zrow = fmaxf(zmax, o[0]);
-        float lower = fmaxf(cd.thr, o[1]);
+        float zrow = kNegInf, lower = kNegInf;
+        bool ovf = false;
+        int ns[NWG];
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          const float* o = xs + (w * 128 + row) * 4;
+          zrow = fmaxf(zrow, o[0]);
+          lower = fmaxf(lower, o[1]);
+          ovf |= o[2] != 0.f;
+          ns[w] = __float_as_int(o[3]);
+        }
         bool pending = false;
         if (!(zrow > kNegInf)) {
           tau = kPosInf;  // no visible key: zero row
-        } else if (!cd.overflow && o[2] == 0.f) {
+        } else if (!ovf) {
           bool exact;
-          const float r = buffer_solve<NORM>(cbuf0, row, cd.n, lower, 64, &exact, &support,
-                                             cbuf0 + CAPW * 128, __float_as_int(o[3]));
+          const float r = buffer_solve_multi<NORM, NWG>(cbuf0, CAPW, row, ns, lower, 64, &exact, &support);
           if (exact) {
             tau = r;
           } else {
@@ -440,45 +521,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         bc[row * 4 + 2] = pending ? 1.f : 0.f;
         bc[row * 4 + 3] = lower;
       }
-      named_bar_sync(1, 256);
+      named_bar_sync(1, NT);
       tau = bc[row * 4 + 0];
       support = bc[row * 4 + 1];
       bool pending = bc[row * 4 + 2] != 0.f;
       float lower = bc[row * 4 + 3];
       for (int sweep = 0;; ++sweep) {
-        // CTA-wide decision (uniform across the 256 row threads): another
+        // CTA-wide decision (uniform across the row threads): another
         // bracket sweep, or the final pass.
-        named_bar_sync(1, 256);
+        named_bar_sync(1, NT);
         if (threadIdx.x == 0) ctl->any_pending = 0;
-        named_bar_sync(1, 256);
+        named_bar_sync(1, NT);
         if (pending) ctl->any_pending = 1;
         if (!ok) ctl->abort = 1;
-        named_bar_sync(1, 256);
+        named_bar_sync(1, NT);
         if (threadIdx.x == 0) {
           const bool more_ = ctl->any_pending != 0 && sweep < kMaxSweeps && ctl->abort == 0;
           ctl->next_pass = more_ ? kPassSweep : kPassFinal;
           mbar_arrive(&bars->ctrl);
         }
-        named_bar_sync(1, 256);
+        named_bar_sync(1, NT);
         if (ctl->next_pass != kPassSweep) break;
         TauStats st{0.f, 0.f, 0.f, kPosInf};
         for (int t = 0; t < n_tiles && ok; ++t) {
           if (!(ok = load_s(t))) break;
           if (pending) {
 #pragma unroll
-            for (int j = 0; j < HALF_COLS; ++j) tau_accumulate(st, sreg[j] * zs, lower);
+            for (int j = 0; j < COLS; ++j) tau_accumulate(st, sreg[j] * zs, lower);
           }
         }
-        // combine the halves' sums; both warpgroups then take the same step
-        float* xt = xch;  // [2 wg][128 rows][4], free again once the merge above was read
+        // combine the warpgroups' sums; all then take the same step
+        float* xt = xch;  // [NWG][128 rows][4], free again once the merge above was read
         xt[(wg * 128 + row) * 4 + 0] = st.cnt;
         xt[(wg * 128 + row) * 4 + 1] = st.s1;
         xt[(wg * 128 + row) * 4 + 2] = st.s2;
         xt[(wg * 128 + row) * 4 + 3] = st.zmin;
-        named_bar_sync(1, 256);
-        const float* o = xt + ((1 - wg) * 128 + row) * 4;
-        TauStats all{st.cnt + o[0], st.s1 + o[1], st.s2 + o[2], fminf(st.zmin, o[3])};
-        named_bar_sync(1, 256);
+        named_bar_sync(1, NT);
+        TauStats all{0.f, 0.f, 0.f, kPosInf};
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          const float* o = xt + (w * 128 + row) * 4;
+          all.cnt += o[0];
+          all.s1 += o[1];
+          all.s2 += o[2];
+          all.zmin = fminf(all.zmin, o[3]);
+        }
+        named_bar_sync(1, NT);
         if (pending && ok) {
           support = all.cnt;
           pending = !tau_step(NORM, all, &lower, &tau);
@@ -496,15 +584,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
-        // log2 units: x = s * scale * log2(e); the row max of both halves
+        // log2 units: x = s * scale * log2(e); the row max over all warpgroups
         float tmax = kNegInf;
 #pragma unroll
-        for (int j = 0; j < HALF_COLS; ++j) tmax = fmaxf(tmax, sreg[j]);
+        for (int j = 0; j < COLS; ++j) tmax = fmaxf(tmax, sreg[j]);
         tmax *= zs;
-        float* xm = xch + (t & 1) * 256;  // double-buffered by tile parity: one barrier per tile
+        float* xm = xch + (t & 1) * (NWG * 128);  // double-buffered by tile parity: one barrier per tile
         xm[wg * 128 + row] = tmax;
-        named_bar_sync(1, 256);
-        tmax = fmaxf(tmax, xm[(1 - wg) * 128 + row]);
+        named_bar_sync(1, NT);
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) tmax = fmaxf(tmax, xm[w * 128 + row]);
         if (tmax > m_ref + kRescaleLog2) {
           alpha = exp2f(m_ref - tmax);
           m_ref = tmax;
@@ -514,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float nm = -m_ref;
         float lsum = 0.f;
 #pragma unroll
-        for (int j = 0; j < HALF_COLS; ++j) {
+        for (int j = 0; j < COLS; ++j) {
           float e = exp2f(fmaf(sreg[j], zs, nm));  // exp2(-inf) = 0 for masked keys
           sreg[j] = e;
           lsum += e;
@@ -522,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         l += lsum;
       } else {
 #pragma unroll
-        for (int j = 0; j < HALF_COLS; ++j) {
+        for (int j = 0; j < COLS; ++j) {
           float d = fmaxf(fmaf(sreg[j], zs, ntau), 0.f);
           sreg[j] = NORM == HFAN_SPARSEMAX ? d : d * d;
         }
@@ -537,21 +626,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         // warp-collective: lanes without a rescale multiply by one
         const float f = rescale ? alpha : 1.f;
         uint32_t r[32];
+        tmem_ld32(tmem_o + lane_addr + wg * 32, r);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
-          const uint32_t col = wg * (HD / 2) + c * 32;
-          tmem_ld32(tmem_o + lane_addr + col, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
-          tmem_st32(tmem_o + lane_addr + col, r);
-        }
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * f);
+        tmem_st32(tmem_o + lane_addr + wg * 32, r);
         tmem_wait_st();
       }
-      uint32_t pk[32];
+      // this warpgroup's COLS columns of the P row -> 128-byte swizzled smem
 #pragma unroll
-      for (int j = 0; j < HALF_COLS; j += 2) pk[j / 2] = pack2<BF16>(sreg[j], sreg[j + 1]);
-      store_half_sw128(sP, wg, row, pk);
+      for (int c = 0; c < COLS / 8; ++c) {
+        const int chunk = wg * (COLS / 8) + c;  // 16-byte chunk index within the 128-column row
+        const int hh = chunk >> 3, cc = chunk & 7;
+        uint4 v;
+        v.x = pack2<BF16>(sreg[c * 8 + 0], sreg[c * 8 + 1]);
+        v.y = pack2<BF16>(sreg[c * 8 + 2], sreg[c * 8 + 3]);
+        v.z = pack2<BF16>(sreg[c * 8 + 4], sreg[c * 8 + 5]);
+        v.w = pack2<BF16>(sreg[c * 8 + 6], sreg[c * 8 + 7]);
+        *reinterpret_cast<uint4*>(sP + hh * kHalf + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_full);
@@ -564,39 +657,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) record_error(p, ctl, kDevWaitTimeout);
     if (!SPARSE) {
       // total denominator of the row
-      float* xl = xch + 512;
+      float* xl = xch + 2 * NWG * 128;
       xl[wg * 128 + row] = l;
-      named_bar_sync(1, 256);
-      l += xl[(1 - wg) * 128 + row];
+      named_bar_sync(1, NT);
+      l = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWG; ++w) l += xl[w * 128 + row];
     }
 
-    // ---- epilogue: this warpgroup's half of the O row -> global, row statistics.
-    // The TMEM loads are warp-collective, so every lane loads; only valid rows store.
+    // ---- epilogue: this warpgroup's 32 columns of the O row -> global, row
+    // statistics.  The TMEM load is warp-collective, so every lane loads; only
+    // valid rows store.
     {
       const float inv = SPARSE ? 1.f : 1.f / l;
       T* orow = static_cast<T*>(p.o) + qrow_off(p, g, b, h, row_ok ? i : 0, p.o_sb, p.o_sh, p.o_st);
       uint32_t r[32];
+      const int col = wg * 32;
+      if (n_tiles > 0) {
+        tmem_ld32(tmem_o + lane_addr + col, r);
+        tmem_wait_ld();
+      }
+      if (n_tiles == 0 || !ok) {
 #pragma unroll
-      for (int c = 0; c < HD / 64; ++c) {
-        const int col = wg * (HD / 2) + c * 32;
-        if (n_tiles > 0) {
-          tmem_ld32(tmem_o + lane_addr + col, r);
-          tmem_wait_ld();
-        }
-        if (n_tiles == 0 || !ok) {
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (row_ok) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
-        }
-        if (row_ok) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            uint4 v;
-            v.x = pack2<BF16>(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
-            v.y = pack2<BF16>(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
-            v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
-            v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + col + j) = v;
-          }
+        for (int j = 0; j < 32; j += 8) {
+          uint4 v;
+          v.x = pack2<BF16>(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
+          v.y = pack2<BF16>(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+          v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
+          v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + col + j) = v;
         }
       }
     }
@@ -614,7 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == Roles<HD>::MMA_WARP) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -645,17 +738,17 @@ cudaError_t launch_fwd(const AttnParams& p, int max_q, cudaStream_t stream) {
     case HFAN_SOFTMAX1:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, Roles<HD>::THREADS, smem, stream>>>(tq, tk, tv, p);
       break;
     case HFAN_SPARSEMAX:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, Roles<HD>::THREADS, smem, stream>>>(tq, tk, tv, p);
       break;
     default:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, Roles<HD>::THREADS, smem, stream>>>(tq, tk, tv, p);
       break;
   }
   return cudaGetLastError();
