@@ -40,15 +40,6 @@ constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
 constexpr int kStages = 2;         // K and V ring depth
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
-// Row warpgroups per CTA: HD / 32 (each owns 128 / NWG key columns of a tile
-// and 32 head-dim columns of O), then one TMA warp and one MMA warp.
-template <int HD> struct Roles {
-  static constexpr int NWG = HD / 32;
-  static constexpr int ROW_THREADS = 128 * NWG;
-  static constexpr int TMA_WARP = 4 * NWG;
-  static constexpr int MMA_WARP = 4 * NWG + 1;
-  static constexpr int THREADS = 32 * (4 * NWG + 2);
-};
 constexpr float kRescaleLog2 = 8.f;
 
 enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2 };

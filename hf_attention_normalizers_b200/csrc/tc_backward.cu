@@ -34,7 +34,6 @@ using namespace tc;
 
 constexpr int kBM = 128;
 constexpr int kBN = 128;
-constexpr int kThreads = 320;  // 2 row warpgroups (warps 0-7), TMA warp 8, MMA warp 9
 
 template <int NORM> __device__ __forceinline__ float zscale(float scale) {
   return NORM == HFAN_SOFTMAX1 ? scale * kLog2e : (NORM == HFAN_SPARSEMAX ? scale : 0.5f * scale);
@@ -80,7 +79,7 @@ struct QLayout {
 };
 
 template <int HD, bool BF16, int NORM>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const AttnParams p) {
@@ -129,21 +128,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, 256);
-    mbar_init(&bars->ds_full, 256);
+    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS);
+    mbar_init(&bars->ds_full, Roles<HD>::ROW_THREADS);
     mbar_init(&bars->ds_empty, 1);
     mbar_init(&bars->dq_done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
   }
-  if (warp == 9) tmem_alloc(tmem_slot, 512);
+  if (warp == Roles<HD>::MMA_WARP) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dq = tmem + 256;
 
-  if (warp == 8) {
+  if (warp == Roles<HD>::TMA_WARP) {
     if (lane == 0 && n_tiles > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
@@ -177,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == Roles<HD>::MMA_WARP) {
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
@@ -242,8 +241,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Two warpgroups share each 128 x 128 tile: warpgroup wg owns key columns
-    // [64 wg, 64 wg + 64) of every row (TMEM lanes are reached through warp % 4).
+    // NWG warpgroups share each 128 x 128 tile: warpgroup wg owns key columns
+    // [COLS wg, COLS (wg + 1)) of every row (TMEM lanes are reached through warp % 4).
+    constexpr int NWG = Roles<HD>::NWG;
+    constexpr int COLS = kBN / NWG;
+    constexpr int CPW = COLS / 32;  // 32-column TMEM chunks per warpgroup
     const int wg = warp >> 2;
     const int row = threadIdx.x & 127;
     const int i = q0 + row;
@@ -262,21 +264,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       st0 = p.stats[si];
       inv_l = NORM == HFAN_SOFTMAX1 ? 1.f / p.stats[(int64_t)p.hq * p.rows_total + si] : 1.f;
     }
-    if (NORM == HFAN_SOFTMAX1 && row_ok) {
-      // c = O . dO (the implicit sink carries no value)
-      const T* orow = static_cast<const T*>(p.o) + qrow_off(p, g, b, h, i, p.o_sb, p.o_sh, p.o_st);
-      const T* drow = static_cast<const T*>(p.dout) + qrow_off(p, g, b, h, i, p.do_sb, p.do_sh, p.do_st);
+    if (NORM == HFAN_SOFTMAX1) {
+      // c = O . dO (the implicit sink carries no value); warpgroup wg sums the
+      // head-dim slice [HD/NWG wg, HD/NWG (wg + 1)), then the slices are combined.
+      constexpr int DW = HD / NWG;
       float acc = 0.f;
-#pragma unroll 4
-      for (int d = 0; d < HD; d += 8) {
-        uint4 ov = *reinterpret_cast<const uint4*>(orow + d);
-        uint4 dv = *reinterpret_cast<const uint4*>(drow + d);
-        const T* oe = reinterpret_cast<const T*>(&ov);
-        const T* de = reinterpret_cast<const T*>(&dv);
+      if (row_ok) {
+        const T* orow = static_cast<const T*>(p.o) + qrow_off(p, g, b, h, i, p.o_sb, p.o_sh, p.o_st) + wg * DW;
+        const T* drow = static_cast<const T*>(p.dout) + qrow_off(p, g, b, h, i, p.do_sb, p.do_sh, p.do_st) + wg * DW;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc = fmaf(to_f32<T>(oe[e]), to_f32<T>(de[e]), acc);
+        for (int d = 0; d < DW; d += 8) {
+          uint4 ov = *reinterpret_cast<const uint4*>(orow + d);
+          uint4 dv = *reinterpret_cast<const uint4*>(drow + d);
+          const T* oe = reinterpret_cast<const T*>(&ov);
+          const T* de = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(to_f32<T>(oe[e]), to_f32<T>(de[e]), acc);
+        }
       }
-      c = acc;
+      float* xc = reinterpret_cast<float*>(smem + L::DS);  // dS buffer: idle until the first dS write
+      xc[wg * 128 + row] = acc;
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      c = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWG; ++w) c += xc[w * 128 + row];
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
     }
     bool ok = true;
     uint32_t sdc = 0;
@@ -303,9 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
+        for (int cc = 0; cc < CPW; ++cc) {
           float sv[32], dv[32];
-          chunk(t, wg * 2 + cc, sv, dv);
+          chunk(t, wg * CPW + cc, sv, dv);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float w, pr;
@@ -318,14 +330,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&bars->sdp_empty);
         ++sdc;
       }
-      // combine the two column halves (the dS buffer is idle until pass B)
+      // combine the warpgroups' column sums (the dS buffer is idle until pass B)
       float* xch = reinterpret_cast<float*>(smem + L::DS);
       xch[(wg * 128 + row) * 2 + 0] = num;
       xch[(wg * 128 + row) * 2 + 1] = den;
-      named_bar_sync(1, 256);
-      num = xch[row * 2] + xch[(128 + row) * 2];
-      den = xch[row * 2 + 1] + xch[(128 + row) * 2 + 1];
-      named_bar_sync(1, 256);
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      num = 0.f;
+      den = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWG; ++w) {
+        num += xch[(w * 128 + row) * 2];
+        den += xch[(w * 128 + row) * 2 + 1];
+      }
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
       c = den > 0.f ? num / den : 0.f;
     }
     if (row_ok && wg == 0) p.corr[si] = c;
@@ -333,11 +350,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < n_tiles && ok; ++t) {
       if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
       tc_fence_after();
-      uint32_t pk[32];
+      uint32_t pk[COLS / 2];
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      for (int cc = 0; cc < CPW; ++cc) {
         float sv[32], dv[32];
-        chunk(t, wg * 2 + cc, sv, dv);
+        chunk(t, wg * CPW + cc, sv, dv);
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           float w0, w1, p0, p1;
@@ -352,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t > 0) {
         if (!(ok = wait_warp(&bars->ds_empty, (t - 1) & 1, abort_flag))) break;
       }
-      store_half_sw128(smem + L::DS, wg, row, pk);
+      store_chunks_sw128<COLS / 8>(smem + L::DS, row, wg * (COLS / 8), pk);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ds_full);
@@ -367,8 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     T* dqrow = static_cast<T*>(p.dq) + qrow_off(p, g, b, h, row_ok ? i : 0, p.dq_sb, p.dq_sh, p.dq_st);
 #pragma unroll
-    for (int cc = 0; cc < HD / 64; ++cc) {
-      const int cidx = wg * (HD / 64) + cc;  // warpgroup wg stores half of the head dim
+    for (int cc = 0; cc < 1; ++cc) {
+      const int cidx = wg;  // warpgroup wg stores head-dim columns [32 wg, 32 wg + 32)
       uint32_t r[32];
       if (n_tiles > 0) {
         tmem_ld32(tmem_dq + lane_addr + cidx * 32, r);
@@ -394,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == Roles<HD>::MMA_WARP) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -423,7 +440,7 @@ struct KLayout {
 };
 
 template <int HD, bool BF16, int NORM>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const AttnParams p) {
@@ -473,21 +490,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->qd_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, 256);
-    mbar_init(&bars->pb_full, 256);
+    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS);
+    mbar_init(&bars->pb_full, Roles<HD>::ROW_THREADS);
     mbar_init(&bars->pb_empty, 1);
     mbar_init(&bars->done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
   }
-  if (warp == 9) tmem_alloc(tmem_slot, 512);
+  if (warp == Roles<HD>::MMA_WARP) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dv = tmem + 256, tmem_dk = tmem + 256 + HD;
 
-  if (warp == 8) {
+  if (warp == Roles<HD>::TMA_WARP) {
     if (lane == 0 && n_units > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
@@ -515,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == Roles<HD>::MMA_WARP) {
     if (lane == 0 && n_units > 0) {
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
@@ -571,7 +588,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int wg = warp >> 2;          // warpgroup wg owns query columns [64 wg, 64 wg + 64)
+    constexpr int NWG = Roles<HD>::NWG;
+    constexpr int COLS = kBM / NWG;  // query columns per warpgroup
+    constexpr int CPW = COLS / 32;
+    const int wg = warp >> 2;         // warpgroup wg owns query columns [COLS wg, COLS (wg + 1))
     const int row = threadIdx.x & 127;  // key within the tile
     const int j = k0 + row;
     const bool key_ok = j < g.k_len;
@@ -586,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m_lo + u % n_m;
       const int qbase = m * kBM;
       // stage the statistics of this tile's 128 query rows
-      named_bar_sync(1, 256);
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
       if (wg == 0) {
         const int iq = qbase + row;
         float a = kPosInf, bb = 1.f, cc = 0.f;
@@ -601,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / bb : 1.f;
         crs[row] = cc;
       }
-      named_bar_sync(1, 256);
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
       if (!ok) continue;
       if (!(ok = wait_warp(&bars->sdp_full, u & 1, abort_flag))) continue;
       tc_fence_after();
@@ -610,10 +630,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int c_lo = p.causal ? jl - qbase : -1 << 30;
       int c_hi = key_ok ? g.q_len - qbase : -(1 << 30);
       if (p.window_left > 0) c_hi = min(c_hi, jl + p.window_left - qbase);
-      uint32_t ppk[32], dpk[32];
+      uint32_t ppk[COLS / 2], dpk[COLS / 2];
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int cidx = wg * 2 + cc;
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int cidx = wg * CPW + cc;
         uint32_t rs[32], rd[32];
         tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
         tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
@@ -642,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (pbc > 0) {
           if (!(ok = wait_warp(&bars->pb_empty, (pbc - 1) & 1, abort_flag))) break;
         }
-        store_half_sw128(smem + L::PB, wg, row, which == 0 ? ppk : dpk);
+        store_chunks_sw128<COLS / 8>(smem + L::PB, row, wg * (COLS / 8), which == 0 ? ppk : dpk);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&bars->pb_full);
@@ -661,13 +681,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t boff = varlen ? 0 : (int64_t)b;
     T* dkrow = static_cast<T*>(p.dk) + boff * p.dk_sb + (int64_t)kvh * p.dk_sh + kt * p.dk_st;
     T* dvrow = static_cast<T*>(p.dv) + boff * p.dv_sb + (int64_t)kvh * p.dv_sh + kt * p.dv_st;
-    {
-      const int which = wg;  // warpgroup 0 stores dV, warpgroup 1 stores dK
+    // dV (columns 0..HD-1) then dK (HD..2HD-1): 2 HD / 32 chunks, two per warpgroup
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int chunk_id = wg * 2 + q;
+      const int which = chunk_id / (HD / 32);
+      const int cidx = chunk_id % (HD / 32);
       const uint32_t src = which == 0 ? tmem_dv : tmem_dk;
       const float f = which == 0 ? 1.f : p.scale;
       T* dst = which == 0 ? dvrow : dkrow;
-#pragma unroll
-      for (int cidx = 0; cidx < HD / 32; ++cidx) {
+      {
         uint32_t r[32];
         if (n_units > 0) {
           tmem_ld32(src + lane_addr + cidx * 32, r);
@@ -694,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == Roles<HD>::MMA_WARP) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -703,11 +726,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // =========================================================== host
 template <typename K>
-cudaError_t launch_k(K kernel, dim3 grid, size_t smem, cudaStream_t s, const CUtensorMap& a,
+cudaError_t launch_k(K kernel, dim3 grid, int threads, size_t smem, cudaStream_t s, const CUtensorMap& a,
                      const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d, const AttnParams& p) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kernel<<<grid, kThreads, smem, s>>>(a, b, c, d, p);
+  kernel<<<grid, threads, smem, s>>>(a, b, c, d, p);
   return cudaGetLastError();
 }
 
@@ -724,10 +747,10 @@ cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t
       !make_map(&mv, p.v, BF16, HD, tk, p.hkv, batch, p.v_st, p.v_sh, varlen ? tk * p.v_st : p.v_sb))
     return cudaErrorInvalidValue;
   cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
-                           QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+                           Roles<HD>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
   if (e != cudaSuccess) return e;
   return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
-                  KLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+                  Roles<HD>::THREADS, KLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
 }
 
 template <int HD, bool BF16>

@@ -53,6 +53,30 @@ __device__ __forceinline__ void store_half_sw128(uint8_t* base, int hh, int row,
   }
 }
 
+// NCH consecutive 16-byte chunks (8 columns each), starting at chunk c0 of a
+// 16-chunk (128-column) row, from packed pairs pk[4 * NCH].
+template <int NCH>
+__device__ __forceinline__ void store_chunks_sw128(uint8_t* base, int row, int c0, const uint32_t* pk) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int chunk = c0 + c, hh = chunk >> 3, cc = chunk & 7;
+    uint4 v = make_uint4(pk[c * 4 + 0], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
+    *reinterpret_cast<uint4*>(base + hh * kHalf + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+  }
+}
+
+// Warp roles of the tensor-core kernels: HD / 32 row warpgroups (warpgroup wg
+// owns 128 / NWG columns of each 128 x 128 tile and 32 head-dim columns),
+// then one TMA warp and one MMA warp.
+template <int HD>
+struct Roles {
+  static constexpr int NWG = HD / 32;
+  static constexpr int ROW_THREADS = 128 * NWG;
+  static constexpr int TMA_WARP = 4 * NWG;
+  static constexpr int MMA_WARP = 4 * NWG + 1;
+  static constexpr int THREADS = 32 * (4 * NWG + 2);
+};
+
 // ------------------------------------------------------------------ host
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
