@@ -231,8 +231,13 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return None
     burst, sustained, hbm, peak_kind = peaks()
+    # Dominant single launch: the entmax15 forward (tc_fwd_kernel).  Its DRAM
+    # traffic comes from the ncu capture summarised in
+    # profiles/tc_kernels_qwen3_8b_small_case.md (25.24 MB read on a case with
+    # 1/16 of the (batch x head) units, scaled by 16).
     dom = phases["entmax15"]
-    achieved = 2.5 * flops_rank / dom["bwd_ms"] / 1e9
+    achieved = flops_rank / dom["fwd_ms"] / 1e9
+    traffic = 25.24e6 * 16 * (world and 1) if (B, S, HQ, HKV) == (4, 8192, 32, 8) and world == 1 else None
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -251,10 +256,10 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"kv-head groups sharded over {world} GPU(s)",
                    "l2": "inputs (~670 MB) exceed L2; no flush"},
         "phases": phases,
-        "roofline": {"kernel": "attention backward (entmax15: dq + dk/dv launches)", "bound": "tensor",
-                     "achieved": round(achieved, 1), "peak": sustained, "unit": "TFLOP/s",
-                     "frac": round(achieved / sustained, 3),
-                     "peak_kind": f"{peak_kind} bf16 sustained", "traffic": None},
+        "roofline": {"kernel": "tc_fwd_kernel<128,bf16,entmax15> (entmax15 forward, one launch)",
+                     "bound": "tensor", "achieved": round(achieved, 1), "peak": sustained, "unit": "TFLOP/s",
+                     "frac": round(achieved / sustained, 3), "peak_kind": f"{peak_kind} bf16 sustained",
+                     "traffic": traffic, "traffic_unit": "bytes per launch (ncu, small case x16)"},
         "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "path": "kernels.hopper_{sparsemax,entmax15}_attention + autograd, pinned host inputs"},
