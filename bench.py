@@ -237,7 +237,7 @@ def run_ours(args, rank, world, local_rank):
     # 1/16 of the (batch x head) units, scaled by 16).
     dom = phases["entmax15"]
     achieved = flops_rank / dom["fwd_ms"] / 1e9
-    traffic = 25.24e6 * 16 * (world and 1) if (B, S, HQ, HKV) == (4, 8192, 32, 8) and world == 1 else None
+    traffic = 25.24e6 * 16 if (B, S, HQ, HKV) == (4, 8192, 32, 8) and world == 1 else None
     line = {
         "metric": METRIC,
         "value": round(value, 1),

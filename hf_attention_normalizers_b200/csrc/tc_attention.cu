@@ -68,8 +68,8 @@ struct Layout {
   static constexpr uint32_t P = V + kStages * NH * kHalf;
   static constexpr uint32_t BARS = P + 2 * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(Bars);
-  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;  // warpgroup exchange, 16 KB
-  static constexpr uint32_t TOTAL = XCH + 16384 + 1024;               // + alignment slack
+  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;  // warpgroup exchange, 32 KB
+  static constexpr uint32_t TOTAL = XCH + 32768 + 1024;               // + alignment slack
 };
 
 __device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
@@ -113,16 +113,16 @@ __device__ float buffer_solve(const float* buf, int row, int n, float t0, int ma
   return t;
 }
 
-// Lower bound of tau from the four largest chunk maxima z1 >= z2 >= z3 >= z4
+// Lower bound of tau from the KT largest chunk maxima zz[0] >= ... >= zz[KT-1]
 // (z units, -inf when missing): any k distinct scores whose closed-form
 // threshold t_k lies at or below the smallest of them give f(t_k) >= 1,
 // hence t_k <= tau.  k = 1 is the zmax - 1 bound.
-template <int NORM>
-__device__ __forceinline__ float top4_bound(float z1, float z2, float z3, float z4) {
-  const float zz[4] = {z1, z2, z3, z4};
+template <int NORM, int KT>
+__device__ __forceinline__ float top_bound(const float (&zz)[KT]) {
+  const float z1 = zz[0];
   float best = z1 - 1.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll
-  for (int k = 1; k <= 4; ++k) {
+  for (int k = 1; k <= KT; ++k) {
     const float y = zz[k - 1] - z1;
     if (!(zz[k - 1] > kNegInf)) break;
     s1 += y;
@@ -414,10 +414,13 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     if (SCAN) {
       Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
-      float t1 = kNegInf, t2 = kNegInf, t3 = kNegInf, t4 = kNegInf;  // top-4 chunk maxima (raw)
+      constexpr int KT = NORM == HFAN_SPARSEMAX ? 4 : 8;  // tracked chunk maxima (entmax15 supports are wider)
+      float tk[KT];  // the KT largest chunk maxima so far (raw scores, descending)
+#pragma unroll
+      for (int k = 0; k < KT; ++k) tk[k] = kNegInf;
       // Every warpgroup's bound is a lower bound of the row's tau, so they
       // publish it and adopt the largest (a stale read is still a valid bound).
-      volatile float* xb = xch + 3072;  // [NWG][128]
+      volatile float* xb = xch + 6144;  // [NWG][128]
       xb[wg * 128 + row] = kNegInf;
       named_bar_sync(1, NT);
       for (int t = 0; t < n_tiles && ok; ++t) {
@@ -432,15 +435,21 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           for (int e = 1; e < 8; ++e) m8 = fmaxf(m8, sreg[c * 8 + e]);
           cm[c] = m8;
           tm = fmaxf(tm, m8);
-          float x = m8, n1;
-          n1 = fmaxf(t1, x); x = fminf(t1, x); t1 = n1;
-          n1 = fmaxf(t2, x); x = fminf(t2, x); t2 = n1;
-          n1 = fmaxf(t3, x); x = fminf(t3, x); t3 = n1;
-          t4 = fmaxf(t4, x);
+          float x = m8;
+#pragma unroll
+          for (int k = 0; k < KT - 1; ++k) {  // branch-free insertion
+            const float hi_ = fmaxf(tk[k], x);
+            x = fminf(tk[k], x);
+            tk[k] = hi_;
+          }
+          tk[KT - 1] = fmaxf(tk[KT - 1], x);
         }
         zmax = fmaxf(zmax, tm * zs);
         {
-          float lb = t1 > kNegInf ? top4_bound<NORM>(t1 * zs, t2 * zs, t3 * zs, t4 * zs) : kNegInf;
+          float zk[KT];
+#pragma unroll
+          for (int k = 0; k < KT; ++k) zk[k] = tk[k] * zs;
+          float lb = tk[0] > kNegInf ? top_bound<NORM, KT>(zk) : kNegInf;
 #pragma unroll
           for (int w = 0; w < NWG; ++w) lb = fmaxf(lb, xb[w * 128 + row]);
           if (lb > cd.thr) {
@@ -472,51 +481,65 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         }
         xb[wg * 128 + row] = cd.thr;
       }
-      // merge the warpgroups: warpgroup 0 solves tau on all buffers of the row
+      // merge the warpgroups: row max, best lower bound, overflow
       float* xs = xch;  // [NWG][128 rows][4]
       xs[(wg * 128 + row) * 4 + 0] = zmax;
       xs[(wg * 128 + row) * 4 + 1] = cd.thr;
       xs[(wg * 128 + row) * 4 + 2] = cd.overflow ? 1.f : 0.f;
-      xs[(wg * 128 + row) * 4 + 3] = __int_as_float(cd.n);
       named_bar_sync(1, NT);
-      float* bc = xch + NWG * 512;  // [128 rows][4]: tau, support, pending, lower
-      if (wg == 0) {
-        float zrow = kNegInf, lower = kNegInf;
-        bool ovf = false;
-        int ns[NWG];
+      float zrow = kNegInf, lower = kNegInf;
+      bool ovf = false;
 #pragma unroll
-        for (int w = 0; w < NWG; ++w) {
-          const float* o = xs + (w * 128 + row) * 4;
-          zrow = fmaxf(zrow, o[0]);
-          lower = fmaxf(lower, o[1]);
-          ovf |= o[2] != 0.f;
-          ns[w] = __float_as_int(o[3]);
-        }
-        bool pending = false;
-        if (!(zrow > kNegInf)) {
-          tau = kPosInf;  // no visible key: zero row
-        } else if (!ovf) {
-          bool exact;
-          const float r = buffer_solve_multi<NORM, NWG>(cbuf0, CAPW, row, ns, lower, 64, &exact, &support);
-          if (exact) {
-            tau = r;
-          } else {
-            pending = true;
-            lower = r;
-          }
-        } else {
-          pending = true;
-        }
-        bc[row * 4 + 0] = tau;
-        bc[row * 4 + 1] = support;
-        bc[row * 4 + 2] = pending ? 1.f : 0.f;
-        bc[row * 4 + 3] = lower;
+      for (int w = 0; w < NWG; ++w) {
+        const float* o = xs + (w * 128 + row) * 4;
+        zrow = fmaxf(zrow, o[0]);
+        lower = fmaxf(lower, o[1]);
+        ovf |= o[2] != 0.f;
       }
       named_bar_sync(1, NT);
-      tau = bc[row * 4 + 0];
-      support = bc[row * 4 + 1];
-      bool pending = bc[row * 4 + 2] != 0.f;
-      float lower = bc[row * 4 + 3];
+      // Exact tau on the union of the row's buffers: every warpgroup sums its
+      // own buffer, the sums are exchanged (double-buffered by iteration
+      // parity) and all warpgroups take the same step.  bar.red.or both
+      // synchronises and tells whether any row is still iterating.
+      const bool empty = !(zrow > kNegInf);
+      bool pending = !empty && ovf;  // overflowing rows go to whole-row sweeps
+      bool done = empty || ovf;
+      float tsol = lower;
+      for (int it = 0;; ++it) {
+        TauStats st{0.f, 0.f, 0.f, kPosInf};
+        if (!done)
+          for (int e = 0; e < cd.n; ++e) tau_accumulate(st, cbuf[e * 128 + row], tsol);
+        float* xi = xch + 2048 + (it & 1) * (NWG * 512);  // [2][NWG][128][4]
+        xi[(wg * 128 + row) * 4 + 0] = st.cnt;
+        xi[(wg * 128 + row) * 4 + 1] = st.s1;
+        xi[(wg * 128 + row) * 4 + 2] = st.s2;
+        xi[(wg * 128 + row) * 4 + 3] = st.zmin;
+        const bool any = named_bar_or(1, NT, !done);
+        if (!any) break;
+        if (done) continue;
+        TauStats all{0.f, 0.f, 0.f, kPosInf};
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          const float* o = xi + (w * 128 + row) * 4;
+          all.cnt += o[0];
+          all.s1 += o[1];
+          all.s2 += o[2];
+          all.zmin = fminf(all.zmin, o[3]);
+        }
+        support = all.cnt;
+        if (all.cnt == 0.f || it >= 63) {  // cannot happen with a valid bound; sweep the row instead
+          done = true;
+          pending = true;
+          lower = tsol;
+        } else if (tau_step(NORM, all, &tsol, &tau)) {
+          done = true;
+        }
+      }
+      if (empty) tau = kPosInf;  // no visible key: zero row
+      if (pending) {
+        tau = kPosInf;
+        lower = fmaxf(lower, tsol);
+      }
       for (int sweep = 0;; ++sweep) {
         // CTA-wide decision (uniform across the row threads): another
         // bracket sweep, or the final pass.
