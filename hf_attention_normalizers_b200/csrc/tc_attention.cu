@@ -31,6 +31,20 @@
 #include "tc_ptx.cuh"
 #include "tc_common.cuh"
 
+#ifdef HFAN_DIAG
+__device__ unsigned long long g_hfan_diag[8];
+extern "C" int hfan_diag_read(unsigned long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 8);
+}
+extern "C" int hfan_diag_clear() {
+  unsigned long long z[8] = {0};
+  return (int)cudaMemcpyToSymbol(g_hfan_diag, z, sizeof(z));
+}
+#define DIAG_ADD(i, v) atomicAdd(&g_hfan_diag[i], (unsigned long long)(v))
+#else
+#define DIAG_ADD(i, v) ((void)0)
+#endif
+
 namespace hfan {
 namespace {
 
@@ -165,6 +179,7 @@ __device__ float buffer_solve_multi(const float* buf0, int capw, int row, const 
 // passed by value so that callers keep it in registers.
 template <int NORM>
 __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap, float zs) {
+  DIAG_ADD(0, 1);
   bool exact;
   float sup;
   float root = buffer_solve<NORM>(buf, row, c.n, c.thr, 8, &exact, &sup);
@@ -194,6 +209,9 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
   constexpr uint32_t IDESC_QK = idesc_f16(BF16, kBM, kBN, false, false);
   constexpr uint32_t IDESC_PV = idesc_f16(BF16, kBM, HD, false, true);
   constexpr bool SPARSE = NORM != HFAN_SOFTMAX1;
+#ifndef HFAN_VOTE_PERIOD
+#define HFAN_VOTE_PERIOD 4
+#endif
 #ifndef HFAN_EXP
 #define HFAN_EXP 0
 #endif
@@ -411,6 +429,48 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
 
     // ---- threshold (sparse normalizers)
     float tau = kPosInf, support = 0.f;
+    // Threshold of the union of this row's candidate buffers, starting from
+    // the lower bound t0: every warpgroup sums its own buffer, the sums are
+    // exchanged (double-buffered by iteration parity) and all warpgroups take
+    // the same step; bar.red.or both synchronises and tells whether any row is
+    // still iterating.  Every row thread must call it.  Returns true with the
+    // exact root of the union in *out, or false with a lower bound of it.
+    auto union_solve = [&](const Cand& cdr, float t0, bool active, int max_iter, float* out, float* sup) -> bool {
+      bool done = !active, exact = false;
+      float tsol = t0;
+      for (int it = 0;; ++it) {
+        TauStats st{0.f, 0.f, 0.f, kPosInf};
+        if (!done)
+          for (int e = 0; e < cdr.n; ++e) tau_accumulate(st, cbuf[e * 128 + row], tsol);
+        float* xi = xch + 2048 + (it & 1) * (NWG * 512);  // [2][NWG][128][4]
+        xi[(wg * 128 + row) * 4 + 0] = st.cnt;
+        xi[(wg * 128 + row) * 4 + 1] = st.s1;
+        xi[(wg * 128 + row) * 4 + 2] = st.s2;
+        xi[(wg * 128 + row) * 4 + 3] = st.zmin;
+        if (!named_bar_or(1, NT, !done)) break;
+        if (done) continue;
+        TauStats all{0.f, 0.f, 0.f, kPosInf};
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          const float* o = xi + (w * 128 + row) * 4;
+          all.cnt += o[0];
+          all.s1 += o[1];
+          all.s2 += o[2];
+          all.zmin = fminf(all.zmin, o[3]);
+        }
+        *sup = all.cnt;
+        float r;
+        if (all.cnt == 0.f || it >= max_iter - 1) {
+          done = true;
+        } else if (tau_step(NORM, all, &tsol, &r)) {
+          done = true;
+          exact = true;
+          tsol = r;
+        }
+      }
+      *out = tsol;
+      return exact;
+    };
     if (SCAN) {
       Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
@@ -423,8 +483,12 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       volatile float* xb = xch + 6144;  // [NWG][128]
       xb[wg * 128 + row] = kNegInf;
       named_bar_sync(1, NT);
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        if (!(ok = load_s(t))) break;
+      // Every row thread runs all n_tiles iterations, also after a timed-out
+      // wait (ok == false, work skipped), so the periodic votes below never
+      // strand a warpgroup at its barrier.
+      for (int t = 0; t < n_tiles; ++t) {
+        if (ok) ok = load_s(t);
+        if (ok) {
         // chunk maxima (8 keys each) gate the candidate appends
         float cm[COLS / 8];
         float tm = kNegInf;
@@ -475,11 +539,40 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
             }
           }
         }
-        // warp-uniform compaction once a lane nears capacity (lanes over half full join)
-        if (__any_sync(0xffffffffu, cd.n > CAPW - 12 && !cd.overflow)) {
-          if (cd.n > CAPW / 2 && !cd.overflow) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
-        }
+        // Cooperative compaction once any buffer nears capacity: the threshold
+        // of all candidates of the row so far (a lower bound of tau, and a far
+        // tighter one than a single warpgroup's) becomes every warpgroup's
+        // admission bound, and dead entries are dropped.
+        }  // ok
+        // The vote runs every fourth tile and after the last (CTA-uniform);
+        // the per-warpgroup compaction above guards the tiles in between.
+        // The bound is published before the vote, so that every warpgroup
+        // starts the union solve from the same t0.
         xb[wg * 128 + row] = cd.thr;
+        // (Sparsemax supports stay far below the capacity: no vote.)
+        if (NORM != HFAN_ENTMAX15) continue;
+        if ((t % HFAN_VOTE_PERIOD) != HFAN_VOTE_PERIOD - 1 && t != n_tiles - 1) continue;
+        if (named_bar_or(1, NT, ok && cd.n > CAPW - 20 && !cd.overflow)) {
+          float t0 = cd.thr;
+#pragma unroll
+          for (int w = 0; w < NWG; ++w) t0 = fmaxf(t0, xb[w * 128 + row]);
+          float r, sup;
+          union_solve(cd, t0, ok && zmax > kNegInf, 16, &r, &sup);
+          if (r > cd.thr) {
+            cd.thr = r;
+            cd.thr_s = r / zs;
+          }
+          if (!cd.overflow) {
+            int live = 0;
+            for (int e = 0; e < cd.n; ++e) {
+              const float z = cbuf[e * 128 + row];
+              if (z > cd.thr) cbuf[live++ * 128 + row] = z;
+            }
+            cd.n = live;
+            if (live > CAPW - 12) cd.overflow = true;
+          }
+          xb[wg * 128 + row] = cd.thr;
+        }
       }
       // merge the warpgroups: row max, best lower bound, overflow
       float* xs = xch;  // [NWG][128 rows][4]
@@ -497,43 +590,14 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         ovf |= o[2] != 0.f;
       }
       named_bar_sync(1, NT);
-      // Exact tau on the union of the row's buffers: every warpgroup sums its
-      // own buffer, the sums are exchanged (double-buffered by iteration
-      // parity) and all warpgroups take the same step.  bar.red.or both
-      // synchronises and tells whether any row is still iterating.
+      // Exact tau on the union of the row's buffers.
       const bool empty = !(zrow > kNegInf);
       bool pending = !empty && ovf;  // overflowing rows go to whole-row sweeps
-      bool done = empty || ovf;
       float tsol = lower;
-      for (int it = 0;; ++it) {
-        TauStats st{0.f, 0.f, 0.f, kPosInf};
-        if (!done)
-          for (int e = 0; e < cd.n; ++e) tau_accumulate(st, cbuf[e * 128 + row], tsol);
-        float* xi = xch + 2048 + (it & 1) * (NWG * 512);  // [2][NWG][128][4]
-        xi[(wg * 128 + row) * 4 + 0] = st.cnt;
-        xi[(wg * 128 + row) * 4 + 1] = st.s1;
-        xi[(wg * 128 + row) * 4 + 2] = st.s2;
-        xi[(wg * 128 + row) * 4 + 3] = st.zmin;
-        const bool any = named_bar_or(1, NT, !done);
-        if (!any) break;
-        if (done) continue;
-        TauStats all{0.f, 0.f, 0.f, kPosInf};
-#pragma unroll
-        for (int w = 0; w < NWG; ++w) {
-          const float* o = xi + (w * 128 + row) * 4;
-          all.cnt += o[0];
-          all.s1 += o[1];
-          all.s2 += o[2];
-          all.zmin = fminf(all.zmin, o[3]);
-        }
-        support = all.cnt;
-        if (all.cnt == 0.f || it >= 63) {  // cannot happen with a valid bound; sweep the row instead
-          done = true;
-          pending = true;
-          lower = tsol;
-        } else if (tau_step(NORM, all, &tsol, &tau)) {
-          done = true;
-        }
+      if (union_solve(cd, lower, !empty && !ovf, 64, &tsol, &support)) {
+        tau = tsol;
+      } else if (!empty && !ovf) {
+        pending = true;  // did not converge: sweep the row
       }
       if (empty) tau = kPosInf;  // no visible key: zero row
       if (pending) {
@@ -556,6 +620,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         }
         named_bar_sync(1, NT);
         if (ctl->next_pass != kPassSweep) break;
+        if (threadIdx.x == 0) DIAG_ADD(3, 1);
         TauStats st{0.f, 0.f, 0.f, kPosInf};
         for (int t = 0; t < n_tiles && ok; ++t) {
           if (!(ok = load_s(t))) break;
