@@ -32,17 +32,24 @@
 #include "tc_common.cuh"
 
 #ifdef HFAN_DIAG
-__device__ unsigned long long g_hfan_diag[8];
+__device__ unsigned long long g_hfan_diag[16];
 extern "C" int hfan_diag_read(unsigned long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 8);
+  return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 16);
 }
 extern "C" int hfan_diag_clear() {
-  unsigned long long z[8] = {0};
+  unsigned long long z[16] = {0};
   return (int)cudaMemcpyToSymbol(g_hfan_diag, z, sizeof(z));
 }
 #define DIAG_ADD(i, v) atomicAdd(&g_hfan_diag[i], (unsigned long long)(v))
+#define DIAG_T(acc, stmt)               \
+  do {                                  \
+    const long long t0_ = clock64();    \
+    stmt;                               \
+    acc += clock64() - t0_;             \
+  } while (0)
 #else
 #define DIAG_ADD(i, v) ((void)0)
+#define DIAG_T(acc, stmt) stmt
 #endif
 
 namespace hfan {
@@ -52,7 +59,14 @@ using namespace tc;
 
 constexpr int kBM = 128;           // query rows per CTA
 constexpr int kBN = 128;           // keys per tile
-constexpr int kStages = 2;         // K and V ring depth
+// K/V tiles share one ring of 128-row stages.  The scan and sweep passes
+// (K only) cycle through the first kScanStages; the stages after them hold
+// the candidate buffers meanwhile.  The final pass cycles through all of them,
+// loading in the order the MMA warp consumes: K0 K1 V0 K2 V1 ... V(n-1).
+template <int HD>
+constexpr int ring_stages() { return HD == 128 ? 5 : 8; }
+constexpr int kScanStages = 2;
+constexpr int kMaxStages = 8;
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
 constexpr float kRescaleLog2 = 8.f;
 
@@ -60,10 +74,9 @@ enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[kStages], k_empty[kStages];
-  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t full[kMaxStages], empty[kMaxStages];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done, ctrl;
+  uint64_t p_full[2], pv_done[2], ctrl;
 };
 
 struct Ctl {
@@ -77,13 +90,15 @@ template <int HD>
 struct Layout {
   static constexpr int NH = HD / 64;
   static constexpr uint32_t Q = 0;
-  static constexpr uint32_t K = Q + NH * kHalf;
-  static constexpr uint32_t V = K + kStages * NH * kHalf;
-  static constexpr uint32_t P = V + kStages * NH * kHalf;
-  static constexpr uint32_t BARS = P + 2 * kHalf;
+  static constexpr int NS = ring_stages<HD>();
+  static constexpr uint32_t RING = Q + NH * kHalf;
+  static constexpr uint32_t CAND = RING + kScanStages * NH * kHalf;  // candidate buffers (scan/sweeps)
+  static constexpr uint32_t CAND_BYTES = (NS - kScanStages) * NH * kHalf;
+  static constexpr uint32_t BARS = RING + NS * NH * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(Bars);
-  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;  // warpgroup exchange, 32 KB
-  static constexpr uint32_t TOTAL = XCH + 32768 + 1024;               // + alignment slack
+  static constexpr uint32_t XCH_FLOATS = 6144 + 4 * 128;             // warpgroup exchange
+  static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;
+  static constexpr uint32_t TOTAL = XCH + XCH_FLOATS * 4 + 1024;      // + alignment slack
 };
 
 __device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
@@ -133,24 +148,45 @@ __device__ float buffer_solve(const float* buf, int row, int n, float t0, int ma
 // hence t_k <= tau.  k = 1 is the zmax - 1 bound.
 template <int NORM, int KT>
 __device__ __forceinline__ float top_bound(const float (&zz)[KT]) {
+  // The sizes k whose closed-form threshold t_k stays at or below the k-th
+  // value form a prefix, and the largest one gives the set's threshold; the
+  // test needs no root or division (1/k is a constant of the unrolled loop),
+  // so a single closed form is evaluated at the end.
   const float z1 = zz[0];
-  float best = z1 - 1.f, s1 = 0.f, s2 = 0.f;
+  float s1 = 0.f, s2 = 0.f, b1 = 0.f, b2 = 0.f;
+  int kb = 0;
 #pragma unroll
   for (int k = 1; k <= KT; ++k) {
     const float y = zz[k - 1] - z1;
-    if (!(zz[k - 1] > kNegInf)) break;
     s1 += y;
     s2 += y * y;
-    float t;
+    const float inv = 1.f / float(k);
+    bool valid;
     if (NORM == HFAN_SPARSEMAX) {
-      t = (s1 - 1.f) / k;
+      valid = (s1 - 1.f) * inv <= y;
     } else {
-      const float mean = s1 / k;
-      t = mean - sqrtf(fmaxf((1.f - (s2 - s1 * mean)) / k, 0.f));
+      const float mean = s1 * inv;
+      const float d = (1.f - (s2 - s1 * mean)) * inv;  // t_k = mean - sqrt(d)
+      const float g = mean - y;                          // t_k <= y  <=>  g <= sqrt(d)
+      valid = g <= 0.f || (d >= 0.f && g * g <= d);
     }
-    if (t <= y) best = fmaxf(best, z1 + t);
+    valid = valid && zz[k - 1] > kNegInf;
+    if (valid) {
+      kb = k;
+      b1 = s1;
+      b2 = s2;
+    }
   }
-  return best;
+  if (kb == 0) return z1 - 1.f;
+  const float inv = 1.f / float(kb);
+  float t;
+  if (NORM == HFAN_SPARSEMAX) {
+    t = (b1 - 1.f) * inv;
+  } else {
+    const float mean = b1 * inv;
+    t = mean - sqrtf(fmaxf((1.f - (b2 - b1 * mean)) * inv, 0.f));
+  }
+  return fmaxf(z1 - 1.f, z1 + t);
 }
 
 // The same solve over the NW per-warpgroup buffers of one row (buffer w holds
@@ -209,13 +245,19 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
   constexpr uint32_t IDESC_QK = idesc_f16(BF16, kBM, kBN, false, false);
   constexpr uint32_t IDESC_PV = idesc_f16(BF16, kBM, HD, false, true);
   constexpr bool SPARSE = NORM != HFAN_SOFTMAX1;
+#ifndef HFAN_KT_ENT
+#define HFAN_KT_ENT 4
+#endif
+#ifndef HFAN_VOTE_ITERS
+#define HFAN_VOTE_ITERS 3
+#endif
 #ifndef HFAN_VOTE_PERIOD
 #define HFAN_VOTE_PERIOD 4
 #endif
 #ifndef HFAN_EXP
 #define HFAN_EXP 0
 #endif
-  constexpr bool SCAN = SPARSE && HFAN_EXP != 2;
+  constexpr bool SCAN = SPARSE && HFAN_EXP != 2 && HFAN_EXP != 5 && HFAN_EXP != 6;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -244,18 +286,18 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->k_full[s], 1);
-      mbar_init(&bars->k_empty[s], 1);
-      mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->v_empty[s], 1);
+    for (int s = 0; s < L::NS; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_empty[s], Roles<HD>::ROW_THREADS);
+      mbar_init(&bars->s_empty[s], Roles<HD>::ROW_THREADS / 32);
     }
-    mbar_init(&bars->p_full, Roles<HD>::ROW_THREADS);
-    mbar_init(&bars->pv_done, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->p_full[s], Roles<HD>::ROW_THREADS / 32);
+      mbar_init(&bars->pv_done[s], 1);
+    }
     mbar_init(&bars->ctrl, 1);
     ctl->abort = 0;
     ctl->next_pass = kPassFinal;
@@ -267,7 +309,8 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const uint32_t tmem_o = tmem + 256;
+  const uint32_t tmem_o = tmem + 256;  // O: HD columns
+  const uint32_t tmem_p = tmem + 384;  // P double buffer: 2 x 64 columns of packed 16-bit pairs
   volatile int* abort_flag = &ctl->abort;
 
   if (warp == Roles<HD>::TMA_WARP) {
@@ -279,30 +322,31 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       mbar_arrive_expect_tx(&bars->q_full, NH * kHalf);
       for (int hh = 0; hh < NH; ++hh)
         tma_load_4d(smem + L::Q + hh * kHalf, &tm_q, &bars->q_full, 64 * hh, qtok, h, bcoord);
-      uint32_t kc = 0, vc = 0, ctrl_phase = 0;
+      // per-stage phase bits: a stage's empty barrier completes once per use
+      uint32_t empty_ph = 0, ctrl_phase = 0;
+      int ring = 0, ns = kScanStages;
+      auto produce = [&](const CUtensorMap* map, int t) -> bool {
+        const int st = ring;
+        ring = ring + 1 == ns ? 0 : ring + 1;
+        if (!mbar_wait(&bars->empty[st], ((empty_ph >> st) & 1) ^ 1, abort_flag)) return false;
+        empty_ph ^= 1u << st;
+        mbar_arrive_expect_tx(&bars->full[st], KV_BYTES);
+        for (int hh = 0; hh < NH; ++hh)
+          tma_load_4d(smem + L::RING + st * KV_BYTES + hh * kHalf, map, &bars->full[st], 64 * hh,
+                      ktok0 + k_lo + t * kBN, kvh, bcoord);
+        return true;
+      };
       int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = true;
       while (ok) {
         const bool fin = pass == kPassFinal;
+        ring = 0;
+        ns = fin ? L::NS : kScanStages;
         for (int t = 0; t < n_tiles && ok; ++t) {
-          const int kb = k_lo + t * kBN;
-          const int s = kc % kStages;
-          if (!(ok = mbar_wait(&bars->k_empty[s], ((kc / kStages) & 1) ^ 1, abort_flag))) break;
-          mbar_arrive_expect_tx(&bars->k_full[s], KV_BYTES);
-          for (int hh = 0; hh < NH; ++hh)
-            tma_load_4d(smem + L::K + s * KV_BYTES + hh * kHalf, &tm_k, &bars->k_full[s], 64 * hh,
-                        ktok0 + kb, kvh, bcoord);
-          ++kc;
-          if (fin) {
-            const int vs = vc % kStages;
-            if (!(ok = mbar_wait(&bars->v_empty[vs], ((vc / kStages) & 1) ^ 1, abort_flag))) break;
-            mbar_arrive_expect_tx(&bars->v_full[vs], KV_BYTES);
-            for (int hh = 0; hh < NH; ++hh)
-              tma_load_4d(smem + L::V + vs * KV_BYTES + hh * kHalf, &tm_v, &bars->v_full[vs], 64 * hh,
-                          ktok0 + kb, kvh, bcoord);
-            ++vc;
-          }
+          ok = produce(&tm_k, t);
+          if (ok && fin && t >= 1) ok = produce(&tm_v, t - 1);
         }
+        if (ok && fin && n_tiles > 0) ok = produce(&tm_v, n_tiles - 1);
         if (!ok || fin) break;
         if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
         ctrl_phase ^= 1;
@@ -314,56 +358,92 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q);
-      const uint32_t k_base = smem_u32(smem + L::K);
-      const uint32_t v_base = smem_u32(smem + L::V);
-      const uint32_t p_base = smem_u32(smem + L::P);
-      uint32_t kc = 0, vc = 0, sc = 0, pc = 0, ctrl_phase = 0;
+      const uint32_t ring_base = smem_u32(smem + L::RING);
+      uint32_t full_ph = 0, sc = 0, pc = 0, ctrl_phase = 0;
+      int ring = 0, ns = kScanStages;
+      long long dg_full = 0, dg_sempty = 0, dg_pfull = 0, dg_qk = 0, dg_pv = 0, dg_t0 = 0;
+      auto consume = [&](int* st) -> bool {
+        *st = ring;
+        ring = ring + 1 == ns ? 0 : ring + 1;
+        bool w_;
+        DIAG_T(dg_full, w_ = mbar_wait(&bars->full[*st], (full_ph >> *st) & 1, abort_flag));
+        if (!w_) return false;
+        full_ph ^= 1u << *st;
+        return true;
+      };
       int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = mbar_wait(&bars->q_full, 0, abort_flag);
       auto issue_pv = [&](int t) -> bool {
-        const int vs = vc % kStages;
-        if (!mbar_wait(&bars->v_full[vs], (vc / kStages) & 1, abort_flag)) return false;
-        if (!mbar_wait(&bars->p_full, pc & 1, abort_flag)) return false;
+        int vs;
+        if (!consume(&vs)) return false;
+        const int pb = pc & 1;
+        bool w_;
+        DIAG_T(dg_pfull, w_ = mbar_wait(&bars->p_full[pb], (pc >> 1) & 1, abort_flag));
+        if (!w_) return false;
         tc_fence_after();
+#ifdef HFAN_DIAG
+        const long long dq0 = clock64();
+#endif
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          // A = P [128 x 128 keys], K-major, two 64-key halves; B = V tile,
-          // MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
-          const uint64_t a = sw128_desc(p_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(v_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
-          mma_f16_ss(tmem_o, a, bd, IDESC_PV, t > 0 || kk > 0);
+          // A = P [128 x 128 keys] in TMEM buffer pb (8 columns per 16 keys);
+          // B = V tile, MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
+          const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
+          mma_f16_ts(tmem_o, tmem_p + pb * 64 + kk * 8, bd, IDESC_PV, t > 0 || kk > 0);
         }
-        mma_commit(&bars->v_empty[vs]);
-        mma_commit(&bars->pv_done);
-        ++vc;
+        mma_commit(&bars->empty[vs]);
+        mma_commit(&bars->pv_done[pb]);
+#ifdef HFAN_DIAG
+        dg_pv += clock64() - dq0;
+#endif
         ++pc;
         return true;
       };
       while (ok) {
         const bool fin = pass == kPassFinal;
+        ring = 0;
+        ns = fin ? L::NS : kScanStages;
         for (int t = 0; t < n_tiles && ok; ++t) {
-          const int s = kc % kStages;
+          int ks;
           const int sb = sc & 1;
-          if (!(ok = mbar_wait(&bars->k_full[s], (kc / kStages) & 1, abort_flag))) break;
-          if (!(ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag))) break;
+          if (!(ok = consume(&ks))) break;
+          DIAG_T(dg_sempty, ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag));
+          if (!ok) break;
           tc_fence_after();
+#ifdef HFAN_DIAG
+          const long long dq0 = clock64();
+#endif
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint64_t a = sw128_desc(q_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(k_base + s * KV_BYTES + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(ring_base + ks * KV_BYTES + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
             mma_f16_ss(tmem + sb * 128, a, bd, IDESC_QK, kk > 0);
           }
           mma_commit(&bars->s_full[sb]);
-          mma_commit(&bars->k_empty[s]);
-          ++kc;
+          mma_commit(&bars->empty[ks]);
+#ifdef HFAN_DIAG
+          dg_qk += clock64() - dq0;
+#endif
           ++sc;
           if (fin && t >= 1) ok = issue_pv(t - 1);
         }
         if (!ok) break;
         if (fin) {
-          ok = issue_pv(n_tiles - 1);
+          if (n_tiles > 0) ok = issue_pv(n_tiles - 1);
+#ifdef HFAN_DIAG
+          DIAG_ADD(8, dg_full);
+          DIAG_ADD(9, dg_sempty);
+          DIAG_ADD(10, dg_pfull);
+          DIAG_ADD(11, clock64() - dg_t0);
+          DIAG_ADD(14, dg_qk);
+          DIAG_ADD(15, dg_pv);
+#endif
           break;
         }
+#ifdef HFAN_DIAG
+        dg_full = dg_sempty = dg_pfull = dg_qk = dg_pv = 0;  // count the final pass only
+        dg_t0 = clock64();
+#endif
         if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
         ctrl_phase ^= 1;
         pass = ctl->next_pass;
@@ -395,11 +475,10 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     // During the scan passes the V ring and the P buffer are idle; they hold
     // the candidate buffers (the producer loads V only in the final pass),
     // one slice per warpgroup.
-    constexpr int CAPW = (int)((kStages * NH * kHalf + 2 * kHalf) / (128 * 4)) / NWG;
-    float* cbuf0 = reinterpret_cast<float*>(smem + L::V);
+    constexpr int CAPW = (int)(L::CAND_BYTES / (128 * 4)) / NWG;
+    float* cbuf0 = reinterpret_cast<float*>(smem + L::CAND);
     float* cbuf = cbuf0 + wg * CAPW * 128;
     float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [4096] floats
-    uint8_t* sP = smem + L::P;
 
     uint32_t sc = 0, pc = 0;
     bool ok = true;
@@ -408,12 +487,18 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       const int sb = sc & 1;
       if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
+      if (HFAN_EXP == 6) {
+        tc_fence_before();
+        warp_arrive(&bars->s_empty[sb]);
+        ++sc;
+        return true;
+      }
       uint32_t r[COLS / 32][32];
 #pragma unroll
       for (int c = 0; c < COLS / 32; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + wg * COLS + c * 32, r[c]);
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&bars->s_empty[sb]);
+      warp_arrive(&bars->s_empty[sb]);
       ++sc;
       const int kb = k_lo + t * kBN + wg * COLS;
       const int lo = vis_lo - kb, hi = vis_hi - kb;
@@ -471,10 +556,13 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       *out = tsol;
       return exact;
     };
+#ifdef HFAN_DIAG
+    long long diag_t0 = clock64();
+#endif
     if (SCAN) {
       Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
-      constexpr int KT = NORM == HFAN_SPARSEMAX ? 4 : 8;  // tracked chunk maxima (entmax15 supports are wider)
+      constexpr int KT = NORM == HFAN_SPARSEMAX ? 4 : HFAN_KT_ENT;  // tracked chunk maxima (entmax15 supports are wider)
       float tk[KT];  // the KT largest chunk maxima so far (raw scores, descending)
 #pragma unroll
       for (int k = 0; k < KT; ++k) tk[k] = kNegInf;
@@ -486,17 +574,22 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       // Every row thread runs all n_tiles iterations, also after a timed-out
       // wait (ok == false, work skipped), so the periodic votes below never
       // strand a warpgroup at its barrier.
+#ifdef HFAN_DIAG
+      long long dw = 0, dt = 0, da = 0, dv = 0, dc = clock64(), dn;
+#define DIAG_LAP(acc) (dn = clock64(), acc += dn - dc, dc = dn)
+#else
+#define DIAG_LAP(acc) ((void)0)
+#endif
       for (int t = 0; t < n_tiles; ++t) {
         if (ok) ok = load_s(t);
+        DIAG_LAP(dw);
         if (ok) {
         // chunk maxima (8 keys each) gate the candidate appends
         float cm[COLS / 8];
         float tm = kNegInf;
 #pragma unroll
         for (int c = 0; c < COLS / 8; ++c) {
-          float m8 = sreg[c * 8];
-#pragma unroll
-          for (int e = 1; e < 8; ++e) m8 = fmaxf(m8, sreg[c * 8 + e]);
+          const float m8 = max_n<8>(sreg + c * 8);
           cm[c] = m8;
           tm = fmaxf(tm, m8);
           float x = m8;
@@ -521,6 +614,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
             cd.thr_s = lb / zs;
           }
         }
+        DIAG_LAP(dt);
         if (HFAN_EXP != 1 && !cd.overflow && tm > cd.thr_s) {
 #pragma unroll
           for (int c = 0; c < COLS / 8; ++c) {
@@ -543,6 +637,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         // of all candidates of the row so far (a lower bound of tau, and a far
         // tighter one than a single warpgroup's) becomes every warpgroup's
         // admission bound, and dead entries are dropped.
+        DIAG_LAP(da);
         }  // ok
         // The vote runs every fourth tile and after the last (CTA-uniform);
         // the per-warpgroup compaction above guards the tiles in between.
@@ -557,7 +652,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
 #pragma unroll
           for (int w = 0; w < NWG; ++w) t0 = fmaxf(t0, xb[w * 128 + row]);
           float r, sup;
-          union_solve(cd, t0, ok && zmax > kNegInf, 16, &r, &sup);
+          union_solve(cd, t0, ok && zmax > kNegInf, HFAN_VOTE_ITERS, &r, &sup);
           if (r > cd.thr) {
             cd.thr = r;
             cd.thr_s = r / zs;
@@ -573,7 +668,20 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           }
           xb[wg * 128 + row] = cd.thr;
         }
+        DIAG_LAP(dv);
       }
+#ifdef HFAN_DIAG
+      if (threadIdx.x == 0) {
+        DIAG_ADD(1, dw);
+        DIAG_ADD(2, dt);
+        DIAG_ADD(3, da);
+        DIAG_ADD(4, dv);
+      }
+#endif
+#ifdef HFAN_DIAG
+      if (threadIdx.x == 0) DIAG_ADD(5, clock64() - diag_t0);
+      diag_t0 = clock64();
+#endif
       // merge the warpgroups: row max, best lower bound, overflow
       float* xs = xch;  // [NWG][128 rows][4]
       xs[(wg * 128 + row) * 4 + 0] = zmax;
@@ -606,7 +714,10 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       }
       for (int sweep = 0;; ++sweep) {
         // CTA-wide decision (uniform across the row threads): another
-        // bracket sweep, or the final pass.
+        // bracket sweep, or the final pass.  The candidate buffers were
+        // written through the generic proxy and the final pass's TMA loads
+        // overwrite them: order the two.
+        fence_proxy_async_smem();
         named_bar_sync(1, NT);
         if (threadIdx.x == 0) ctl->any_pending = 0;
         named_bar_sync(1, NT);
@@ -620,7 +731,6 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         }
         named_bar_sync(1, NT);
         if (ctl->next_pass != kPassSweep) break;
-        if (threadIdx.x == 0) DIAG_ADD(3, 1);
         TauStats st{0.f, 0.f, 0.f, kPosInf};
         for (int t = 0; t < n_tiles && ok; ++t) {
           if (!(ok = load_s(t))) break;
@@ -653,21 +763,25 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       }
     }
 
+#ifdef HFAN_DIAG
+    if (threadIdx.x == 0) DIAG_ADD(6, clock64() - diag_t0);
+    diag_t0 = clock64();
+#endif
     // ---- final pass: P and O
     float m_ref = 0.f, l = wg == 0 ? 1.f : 0.f;  // the implicit zero logit counts once
     const float ntau = -tau;
     // softmax1 meets a named barrier on every tile, so after a timeout the loop
     // keeps running (with the work skipped) instead of leaving it.
+#ifdef HFAN_DIAG
+    long long dg_s = 0, dg_pv = 0;
+#endif
     for (int t = 0; t < n_tiles && (ok || !SPARSE); ++t) {
-      if (ok) ok = load_s(t);
+      if (ok) DIAG_T(dg_s, ok = load_s(t));
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
         // log2 units: x = s * scale * log2(e); the row max over all warpgroups
-        float tmax = kNegInf;
-#pragma unroll
-        for (int j = 0; j < COLS; ++j) tmax = fmaxf(tmax, sreg[j]);
-        tmax *= zs;
+        float tmax = max_n<COLS>(sreg) * zs;
         float* xm = xch + (t & 1) * (NWG * 128);  // double-buffered by tile parity: one barrier per tile
         xm[wg * 128 + row] = tmax;
         named_bar_sync(1, NT);
@@ -679,29 +793,35 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           l *= alpha;
           rescale = t > 0;
         }
-        const float nm = -m_ref;
-        float lsum = 0.f;
+        const uint64_t zs2 = f2_pack(zs, zs), nm2 = f2_pack(-m_ref, -m_ref);
+        uint64_t l2 = 0;
 #pragma unroll
-        for (int j = 0; j < COLS; ++j) {
-          float e = exp2f(fmaf(sreg[j], zs, nm));  // exp2(-inf) = 0 for masked keys
-          sreg[j] = e;
-          lsum += e;
+        for (int j = 0; j < COLS; j += 2) {
+          const uint64_t x = ffma2(f2_pack(sreg[j], sreg[j + 1]), zs2, nm2);
+          const float e0 = ex2_ftz(f2_lo(x)), e1 = ex2_ftz(f2_hi(x));  // exp2(-inf) = 0 for masked keys
+          sreg[j] = e0;
+          sreg[j + 1] = e1;
+          l2 = fadd2(l2, f2_pack(e0, e1));
         }
-        l += lsum;
-      } else {
+        l += f2_lo(l2) + f2_hi(l2);
+      } else if (HFAN_EXP != 5 && HFAN_EXP != 6) {
+        const uint64_t zs2 = f2_pack(zs, zs), nt2 = f2_pack(ntau, ntau);
 #pragma unroll
-        for (int j = 0; j < COLS; ++j) {
-          float d = fmaxf(fmaf(sreg[j], zs, ntau), 0.f);
-          sreg[j] = NORM == HFAN_SPARSEMAX ? d : d * d;
+        for (int j = 0; j < COLS; j += 2) {
+          uint64_t d = ffma2(f2_pack(sreg[j], sreg[j + 1]), zs2, nt2);
+          d = f2_pack(fmaxf(f2_lo(d), 0.f), fmaxf(f2_hi(d), 0.f));
+          if (NORM != HFAN_SPARSEMAX) d = fmul2(d, d);
+          sreg[j] = f2_lo(d);
+          sreg[j + 1] = f2_hi(d);
         }
       }
       if (!ok) continue;
-      // P buffer and O are free once the previous P V has completed.
-      if (t > 0) {
-        if (!(ok = wait_warp(&bars->pv_done, (pc - 1) & 1, abort_flag))) continue;
-        tc_fence_after();
-      }
+      // O may be rescaled once every earlier P V has completed; P buffer pb
+      // is free once the P V two tiles back (its last reader) has.
+      const int pb = pc & 1;
       if (__any_sync(0xffffffffu, rescale)) {
+        if (!(ok = wait_warp(&bars->pv_done[(pc - 1) & 1], ((pc - 1) >> 1) & 1, abort_flag))) continue;
+        tc_fence_after();
         // warp-collective: lanes without a rescale multiply by one
         const float f = rescale ? alpha : 1.f;
         uint32_t r[32];
@@ -712,27 +832,36 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         tmem_st32(tmem_o + lane_addr + wg * 32, r);
         tmem_wait_st();
       }
-      // this warpgroup's COLS columns of the P row -> 128-byte swizzled smem
-#pragma unroll
-      for (int c = 0; c < COLS / 8; ++c) {
-        const int chunk = wg * (COLS / 8) + c;  // 16-byte chunk index within the 128-column row
-        const int hh = chunk >> 3, cc = chunk & 7;
-        uint4 v;
-        v.x = pack2<BF16>(sreg[c * 8 + 0], sreg[c * 8 + 1]);
-        v.y = pack2<BF16>(sreg[c * 8 + 2], sreg[c * 8 + 3]);
-        v.z = pack2<BF16>(sreg[c * 8 + 4], sreg[c * 8 + 5]);
-        v.w = pack2<BF16>(sreg[c * 8 + 6], sreg[c * 8 + 7]);
-        *reinterpret_cast<uint4*>(sP + hh * kHalf + row * 128 + ((cc ^ (row & 7)) << 4)) = v;
+      if (pc >= 2) {
+        DIAG_T(dg_pv, ok = wait_warp(&bars->pv_done[pb], ((pc >> 1) & 1) ^ 1, abort_flag));
+        if (!ok) continue;
+        tc_fence_after();
       }
-      fence_proxy_async_smem();
+      // this warpgroup's COLS keys of the P row -> TMEM columns
+      // [COLS/2 wg, COLS/2 (wg + 1)) of buffer pb, packed in key order
+#pragma unroll
+      for (int c = 0; c < COLS / 32 && HFAN_EXP != 6; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
+        tmem_st16(tmem_p + lane_addr + pb * 64 + wg * (COLS / 2) + c * 16, pk);
+      }
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->p_full);
+      warp_arrive(&bars->p_full[pb]);
       ++pc;
     }
     if (ok && n_tiles > 0) {
-      ok = wait_warp(&bars->pv_done, (pc - 1) & 1, abort_flag);
+      ok = wait_warp(&bars->pv_done[(pc - 1) & 1], ((pc - 1) >> 1) & 1, abort_flag);
       tc_fence_after();
     }
+#ifdef HFAN_DIAG
+    if (threadIdx.x == 0) {
+      DIAG_ADD(7, clock64() - diag_t0);
+      DIAG_ADD(12, dg_s);
+      DIAG_ADD(13, dg_pv);
+    }
+#endif
     if (!ok) record_error(p, ctl, kDevWaitTimeout);
     if (!SPARSE) {
       // total denominator of the row

@@ -128,8 +128,8 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS);
-    mbar_init(&bars->ds_full, Roles<HD>::ROW_THREADS);
+    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS / 32);
+    mbar_init(&bars->ds_full, Roles<HD>::ROW_THREADS / 32);
     mbar_init(&bars->ds_empty, 1);
     mbar_init(&bars->dq_done, 1);
     *abort_ptr = 0;
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&bars->sdp_empty);
+        warp_arrive(&bars->sdp_empty);
         ++sdc;
       }
       // combine the warpgroups' column sums (the dS buffer is idle until pass B)
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars->sdp_empty);
+      warp_arrive(&bars->sdp_empty);
       ++sdc;
       if (t > 0) {
         if (!(ok = wait_warp(&bars->ds_empty, (t - 1) & 1, abort_flag))) break;
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       store_chunks_sw128<COLS / 8>(smem + L::DS, row, wg * (COLS / 8), pk);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->ds_full);
+      warp_arrive(&bars->ds_full);
     }
     if (ok && n_tiles > 0) {
       ok = wait_warp(&bars->dq_done, 0, abort_flag);
@@ -490,8 +490,8 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       mbar_init(&bars->qd_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS);
-    mbar_init(&bars->pb_full, Roles<HD>::ROW_THREADS);
+    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS / 32);
+    mbar_init(&bars->pb_full, Roles<HD>::ROW_THREADS / 32);
     mbar_init(&bars->pb_empty, 1);
     mbar_init(&bars->done, 1);
     *abort_ptr = 0;
@@ -656,7 +656,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars->sdp_empty);
+      warp_arrive(&bars->sdp_empty);
       // P^T, then dS^T, through the shared buffer
       for (int which = 0; which < 2 && ok; ++which) {
         if (pbc > 0) {
@@ -665,7 +665,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         store_chunks_sw128<COLS / 8>(smem + L::PB, row, wg * (COLS / 8), which == 0 ? ppk : dpk);
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(&bars->pb_full);
+        warp_arrive(&bars->pb_full);
         ++pbc;
       }
     }

@@ -21,6 +21,65 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
+// Arrival of a whole warp on a barrier initialised with one count per warp:
+// every lane has finished (and fenced) its own accesses before the call, the
+// warp converges, and lane 0 arrives.  Row-to-MMA barriers count warps, not
+// threads, so that their completion is not serialised behind hundreds of
+// shared-memory arrivals.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+// ---- per-element arithmetic of the row warps (their issue slots bound the
+// kernels): three-input max, packed f32x2 FMA/MUL/ADD, and the hardware
+// base-2 exponential (denormal results flush to zero; P is stored as 16-bit
+// values whose smallest normal is 2^-126 (bf16) or 2^-14 (fp16) anyway).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Maximum of N values as a tree of three-input maxima.
+template <int N>
+__device__ __forceinline__ float max_n(const float* v) {
+  if constexpr (N == 1) {
+    return v[0];
+  } else if constexpr (N == 2) {
+    return fmaxf(v[0], v[1]);
+  } else if constexpr (N == 3) {
+    return max3f(v[0], v[1], v[2]);
+  } else {
+    constexpr int A = (N + 2) / 3, B = (N - A + 1) / 2;
+    return max3f(max_n<A>(v), max_n<B>(v + A), max_n<N - A - B>(v + A + B));
+  }
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if (BF16) {
