@@ -36,11 +36,17 @@ __device__ unsigned long long g_hfan_diag[16];
 extern "C" int hfan_diag_read(unsigned long long* out) {
   return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 16);
 }
+__device__ long long g_hfan_tl[2][128][8];
+extern "C" int hfan_tl_read(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, g_hfan_tl, sizeof(long long) * 2 * 128 * 8);
+}
 extern "C" int hfan_diag_clear() {
   unsigned long long z[16] = {0};
   return (int)cudaMemcpyToSymbol(g_hfan_diag, z, sizeof(z));
 }
 #define DIAG_ADD(i, v) atomicAdd(&g_hfan_diag[i], (unsigned long long)(v))
+#define TL(slot, t, k) \
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (t) < 128) g_hfan_tl[slot][t][k] = clock64()
 #define DIAG_T(acc, stmt)               \
   do {                                  \
     const long long t0_ = clock64();    \
@@ -50,6 +56,7 @@ extern "C" int hfan_diag_clear() {
 #else
 #define DIAG_ADD(i, v) ((void)0)
 #define DIAG_T(acc, stmt) stmt
+#define TL(slot, t, k) ((void)0)
 #endif
 
 namespace hfan {
@@ -235,7 +242,7 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
 
 // ------------------------------------------------------------------ kernel
 template <int HD, bool BF16, int NORM>
-__global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
+__global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   using L = Layout<HD>;
@@ -354,96 +361,73 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       }
       if (!ok) record_error(p, ctl, kDevWaitTimeout);
     }
-  } else if (warp == Roles<HD>::MMA_WARP) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == Roles<HD>::MMA_WARP || warp == Roles<HD>::MMA2_WARP) {
+    // ------------------------------------------------------------ MMA issuers
+    // tcgen05.mma issue is nearly synchronous with its execution, so every
+    // wait of a single issuing thread would leave the tensor pipe idle.  Two
+    // issuers: this warp's lane 0 issues S = Q K^T (every pass), the second
+    // issuer's lane 0 issues O += P V (final pass); each one's barrier waits
+    // overlap the other's MMAs.
+    //
+    // Ring bookkeeping shared by both: a K-only pass consumes items t = 0..n-1
+    // from stages t % kScanStages; the final pass consumes K(t) as item
+    // (t ? 2t - 1 : 0) and V(j) as item min(2j + 2, 2n - 1) from stages
+    // item % NS.  A stage's full barrier has completed once per earlier use,
+    // so the parity to wait for is (earlier uses) & 1.
+    const bool qk_issuer = warp == Roles<HD>::MMA_WARP;
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q);
       const uint32_t ring_base = smem_u32(smem + L::RING);
-      uint32_t full_ph = 0, sc = 0, pc = 0, ctrl_phase = 0;
-      int ring = 0, ns = kScanStages;
-      long long dg_full = 0, dg_sempty = 0, dg_pfull = 0, dg_qk = 0, dg_pv = 0, dg_t0 = 0;
-      auto consume = [&](int* st) -> bool {
-        *st = ring;
-        ring = ring + 1 == ns ? 0 : ring + 1;
-        bool w_;
-        DIAG_T(dg_full, w_ = mbar_wait(&bars->full[*st], (full_ph >> *st) & 1, abort_flag));
-        if (!w_) return false;
-        full_ph ^= 1u << *st;
-        return true;
+      uint32_t base0 = 0, base1 = 0, ctrl_phase = 0;  // uses of stages 0 / 1 by finished K-only passes
+      auto wait_item = [&](int idx, int nst, int* st) -> bool {
+        const int s_ = idx % nst;
+        const uint32_t uses = (uint32_t)(idx / nst) + (s_ == 0 ? base0 : s_ == 1 ? base1 : 0u);
+        *st = s_;
+        return mbar_wait(&bars->full[s_], uses & 1, abort_flag);
       };
       int pass = SCAN ? kPassTopC : kPassFinal;
-      bool ok = mbar_wait(&bars->q_full, 0, abort_flag);
-      auto issue_pv = [&](int t) -> bool {
-        int vs;
-        if (!consume(&vs)) return false;
-        const int pb = pc & 1;
-        bool w_;
-        DIAG_T(dg_pfull, w_ = mbar_wait(&bars->p_full[pb], (pc >> 1) & 1, abort_flag));
-        if (!w_) return false;
-        tc_fence_after();
-#ifdef HFAN_DIAG
-        const long long dq0 = clock64();
-#endif
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // A = P [128 x 128 keys] in TMEM buffer pb (8 columns per 16 keys);
-          // B = V tile, MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
-          const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
-          mma_f16_ts(tmem_o, tmem_p + pb * 64 + kk * 8, bd, IDESC_PV, t > 0 || kk > 0);
-        }
-        mma_commit(&bars->empty[vs]);
-        mma_commit(&bars->pv_done[pb]);
-#ifdef HFAN_DIAG
-        dg_pv += clock64() - dq0;
-#endif
-        ++pc;
-        return true;
-      };
+      bool ok = qk_issuer ? mbar_wait(&bars->q_full, 0, abort_flag) : true;
+      uint32_t sc = 0;
       while (ok) {
         const bool fin = pass == kPassFinal;
-        ring = 0;
-        ns = fin ? L::NS : kScanStages;
-        for (int t = 0; t < n_tiles && ok; ++t) {
-          int ks;
-          const int sb = sc & 1;
-          if (!(ok = consume(&ks))) break;
-          DIAG_T(dg_sempty, ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag));
-          if (!ok) break;
-          tc_fence_after();
-#ifdef HFAN_DIAG
-          const long long dq0 = clock64();
-#endif
+        if (qk_issuer) {
+          for (int t = 0; t < n_tiles && ok; ++t) {
+            int ks;
+            const int sb = sc & 1;
+            if (!(ok = wait_item(fin ? (t ? 2 * t - 1 : 0) : t, fin ? L::NS : kScanStages, &ks))) break;
+            if (!(ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag))) break;
+            tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t a = sw128_desc(q_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(ring_base + ks * KV_BYTES + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-            mma_f16_ss(tmem + sb * 128, a, bd, IDESC_QK, kk > 0);
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint64_t a = sw128_desc(q_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+              const uint64_t bd = sw128_desc(ring_base + ks * KV_BYTES + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+              mma_f16_ss(tmem + sb * 128, a, bd, IDESC_QK, kk > 0);
+            }
+            mma_commit(&bars->s_full[sb]);
+            mma_commit(&bars->empty[ks]);
+            ++sc;
           }
-          mma_commit(&bars->s_full[sb]);
-          mma_commit(&bars->empty[ks]);
-#ifdef HFAN_DIAG
-          dg_qk += clock64() - dq0;
-#endif
-          ++sc;
-          if (fin && t >= 1) ok = issue_pv(t - 1);
+        } else if (fin) {
+          for (int j = 0; j < n_tiles && ok; ++j) {
+            int vs;
+            const int pb = j & 1;
+            if (!(ok = wait_item(min(2 * j + 2, 2 * n_tiles - 1), L::NS, &vs))) break;
+            if (!(ok = mbar_wait(&bars->p_full[pb], (j >> 1) & 1, abort_flag))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              // A = P [128 x 128 keys] in TMEM buffer pb (8 columns per 16 keys);
+              // B = V tile, MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
+              const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
+              mma_f16_ts(tmem_o, tmem_p + pb * 64 + kk * 8, bd, IDESC_PV, j > 0 || kk > 0);
+            }
+            mma_commit(&bars->empty[vs]);
+            mma_commit(&bars->pv_done[pb]);
+          }
         }
-        if (!ok) break;
-        if (fin) {
-          if (n_tiles > 0) ok = issue_pv(n_tiles - 1);
-#ifdef HFAN_DIAG
-          DIAG_ADD(8, dg_full);
-          DIAG_ADD(9, dg_sempty);
-          DIAG_ADD(10, dg_pfull);
-          DIAG_ADD(11, clock64() - dg_t0);
-          DIAG_ADD(14, dg_qk);
-          DIAG_ADD(15, dg_pv);
-#endif
-          break;
-        }
-#ifdef HFAN_DIAG
-        dg_full = dg_sempty = dg_pfull = dg_qk = dg_pv = 0;  // count the final pass only
-        dg_t0 = clock64();
-#endif
+        if (!ok || fin) break;
+        base0 += (uint32_t)(n_tiles + 1) / 2;
+        base1 += (uint32_t)n_tiles / 2;
         if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
         ctrl_phase ^= 1;
         pass = ctl->next_pass;
@@ -776,7 +760,9 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
     long long dg_s = 0, dg_pv = 0;
 #endif
     for (int t = 0; t < n_tiles && (ok || !SPARSE); ++t) {
+      if (threadIdx.x == 0) TL(1, t, 0);
       if (ok) DIAG_T(dg_s, ok = load_s(t));
+      if (threadIdx.x == 0) TL(1, t, 1);
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
@@ -849,6 +835,7 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(&bars->p_full[pb]);
+      if (threadIdx.x == 0) TL(1, t, 2);
       ++pc;
     }
     if (ok && n_tiles > 0) {
@@ -946,17 +933,17 @@ cudaError_t launch_fwd(const AttnParams& p, int max_q, cudaStream_t stream) {
     case HFAN_SOFTMAX1:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, Roles<HD>::THREADS, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, p);
       break;
     case HFAN_SPARSEMAX:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, Roles<HD>::THREADS, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, p);
       break;
     default:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, Roles<HD>::THREADS, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, p);
       break;
   }
   return cudaGetLastError();

@@ -127,13 +127,14 @@ __device__ __forceinline__ void store_chunks_sw128(uint8_t* base, int row, int c
 // Warp roles of the tensor-core kernels: HD / 32 row warpgroups (warpgroup wg
 // owns 128 / NWG columns of each 128 x 128 tile and 32 head-dim columns),
 // then one TMA warp and one MMA warp.
-template <int HD>
+template <int HD, int ISSUERS = 1>
 struct Roles {
   static constexpr int NWG = HD / 32;
   static constexpr int ROW_THREADS = 128 * NWG;
   static constexpr int TMA_WARP = 4 * NWG;
   static constexpr int MMA_WARP = 4 * NWG + 1;
-  static constexpr int THREADS = 32 * (4 * NWG + 2);
+  static constexpr int MMA2_WARP = 4 * NWG + 2;  // second MMA issuer (kernels with ISSUERS == 2)
+  static constexpr int THREADS = 32 * (4 * NWG + 1 + ISSUERS);
 };
 
 // ------------------------------------------------------------------ host

@@ -61,15 +61,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`
+// while the phase is incomplete (a waiting warp then takes no issue slots
+// from the warps it shares a scheduler with); it resumes as soon as the phase
+// completes.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: gives up after `limit_ns` of wall time or as soon as *abort
 // is set by another warp; returns false on give-up (the caller then records
-// the error and leaves its loop).
+// the error and leaves its loop).  Between checks of the limit the thread is
+// suspended on the barrier rather than spinning.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > limit_ns) return false;
   }
