@@ -79,7 +79,7 @@ struct QLayout {
 };
 
 template <int HD, bool BF16, int NORM>
-__global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
+__global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const AttnParams p) {
@@ -177,29 +177,15 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       }
     }
   } else if (warp == Roles<HD>::MMA_WARP) {
+    // S and dP issuer (every pass).  dQ has its own issuer warp, so that the
+    // waits of one overlap the tensor work of the other.
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
-      const uint32_t ds_base = smem_u32(smem + L::DS);
       bool ok = mbar_wait(&bars->qd_full, 0, abort_flag);
-      uint32_t kc = 0, sdc = 0, dsc = 0;
-      auto issue_dq = [&](int s, int t) -> bool {
-        if (!mbar_wait(&bars->ds_full, dsc & 1, abort_flag)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t a = sw128_desc(ds_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(k_base + s * TILE + kk * 16 * 128, kHalf, 1024);
-          mma_f16_ss(tmem_dq, a, bd, IDESC_DQ, t > 0 || kk > 0);
-        }
-        mma_commit(&bars->k_empty[s]);
-        mma_commit(&bars->ds_empty);
-        ++dsc;
-        return true;
-      };
+      uint32_t kc = 0, sdc = 0;
       for (int pass = 0; pass < NPASS && ok; ++pass) {
         const bool last = pass == NPASS - 1;
-        int prev_s = 0;
         for (int t = 0; t < n_tiles && ok; ++t) {
           const int s = kc & 1;
           const uint32_t ph = (kc >> 1) & 1;
@@ -221,20 +207,37 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           }
           mma_commit(&bars->sdp_full);
           mma_commit(&bars->v_empty[s]);
+          // K stays resident for dQ in the last pass (the dQ issuer releases it)
+          if (!last) mma_commit(&bars->k_empty[s]);
           ++sdc;
-          if (!last) {
-            mma_commit(&bars->k_empty[s]);
-          } else {
-            if (t > 0) ok = issue_dq(prev_s, t - 1);
-            prev_s = s;
-          }
           ++kc;
         }
-        if (ok && last) {
-          ok = issue_dq(prev_s, n_tiles - 1);
-          mma_commit(&bars->dq_done);
-        }
       }
+      if (!ok) {
+        *abort_ptr = 1;
+        if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+      }
+    }
+  } else if (warp == Roles<HD>::MMA2_WARP) {
+    // dQ += dS K issuer (last pass).  K(t) sits in stage ((NPASS - 1) n + t) & 1;
+    // it was loaded before S(t), which preceded dS(t).
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t k_base = smem_u32(smem + L::K), ds_base = smem_u32(smem + L::DS);
+      bool ok = true;
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        const int s = ((NPASS - 1) * n_tiles + t) & 1;
+        if (!(ok = mbar_wait(&bars->ds_full, t & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t a = sw128_desc(ds_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(k_base + s * TILE + kk * 16 * 128, kHalf, 1024);
+          mma_f16_ss(tmem_dq, a, bd, IDESC_DQ, t > 0 || kk > 0);
+        }
+        mma_commit(&bars->k_empty[s]);
+        mma_commit(&bars->ds_empty);
+      }
+      if (ok) mma_commit(&bars->dq_done);
       if (!ok) {
         *abort_ptr = 1;
         if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
@@ -318,6 +321,10 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         for (int cc = 0; cc < CPW; ++cc) {
           float sv[32], dv[32];
           chunk(t, wg * CPW + cc, sv, dv);
+          if (cc == CPW - 1) {  // S and dP are in registers: the next tile's MMAs may overwrite them
+            tc_fence_before();
+            warp_arrive(&bars->sdp_empty);
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float w, pr;
@@ -326,8 +333,6 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
             den += w;
           }
         }
-        tc_fence_before();
-        warp_arrive(&bars->sdp_empty);
         ++sdc;
       }
       // combine the warpgroups' column sums (the dS buffer is idle until pass B)
@@ -355,6 +360,10 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       for (int cc = 0; cc < CPW; ++cc) {
         float sv[32], dv[32];
         chunk(t, wg * CPW + cc, sv, dv);
+        if (cc == CPW - 1) {  // S and dP are in registers: the next tile's MMAs may overwrite them
+          tc_fence_before();
+          warp_arrive(&bars->sdp_empty);
+        }
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           float w0, w1, p0, p1;
@@ -363,8 +372,6 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           pk[cc * 16 + j / 2] = pack2<BF16>(w0 * (dv[j] - c), w1 * (dv[j + 1] - c));
         }
       }
-      tc_fence_before();
-      warp_arrive(&bars->sdp_empty);
       ++sdc;
       if (t > 0) {
         if (!(ok = wait_warp(&bars->ds_empty, (t - 1) & 1, abort_flag))) break;
@@ -440,7 +447,7 @@ struct KLayout {
 };
 
 template <int HD, bool BF16, int NORM>
-__global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
+__global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const AttnParams p) {
@@ -533,31 +540,11 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
       }
     }
   } else if (warp == Roles<HD>::MMA_WARP) {
+    // S^T and dP^T issuer; dV / dK have their own issuer warp.
     if (lane == 0 && n_units > 0) {
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
-      const uint32_t pb_base = smem_u32(smem + L::PB);
       bool ok = mbar_wait(&bars->kv_full, 0, abort_flag);
-      uint32_t pbc = 0;
-      // dV += P^T dO and dK += dS^T Q for unit u (stage s)
-      auto issue_acc = [&](int u, int s) -> bool {
-        for (int which = 0; which < 2; ++which) {
-          if (!mbar_wait(&bars->pb_full, pbc & 1, abort_flag)) return false;
-          tc_fence_after();
-          const uint32_t bsrc = (which == 0 ? do_base : q_base) + s * TILE;
-          const uint32_t dst = which == 0 ? tmem_dv : tmem_dk;
-#pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk) {
-            const uint64_t a = sw128_desc(pb_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(bsrc + kk * 16 * 128, kHalf, 1024);
-            mma_f16_ss(dst, a, bd, IDESC_ACC, u > 0 || kk > 0);
-          }
-          mma_commit(&bars->pb_empty);
-          ++pbc;
-        }
-        mma_commit(&bars->qd_empty[s]);
-        return true;
-      };
       for (int u = 0; u < n_units && ok; ++u) {
         const int s = u & 1;
         if (!(ok = mbar_wait(&bars->qd_full[s], (u >> 1) & 1, abort_flag))) break;
@@ -576,12 +563,39 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
                      IDESC_S, kk > 0);
         }
         mma_commit(&bars->sdp_full);
-        if (u > 0) ok = issue_acc(u - 1, (u - 1) & 1);
       }
-      if (ok) {
-        ok = issue_acc(n_units - 1, (n_units - 1) & 1);
-        mma_commit(&bars->done);
+      if (!ok) {
+        *abort_ptr = 1;
+        if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
       }
+    }
+  } else if (warp == Roles<HD>::MMA2_WARP) {
+    // dV += P^T dO, then dK += dS^T Q, for every unit; the unit's Q / dO stage
+    // is released after both (its S^T / dP^T MMAs completed before P^T existed).
+    if (lane == 0 && n_units > 0) {
+      const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
+      const uint32_t pb_base = smem_u32(smem + L::PB);
+      bool ok = true;
+      uint32_t pbc = 0;
+      for (int u = 0; u < n_units && ok; ++u) {
+        const int s = u & 1;
+        for (int which = 0; which < 2 && ok; ++which) {
+          if (!(ok = mbar_wait(&bars->pb_full, pbc & 1, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t bsrc = (which == 0 ? do_base : q_base) + s * TILE;
+          const uint32_t dst = which == 0 ? tmem_dv : tmem_dk;
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk) {
+            const uint64_t a = sw128_desc(pb_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(bsrc + kk * 16 * 128, kHalf, 1024);
+            mma_f16_ss(dst, a, bd, IDESC_ACC, u > 0 || kk > 0);
+          }
+          mma_commit(&bars->pb_empty);
+          ++pbc;
+        }
+        if (ok) mma_commit(&bars->qd_empty[s]);
+      }
+      if (ok) mma_commit(&bars->done);
       if (!ok) {
         *abort_ptr = 1;
         if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
@@ -638,6 +652,10 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
         tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
         tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
         tmem_wait_ld();
+        if (cc == CPW - 1) {  // S^T and dP^T are in registers: the next unit's MMAs may overwrite them
+          tc_fence_before();
+          warp_arrive(&bars->sdp_empty);
+        }
         const int lo = c_lo - cidx * 32, hi = c_hi - cidx * 32;
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
@@ -655,8 +673,6 @@ __global__ void __launch_bounds__(Roles<HD>::THREADS, 1)
           dpk[cc * 16 + e / 2] = pack2<BF16>(dsv[0], dsv[1]);
         }
       }
-      tc_fence_before();
-      warp_arrive(&bars->sdp_empty);
       // P^T, then dS^T, through the shared buffer
       for (int which = 0; which < 2 && ok; ++which) {
         if (pbc > 0) {
@@ -747,10 +763,10 @@ cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t
       !make_map(&mv, p.v, BF16, HD, tk, p.hkv, batch, p.v_st, p.v_sh, varlen ? tk * p.v_st : p.v_sb))
     return cudaErrorInvalidValue;
   cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
-                           Roles<HD>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+                           Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
   if (e != cudaSuccess) return e;
   return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
-                  Roles<HD>::THREADS, KLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+                  Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
 }
 
 template <int HD, bool BF16>
