@@ -43,7 +43,7 @@ template <int NORM> __device__ __forceinline__ float zscale(float scale) {
 template <int NORM>
 __device__ __forceinline__ void weight(float z, float st0, float inv_l, float* w, float* pr) {
   if (NORM == HFAN_SOFTMAX1) {
-    float e = exp2f(z - st0) * inv_l;
+    float e = ex2_ftz(z - st0) * inv_l;
     *w = e;
     *pr = e;
   } else {
@@ -615,27 +615,35 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     uint32_t pbc = 0;
     // The named barriers run on every iteration, even after a timeout, so that
     // no warp waits for one that has left the loop.
+    // Row statistics of a unit's 128 query rows: warpgroup 0 loads those of
+    // the next unit into registers while this one is processed, and stages
+    // them in shared memory between two barriers at the unit's start.
+    float na = kPosInf, nb = 1.f, nc = 0.f;
+    auto fetch = [&](int u_) {
+      na = kPosInf;
+      nb = 1.f;
+      nc = 0.f;
+      if (wg != 0 || u_ >= n_units) return;
+      const int iq = (m_lo + u_ % n_m) * kBM + row;
+      if (iq < g.q_len) {
+        const int64_t si = stat_index(p, g, kvh * groups + u_ / n_m, iq);
+        na = p.stats[si];
+        nb = p.stats[(int64_t)p.hq * p.rows_total + si];
+        nc = p.corr[si];
+      }
+    };
+    fetch(0);
     for (int u = 0; u < n_units; ++u) {
-      const int hq = kvh * groups + u / n_m;
       const int m = m_lo + u % n_m;
       const int qbase = m * kBM;
-      // stage the statistics of this tile's 128 query rows
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
       if (wg == 0) {
-        const int iq = qbase + row;
-        float a = kPosInf, bb = 1.f, cc = 0.f;
-        if (iq < g.q_len) {
-          const int64_t si = stat_index(p, g, hq, iq);
-          a = p.stats[si];
-          bb = p.stats[(int64_t)p.hq * p.rows_total + si];
-          cc = p.corr[si];
-        }
-        if (NORM == HFAN_SOFTMAX1 && !(iq < g.q_len)) a = kPosInf;
-        st0s[row] = a;
-        st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / bb : 1.f;
-        crs[row] = cc;
+        st0s[row] = na;
+        st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
+        crs[row] = nc;
       }
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      fetch(u + 1);
       if (!ok) continue;
       if (!(ok = wait_warp(&bars->sdp_full, u & 1, abort_flag))) continue;
       tc_fence_after();
