@@ -27,9 +27,11 @@
 // Row statistics use the same layout as the other attention kernels, so the
 // general paged backward can consume them.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "params.cuh"
+#include "tc_common.cuh"
 
 namespace hfan {
 namespace {
@@ -201,6 +203,402 @@ __global__ void __launch_bounds__(256, 2) decode_sm1_split(AttnParams p, DecodeW
       }
     }
   }
+}
+
+// ---------------------------------------------------- softmax1, tiled path
+// Same work unit and result as decode_sm1_split, restructured so that HBM,
+// not instruction issue, bounds it:
+//  * a producer warp streams blocks of kBlk tokens (every KV head) into a
+//    kStagesDec-deep shared-memory ring with TMA tile loads (a 3-D tensor map
+//    over (dim, token, head), 128-byte swizzle, completion on mbarriers), so
+//    several blocks per SM are in flight;
+//  * one consumer warp per KV head computes with mma.sync m16n8k16 (the G
+//    query heads padded to 16 rows): S = Q K^T over the block, the online
+//    softmax on the accumulator fragments, then O += P V with P taken
+//    directly from the S fragments as the A operand.  K and V fragments come
+//    from the swizzled tiles with ldmatrix (V transposed), conflict-free.
+// A block never crosses a page (pages hold a multiple of kBlk tokens).
+constexpr int kBlk = 16;        // tokens per block (the MMA k extent of P V)
+constexpr int kStagesDec = 3;   // ring depth
+
+struct BulkCtl {
+  uint64_t full[kStagesDec], empty[kStagesDec];
+  int valid[kStagesDec];
+  int abort;
+};
+
+// Bytes of one block of one cache (K or V): D/64 swizzled 64-dim halves of
+// [hkv][kBlk] rows of 128 bytes.
+template <int D>
+__host__ __device__ constexpr uint32_t tiled_block_bytes(int hkv) {
+  return (uint32_t)(D / 64) * 128u * kBlk * (uint32_t)hkv;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_t(float a, float b) {
+  return tc::pack2<std::is_same<T, __nv_bfloat16>::value>(a, b);
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(288, 1)
+    decode_sm1_tiled(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, AttnParams p,
+                     DecodeWs ws) {
+  static_assert(G <= 8, "query heads per KV head");
+  constexpr int NHALF = D / 64;
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  const int b = blockIdx.y, split = blockIdx.x;
+  const int L = p.seq_lens[b];
+  const int t0 = split * kChunk;
+  if (t0 >= L) return;
+  const int t1 = min(L, t0 + kChunk);
+  const int nblk = (t1 - t0 + kBlk - 1) / kBlk;
+  const int hkv = p.hkv;  // <= 8 (host check)
+  const uint32_t blk_bytes = tiled_block_bytes<D>(hkv), half_bytes = blk_bytes / NHALF;
+  uint8_t* kring = dsm;
+  uint8_t* vring = dsm + kStagesDec * blk_bytes;
+  BulkCtl* ctl = reinterpret_cast<BulkCtl*>(dsm + 2 * kStagesDec * blk_bytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesDec; ++s) {
+      tc::mbar_init(&ctl->full[s], 1);
+      tc::mbar_init(&ctl->empty[s], hkv);
+    }
+    ctl->abort = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &ctl->abort;
+  const int* bt = page_row(p, b);
+
+  if (warp == 8) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_k);
+      tc::prefetch_tmap(&tm_v);
+      for (int blk = 0; blk < nblk; ++blk) {
+        const int s = blk % kStagesDec;
+        if (blk >= kStagesDec &&
+            !tc::mbar_wait(&ctl->empty[s], ((blk / kStagesDec) - 1) & 1, abort_flag)) {
+          ctl->abort = 1;
+          if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+          break;
+        }
+        const int t = t0 + blk * kBlk;
+        const int page = bt[t / p.page_size];
+        const int64_t tok0 = (int64_t)page * p.page_size + (t % p.page_size);
+        const bool ok = page >= 0 && tok0 + kBlk <= p.num_cache_tokens;
+        ctl->valid[s] = ok ? 1 : 0;
+        if (ok) {
+          tc::mbar_arrive_expect_tx(&ctl->full[s], 2 * blk_bytes);
+#pragma unroll
+          for (int hh = 0; hh < NHALF; ++hh) {
+            tma_load_3d(tc::smem_u32(kring + s * blk_bytes + hh * half_bytes), &tm_k, &ctl->full[s], 64 * hh,
+                        (int)tok0, 0);
+            tma_load_3d(tc::smem_u32(vring + s * blk_bytes + hh * half_bytes), &tm_v, &ctl->full[s], 64 * hh,
+                        (int)tok0, 0);
+          }
+        } else {
+          if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevBadPage);
+          tc::mbar_arrive(&ctl->full[s]);
+        }
+      }
+    }
+  } else if (warp < hkv) {
+    // ---------------------------------------------------------- consumers
+    const int kvh = warp;
+    const int g = lane >> 2, tq = lane & 3;  // fragment row (query head) and column pair
+    const float zs = p.scale * kLog2e;
+    // A fragments of Q (rows >= G are zero): a0 = Q[g][16ks + 2tq ..], a2 = Q[g][16ks + 8 + 2tq ..]
+    uint32_t qa[D / 16][2];
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) qa[ks][0] = qa[ks][1] = 0u;
+    if (g < G) {
+      const T* qr = static_cast<const T*>(p.q) + (int64_t)b * p.q_sb + (int64_t)(kvh * G + g) * p.q_sh;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        qa[ks][0] = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * tq);
+        qa[ks][1] = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * tq);
+      }
+    }
+    float o[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m = kNegInf, l = 0.f;
+    // ldmatrix row addresses of this lane: matrix mi = lane >> 3, row ri = lane & 7 (= token & 7,
+    // which is also the 128-byte swizzle phase of the row)
+    const int mi = lane >> 3, ri = lane & 7;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int s = blk % kStagesDec;
+      bool got = tc::mbar_wait(&ctl->full[s], (blk / kStagesDec) & 1, abort_flag);
+      got = __all_sync(0xffffffffu, got);
+      if (!got) {
+        if (lane == 0) {
+          ctl->abort = 1;
+          if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+        }
+        break;
+      }
+      const bool bvalid = ctl->valid[s] != 0;
+      const uint32_t kst = tc::smem_u32(kring + s * blk_bytes), vst = tc::smem_u32(vring + s * blk_bytes);
+      // ---- S = Q K^T: two n-tiles of 8 tokens
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        // matrix mi: tokens 8 (mi >> 1) + ri, dims 16 ks + 8 (mi & 1) .. + 8
+        const int dim0 = 16 * ks + 8 * (mi & 1);
+        const int row = kvh * kBlk + 8 * (mi >> 1) + ri;
+        const uint32_t addr = kst + (dim0 >> 6) * half_bytes + row * 128 + ((((dim0 & 63) >> 3) ^ ri) << 4);
+        uint32_t kb4[4];
+        ldsm_x4(addr, kb4);
+        const uint32_t a[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        mma16816<T>(sacc[0], a, kb4[0], kb4[1]);
+        mma16816<T>(sacc[1], a, kb4[2], kb4[3]);
+      }
+      // ---- online softmax of row g over the block's 16 tokens (4 per lane)
+      const int tb = t0 + blk * kBlk;
+      float sv[4] = {sacc[0][0] * zs, sacc[0][1] * zs, sacc[1][0] * zs, sacc[1][1] * zs};
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int tok = 8 * (x >> 1) + 2 * tq + (x & 1);
+        if (!(bvalid && tb + tok < t1)) sv[x] = kNegInf;
+      }
+      float bmax = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+      bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+      // lazy reference: move it only when the block max exceeds it by 2^8
+      const bool move = bmax > m + 8.f;
+      const float m_new = move ? bmax : m;
+      const float alpha = move ? exp2f(m - m_new) : 1.f;  // 0 when m was -inf
+      if (__any_sync(0xffffffffu, move)) {
+        l *= alpha;
+#pragma unroll
+        for (int j = 0; j < D / 8; ++j) {
+          o[j][0] *= alpha;
+          o[j][1] *= alpha;
+        }
+      }
+      m = m_new;
+      float pv[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) pv[x] = sv[x] > kNegInf ? exp2f(sv[x] - m) : 0.f;
+      l += (pv[0] + pv[1]) + (pv[2] + pv[3]);
+      uint32_t pa[4];
+      pa[0] = pack2_t<T>(pv[0], pv[1]);
+      pa[1] = 0u;
+      pa[2] = pack2_t<T>(pv[2], pv[3]);
+      pa[3] = 0u;
+      // ---- O += P V: D/8 n-tiles of 8 dims, k = the block's 16 tokens
+#pragma unroll
+      for (int jp = 0; jp < D / 16; ++jp) {
+        // matrix mi: dims 8 (2 jp + (mi >> 1)) .. + 8, tokens 8 (mi & 1) + ri (transposed load)
+        const int dt = 2 * jp + (mi >> 1);
+        const int row = kvh * kBlk + 8 * (mi & 1) + ri;
+        const uint32_t addr = vst + (dt >> 3) * half_bytes + row * 128 + (((dt & 7) ^ ri) << 4);
+        uint32_t vb4[4];
+        ldsm_x4_t(addr, vb4);
+        mma16816<T>(o[2 * jp], pa, vb4[0], vb4[1]);
+        mma16816<T>(o[2 * jp + 1], pa, vb4[2], vb4[3]);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ctl->empty[s]);
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (g < G) {
+      const int64_t unit = ((int64_t)b * p.hkv + kvh) * ws.splits + split;
+      float* dst = ws.acc + (unit * G + g) * D + 2 * tq;
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][0], o[j][1]);
+      if (tq == 0) {
+        ws.ml[(unit * G + g) * 2 + 0] = m;
+        ws.ml[(unit * G + g) * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+// Sparse scores through the same ring (K blocks only): z = s * zs for every
+// key, written to the workspace rows like decode_sparse_scores.
+template <typename T, int D, int G, int NORM>
+__global__ void __launch_bounds__(288, 1)
+    decode_sparse_scores_tiled(const __grid_constant__ CUtensorMap tm_k, AttnParams p, DecodeWs ws, int max_len) {
+  static_assert(G <= 8, "query heads per KV head");
+  constexpr int NHALF = D / 64;
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  const int b = blockIdx.y, split = blockIdx.x;
+  const int L = p.seq_lens[b];
+  const int t0 = split * kChunk;
+  if (t0 >= L) return;
+  const int t1 = min(L, t0 + kChunk);
+  const int nblk = (t1 - t0 + kBlk - 1) / kBlk;
+  const int hkv = p.hkv;
+  const uint32_t blk_bytes = tiled_block_bytes<D>(hkv), half_bytes = blk_bytes / NHALF;
+  constexpr int NS = 2 * kStagesDec;  // K only: twice the stages in the same space
+  uint8_t* kring = dsm;
+  BulkCtl* ctl0 = reinterpret_cast<BulkCtl*>(dsm + NS * blk_bytes);
+  BulkCtl* ctl1 = ctl0 + 1;
+  auto full = [&](int s_) { return s_ < kStagesDec ? &ctl0->full[s_] : &ctl1->full[s_ - kStagesDec]; };
+  auto empty = [&](int s_) { return s_ < kStagesDec ? &ctl0->empty[s_] : &ctl1->empty[s_ - kStagesDec]; };
+  auto valid = [&](int s_) -> int* { return s_ < kStagesDec ? &ctl0->valid[s_] : &ctl1->valid[s_ - kStagesDec]; };
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s_ = 0; s_ < NS; ++s_) {
+      tc::mbar_init(full(s_), 1);
+      tc::mbar_init(empty(s_), hkv);
+    }
+    ctl0->abort = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &ctl0->abort;
+  const int* bt = page_row(p, b);
+
+  if (warp == 8) {
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_k);
+      for (int blk = 0; blk < nblk; ++blk) {
+        const int s_ = blk % NS;
+        if (blk >= NS && !tc::mbar_wait(empty(s_), ((blk / NS) - 1) & 1, abort_flag)) {
+          ctl0->abort = 1;
+          if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+          break;
+        }
+        const int t = t0 + blk * kBlk;
+        const int page = bt[t / p.page_size];
+        const int64_t tok0 = (int64_t)page * p.page_size + (t % p.page_size);
+        const bool ok = page >= 0 && tok0 + kBlk <= p.num_cache_tokens;
+        *valid(s_) = ok ? 1 : 0;
+        if (ok) {
+          tc::mbar_arrive_expect_tx(full(s_), blk_bytes);
+#pragma unroll
+          for (int hh = 0; hh < NHALF; ++hh)
+            tma_load_3d(tc::smem_u32(kring + s_ * blk_bytes + hh * half_bytes), &tm_k, full(s_), 64 * hh, (int)tok0,
+                        0);
+        } else {
+          if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevBadPage);
+          tc::mbar_arrive(full(s_));
+        }
+      }
+    }
+  } else if (warp < hkv) {
+    const int kvh = warp;
+    const int g = lane >> 2, tq = lane & 3;
+    const float zs = NORM == HFAN_SPARSEMAX ? p.scale : 0.5f * p.scale;
+    uint32_t qa[D / 16][2];
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) qa[ks][0] = qa[ks][1] = 0u;
+    if (g < G) {
+      const T* qr = static_cast<const T*>(p.q) + (int64_t)b * p.q_sb + (int64_t)(kvh * G + g) * p.q_sh;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        qa[ks][0] = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * tq);
+        qa[ks][1] = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * tq);
+      }
+    }
+    float* srow = ws.scores + ((int64_t)b * p.hq + kvh * G + (g < G ? g : 0)) * max_len;
+    const int mi = lane >> 3, ri = lane & 7;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int s_ = blk % NS;
+      bool got = tc::mbar_wait(full(s_), (blk / NS) & 1, abort_flag);
+      got = __all_sync(0xffffffffu, got);
+      if (!got) {
+        if (lane == 0) {
+          ctl0->abort = 1;
+          if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevWaitTimeout);
+        }
+        break;
+      }
+      const bool bvalid = *valid(s_) != 0;
+      const uint32_t kst = tc::smem_u32(kring + s_ * blk_bytes);
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int dim0 = 16 * ks + 8 * (mi & 1);
+        const int row = kvh * kBlk + 8 * (mi >> 1) + ri;
+        const uint32_t addr = kst + (dim0 >> 6) * half_bytes + row * 128 + ((((dim0 & 63) >> 3) ^ ri) << 4);
+        uint32_t kb4[4];
+        ldsm_x4(addr, kb4);
+        const uint32_t a[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        mma16816<T>(sacc[0], a, kb4[0], kb4[1]);
+        mma16816<T>(sacc[1], a, kb4[2], kb4[3]);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(empty(s_));
+      const int tb = t0 + blk * kBlk;
+      if (g < G && bvalid) {
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int t = tb + 8 * (x >> 1) + 2 * tq + (x & 1);
+          if (t < t1) srow[t] = sacc[x >> 1][x & 1] * zs;
+        }
+      }
+    }
+  }
+}
+
+// Tensor map over one cache, dims (D, tokens, Hkv) with the cache's token and
+// head strides, box (64, kBlk, Hkv), 128-byte swizzle.
+inline bool make_cache_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t tokens, int hkv,
+                           int64_t st, int64_t sh) {
+  auto fn = tc::encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)hkv};
+  cuuint64_t strides[2] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)kBlk, (cuuint32_t)hkv};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The tiled path applies: at most 8 KV heads, pages of a multiple of kBlk
+// tokens, a ring that fits, and both caches describable by a tensor map.
+template <typename T, int D>
+bool tiled_ok(const AttnParams& p, CUtensorMap* mk, CUtensorMap* mv) {
+  if (p.hkv > 8 || p.page_size % kBlk) return false;
+  if (p.num_cache_tokens >= ((int64_t)1 << 31)) return false;
+  if (2 * kStagesDec * (size_t)tiled_block_bytes<D>(p.hkv) + sizeof(BulkCtl) + 1024 > 220 * 1024) return false;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  return make_cache_map(mk, p.k, bf16, D, p.num_cache_tokens, p.hkv, p.k_st, p.k_sh) &&
+         make_cache_map(mv, p.v, bf16, D, p.num_cache_tokens, p.hkv, p.v_st, p.v_sh);
 }
 
 template <typename T, int D, int G>
@@ -449,6 +847,20 @@ WsLayout ws_layout(const AttnParams& p, int max_len) {
   return w;
 }
 
+// Launches the tiled scores kernel when its conditions hold; false leaves the
+// work to decode_sparse_scores.
+template <typename T, int D, int G, int NORM>
+bool launch_scores_tiled(const AttnParams& p, DecodeWs ws, int max_len, dim3 grid, cudaStream_t s) {
+  CUtensorMap mk, mv;
+  if (!tiled_ok<T, D>(p, &mk, &mv)) return false;
+  const size_t smem = 2 * kStagesDec * (size_t)tiled_block_bytes<D>(p.hkv) + 2 * sizeof(BulkCtl) + 1024;
+  if (cudaFuncSetAttribute(decode_sparse_scores_tiled<T, D, G, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return false;
+  decode_sparse_scores_tiled<T, D, G, NORM><<<grid, 288, smem, s>>>(mk, p, ws, max_len);
+  return true;
+}
+
 template <typename T, int D, int G>
 cudaError_t run(const AttnParams& p, int max_len, void* workspace, cudaStream_t s) {
   const WsLayout w = ws_layout(p, max_len);
@@ -458,7 +870,16 @@ cudaError_t run(const AttnParams& p, int max_len, void* workspace, cudaStream_t 
   dim3 grid_u(w.splits, p.batch), grid_r(p.hq, p.batch);
   const int ut = 32 * min(p.hkv, 8);  // one warp per KV head
   if (p.norm == HFAN_SOFTMAX1) {
-    decode_sm1_split<T, D, G><<<grid_u, ut, 0, s>>>(p, ws);
+    CUtensorMap mk, mv;
+    if (tiled_ok<T, D>(p, &mk, &mv)) {
+      const size_t smem = 2 * kStagesDec * (size_t)tiled_block_bytes<D>(p.hkv) + sizeof(BulkCtl) + 1024;
+      cudaError_t e = cudaFuncSetAttribute(decode_sm1_tiled<T, D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+      if (e != cudaSuccess) return e;
+      decode_sm1_tiled<T, D, G><<<grid_u, 288, smem, s>>>(mk, mv, p, ws);
+    } else {
+      decode_sm1_split<T, D, G><<<grid_u, ut, 0, s>>>(p, ws);
+    }
     decode_sm1_combine<T, D, G><<<grid_r, D, 0, s>>>(p, ws);
     return cudaGetLastError();
   }
@@ -467,13 +888,15 @@ cudaError_t run(const AttnParams& p, int max_len, void* workspace, cudaStream_t 
   if (p.norm == HFAN_SPARSEMAX) {
     e = cudaFuncSetAttribute(decode_sparse_tau<HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tau_smem);
     if (e != cudaSuccess) return e;
-    decode_sparse_scores<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
+    if (!launch_scores_tiled<T, D, G, HFAN_SPARSEMAX>(p, ws, max_len, grid_u, s))
+      decode_sparse_scores<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
     decode_sparse_tau<HFAN_SPARSEMAX><<<grid_r, 512, tau_smem, s>>>(p, ws, max_len);
     decode_sparse_pv<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
   } else {
     e = cudaFuncSetAttribute(decode_sparse_tau<HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tau_smem);
     if (e != cudaSuccess) return e;
-    decode_sparse_scores<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
+    if (!launch_scores_tiled<T, D, G, HFAN_ENTMAX15>(p, ws, max_len, grid_u, s))
+      decode_sparse_scores<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
     decode_sparse_tau<HFAN_ENTMAX15><<<grid_r, 512, tau_smem, s>>>(p, ws, max_len);
     decode_sparse_pv<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
   }
