@@ -268,6 +268,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if args.decode:
         line["paged_decode"] = bench_decode(dev, hbm)
+        line["varlen"] = bench_varlen(dev)
+        line["prescaled_worst_case"] = bench_prescaled(t, flops_rank)
     if args.cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
     return line
@@ -322,6 +324,81 @@ def bench_decode(dev, hbm_peak, bsz=256, norms=("softmax1", "sparsemax", "entmax
         out[name] = {"ms": round(ms, 3), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 3)}
     out["note"] = ("sparsemax/entmax15 read V only for keys in the support, so their algorithmic GB/s "
                    "can exceed the DRAM bandwidth")
+    return out
+
+
+def bench_varlen(dev, norms=("softmax1", "entmax15")):
+    """64 packed sequences with lengths U[128, 4096]
+    (seed 0), cu_seqlens_k = cu_seqlens_q, 16 query / 8 KV heads, D=128, bf16
+    N(0,1) (seed 0), causal; forward and backward device times per normalizer
+    through the varlen ops, in algorithmic TFLOP/s (fwd = 4 Hq D sum L(L+1)/2)."""
+    import torch
+
+    from hf_attention_normalizers_b200 import _native as N
+    from hf_attention_normalizers_b200 import ops
+
+    hq, hkv, d = 16, 8, 128
+    lens = torch.randint(128, 4097, (64,), generator=torch.Generator().manual_seed(0))
+    cu = torch.zeros(65, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0).int()
+    tot, mx = int(cu[-1]), int(lens.max())
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    q = torch.randn(tot, hq, d, generator=gen).to(torch.bfloat16).to(dev)
+    k = torch.randn(tot, hkv, d, generator=gen).to(torch.bfloat16).to(dev)
+    v = torch.randn(tot, hkv, d, generator=gen).to(torch.bfloat16).to(dev)
+    do = torch.randn(tot, hq, d, generator=gen).to(torch.bfloat16).to(dev)
+    cu_d = cu.to(dev)
+    flops = 4.0 * hq * d * float(sum(int(x) * (int(x) + 1) / 2 for x in lens))
+    out = {"config": "BASELINE configs[2]", "tokens": tot, "fwd_flop": flops}
+    for name in norms:
+        nid = N.NORMALIZER_IDS[name]
+        fwd = lambda: ops.varlen_fwd(q, k, v, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
+        o, st = fwd()
+        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
+        bwd()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        reps = 5
+        ev[0].record()
+        for _ in range(reps):
+            fwd()
+        ev[1].record()
+        for _ in range(reps):
+            bwd()
+        ev[2].record()
+        torch.cuda.synchronize()
+        f_ms, b_ms = ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps
+        out[name] = {"fwd_ms": round(f_ms, 3), "bwd_ms": round(b_ms, 3),
+                     "fwd_tflops": round(flops / f_ms / 1e9, 1),
+                     "fwd_bwd_tflops": round(3.5 * flops / (f_ms + b_ms) / 1e9, 1)}
+    return out
+
+
+def bench_prescaled(t, flops, norms=NORMS):
+    """The no-skip worst case of the prefill config: q and k additionally
+    scaled by D^-1/4 each, so the scores are ~N(0, 1/128) and the supports are
+    wide (hundreds of keys for sparsemax, nearly dense for entmax15)."""
+    import torch
+
+    from hf_attention_normalizers_b200 import _native as N
+    from hf_attention_normalizers_b200 import ops
+
+    qs, ks = t["q"] * D ** -0.25, t["k"] * D ** -0.25
+    out = {}
+    for name in norms:
+        nid = N.NORMALIZER_IDS[name]
+        o, st = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
+        ev[1].record()
+        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, nid, D ** -0.5, True, -1)
+        ev[2].record()
+        torch.cuda.synchronize()
+        f_ms, b_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        out[name] = {"fwd_ms": round(f_ms, 3), "bwd_ms": round(b_ms, 3),
+                     "fwd_bwd_tflops": round(3.5 * flops / (f_ms + b_ms) / 1e9, 1)}
     return out
 
 
