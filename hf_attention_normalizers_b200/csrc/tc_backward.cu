@@ -59,10 +59,13 @@ __device__ __forceinline__ void weight(float z, float st0, float inv_l, float* w
 }
 
 // =========================================================== dq kernel
+constexpr int kQStagesK = 3;  // K stays resident until its dQ MMA: one stage deeper than V
+constexpr int kQStagesV = 2;
+
 struct QBars {
   uint64_t qd_full;
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t sdp_full, sdp_empty, ds_full, ds_empty, dq_done;
+  uint64_t k_full[kQStagesK], k_empty[kQStagesK], v_full[kQStagesV], v_empty[kQStagesV];
+  uint64_t sdp_full, sdp_empty, ds_full[2], ds_empty[2], dq_done;
 };
 
 template <int HD>
@@ -71,9 +74,8 @@ struct QLayout {
   static constexpr uint32_t Q = 0;
   static constexpr uint32_t DO = Q + NH * kHalf;
   static constexpr uint32_t K = DO + NH * kHalf;
-  static constexpr uint32_t V = K + 2 * NH * kHalf;
-  static constexpr uint32_t DS = V + 2 * NH * kHalf;
-  static constexpr uint32_t BARS = DS + 2 * kHalf;
+  static constexpr uint32_t V = K + kQStagesK * NH * kHalf;
+  static constexpr uint32_t BARS = V + kQStagesV * NH * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(QBars);
   static constexpr uint32_t TOTAL = CTL + 16 + 1024;
 };
@@ -121,16 +123,20 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->qd_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kQStagesK; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < kQStagesV; ++s) {
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->sdp_full, 1);
     mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS / 32);
-    mbar_init(&bars->ds_full, Roles<HD>::ROW_THREADS / 32);
-    mbar_init(&bars->ds_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->ds_full[s], Roles<HD>::ROW_THREADS / 32);
+      mbar_init(&bars->ds_empty[s], 1);
+    }
     mbar_init(&bars->dq_done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
@@ -140,7 +146,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dq = tmem + 256;
+  // TMEM: S [0, 128), dP [128, 256), dQ [256, 256 + HD), dS double buffer
+  // [384, 512) as packed 16-bit pairs (the A operand of the dQ MMA)
+  const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dq = tmem + 256, tmem_ds = tmem + 384;
 
   if (warp == Roles<HD>::TMA_WARP) {
     if (lane == 0 && n_tiles > 0) {
@@ -158,16 +166,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       for (int pass = 0; pass < NPASS && ok; ++pass) {
         for (int t = 0; t < n_tiles && ok; ++t) {
           const int kb = k_lo + t * kBN;
-          const int s = kc & 1;
-          const uint32_t ph = ((kc >> 1) & 1) ^ 1;
-          if (!(ok = mbar_wait(&bars->k_empty[s], ph, abort_flag))) break;
-          mbar_arrive_expect_tx(&bars->k_full[s], TILE);
+          const int ks = kc % kQStagesK, vs = kc % kQStagesV;
+          if (!(ok = mbar_wait(&bars->k_empty[ks], ((kc / kQStagesK) & 1) ^ 1, abort_flag))) break;
+          mbar_arrive_expect_tx(&bars->k_full[ks], TILE);
           for (int hh = 0; hh < NH; ++hh)
-            tma_load_4d(smem + L::K + s * TILE + hh * kHalf, &tm_k, &bars->k_full[s], 64 * hh, ktok0 + kb, kvh, bcoord);
-          if (!(ok = mbar_wait(&bars->v_empty[s], ph, abort_flag))) break;
-          mbar_arrive_expect_tx(&bars->v_full[s], TILE);
+            tma_load_4d(smem + L::K + ks * TILE + hh * kHalf, &tm_k, &bars->k_full[ks], 64 * hh, ktok0 + kb, kvh,
+                        bcoord);
+          if (!(ok = mbar_wait(&bars->v_empty[vs], ((kc / kQStagesV) & 1) ^ 1, abort_flag))) break;
+          mbar_arrive_expect_tx(&bars->v_full[vs], TILE);
           for (int hh = 0; hh < NH; ++hh)
-            tma_load_4d(smem + L::V + s * TILE + hh * kHalf, &tm_v, &bars->v_full[s], 64 * hh, ktok0 + kb, kvh, bcoord);
+            tma_load_4d(smem + L::V + vs * TILE + hh * kHalf, &tm_v, &bars->v_full[vs], 64 * hh, ktok0 + kb, kvh,
+                        bcoord);
           ++kc;
         }
       }
@@ -187,10 +196,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       for (int pass = 0; pass < NPASS && ok; ++pass) {
         const bool last = pass == NPASS - 1;
         for (int t = 0; t < n_tiles && ok; ++t) {
-          const int s = kc & 1;
-          const uint32_t ph = (kc >> 1) & 1;
-          if (!(ok = mbar_wait(&bars->k_full[s], ph, abort_flag))) break;
-          if (!(ok = mbar_wait(&bars->v_full[s], ph, abort_flag))) break;
+          const int s = kc % kQStagesK, vs = kc % kQStagesV;
+          if (!(ok = mbar_wait(&bars->k_full[s], (kc / kQStagesK) & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(&bars->v_full[vs], (kc / kQStagesV) & 1, abort_flag))) break;
           if (!(ok = mbar_wait(&bars->sdp_empty, (sdc & 1) ^ 1, abort_flag))) break;
           tc_fence_after();
 #pragma unroll
@@ -202,11 +210,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            mma_f16_ss(tmem_dp, sw128_desc(do_base + off, 16, 1024), sw128_desc(v_base + s * TILE + off, 16, 1024),
+            mma_f16_ss(tmem_dp, sw128_desc(do_base + off, 16, 1024), sw128_desc(v_base + vs * TILE + off, 16, 1024),
                        IDESC_S, kk > 0);
           }
           mma_commit(&bars->sdp_full);
-          mma_commit(&bars->v_empty[s]);
+          mma_commit(&bars->v_empty[vs]);
           // K stays resident for dQ in the last pass (the dQ issuer releases it)
           if (!last) mma_commit(&bars->k_empty[s]);
           ++sdc;
@@ -219,23 +227,24 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       }
     }
   } else if (warp == Roles<HD>::MMA2_WARP) {
-    // dQ += dS K issuer (last pass).  K(t) sits in stage ((NPASS - 1) n + t) & 1;
-    // it was loaded before S(t), which preceded dS(t).
+    // dQ += dS K issuer (last pass).  K(t) sits in stage ((NPASS - 1) n + t) % 3;
+    // it was loaded before S(t), which preceded dS(t).  dS(t) is read from
+    // TMEM buffer t & 1.
     if (lane == 0 && n_tiles > 0) {
-      const uint32_t k_base = smem_u32(smem + L::K), ds_base = smem_u32(smem + L::DS);
+      const uint32_t k_base = smem_u32(smem + L::K);
       bool ok = true;
       for (int t = 0; t < n_tiles && ok; ++t) {
-        const int s = ((NPASS - 1) * n_tiles + t) & 1;
-        if (!(ok = mbar_wait(&bars->ds_full, t & 1, abort_flag))) break;
+        const int s = ((NPASS - 1) * n_tiles + t) % kQStagesK;
+        const int db = t & 1;
+        if (!(ok = mbar_wait(&bars->ds_full[db], (t >> 1) & 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t a = sw128_desc(ds_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(k_base + s * TILE + kk * 16 * 128, kHalf, 1024);
-          mma_f16_ss(tmem_dq, a, bd, IDESC_DQ, t > 0 || kk > 0);
+          mma_f16_ts(tmem_dq, tmem_ds + db * 64 + kk * 8, bd, IDESC_DQ, t > 0 || kk > 0);
         }
         mma_commit(&bars->k_empty[s]);
-        mma_commit(&bars->ds_empty);
+        mma_commit(&bars->ds_empty[db]);
       }
       if (ok) mma_commit(&bars->dq_done);
       if (!ok) {
@@ -267,6 +276,41 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       st0 = p.stats[si];
       inv_l = NORM == HFAN_SOFTMAX1 ? 1.f / p.stats[(int64_t)p.hq * p.rows_total + si] : 1.f;
     }
+    // Sums (a, b) of this row over the warpgroups, through the dS TMEM
+    // columns (idle until the first dS write; every thread touches only its
+    // own lane, and the second barrier orders the reads before that write).
+    auto row_exchange = [&](float a, float b, float* sa, float* sb) {
+      tmem_st2(tmem_ds + lane_addr + 2 * wg, __float_as_uint(a), __float_as_uint(b));
+      tmem_wait_st();
+      tc_fence_before();
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      tc_fence_after();
+      float ra = 0.f, rb = 0.f;
+      if constexpr (NWG == 4) {
+        uint32_t r[8];
+        tmem_ld8(tmem_ds + lane_addr, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          ra += __uint_as_float(r[2 * w]);
+          rb += __uint_as_float(r[2 * w + 1]);
+        }
+      } else {
+        uint32_t r[4];
+        tmem_ld4(tmem_ds + lane_addr, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          ra += __uint_as_float(r[2 * w]);
+          rb += __uint_as_float(r[2 * w + 1]);
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      tc_fence_after();
+      *sa = ra;
+      *sb = rb;
+    };
     if (NORM == HFAN_SOFTMAX1) {
       // c = O . dO (the implicit sink carries no value); warpgroup wg sums the
       // head-dim slice [HD/NWG wg, HD/NWG (wg + 1)), then the slices are combined.
@@ -285,13 +329,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           for (int e = 0; e < 8; ++e) acc = fmaf(to_f32<T>(oe[e]), to_f32<T>(de[e]), acc);
         }
       }
-      float* xc = reinterpret_cast<float*>(smem + L::DS);  // dS buffer: idle until the first dS write
-      xc[wg * 128 + row] = acc;
-      named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      c = 0.f;
-#pragma unroll
-      for (int w = 0; w < NWG; ++w) c += xc[w * 128 + row];
-      named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      float sum_unused;
+      row_exchange(acc, 0.f, &c, &sum_unused);
     }
     bool ok = true;
     uint32_t sdc = 0;
@@ -335,19 +374,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         }
         ++sdc;
       }
-      // combine the warpgroups' column sums (the dS buffer is idle until pass B)
-      float* xch = reinterpret_cast<float*>(smem + L::DS);
-      xch[(wg * 128 + row) * 2 + 0] = num;
-      xch[(wg * 128 + row) * 2 + 1] = den;
-      named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      num = 0.f;
-      den = 0.f;
-#pragma unroll
-      for (int w = 0; w < NWG; ++w) {
-        num += xch[(w * 128 + row) * 2];
-        den += xch[(w * 128 + row) * 2 + 1];
-      }
-      named_bar_sync(1, Roles<HD>::ROW_THREADS);
+      // combine the warpgroups' column sums
+      row_exchange(num, den, &num, &den);
       c = den > 0.f ? num / den : 0.f;
     }
     if (row_ok && wg == 0) p.corr[si] = c;
@@ -373,13 +401,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         }
       }
       ++sdc;
-      if (t > 0) {
-        if (!(ok = wait_warp(&bars->ds_empty, (t - 1) & 1, abort_flag))) break;
+      // dS(t) -> TMEM buffer t & 1, free once dQ(t - 2) has completed
+      const int db = t & 1;
+      if (t >= 2) {
+        if (!(ok = wait_warp(&bars->ds_empty[db], ((t >> 1) & 1) ^ 1, abort_flag))) break;
+        tc_fence_after();
       }
-      store_chunks_sw128<COLS / 8>(smem + L::DS, row, wg * (COLS / 8), pk);
-      fence_proxy_async_smem();
+#pragma unroll
+      for (int cc = 0; cc < CPW; ++cc) tmem_st16(tmem_ds + lane_addr + db * 64 + wg * (COLS / 2) + cc * 16, pk + cc * 16);
+      tmem_wait_st();
       tc_fence_before();
-      warp_arrive(&bars->ds_full);
+      warp_arrive(&bars->ds_full[db]);
     }
     if (ok && n_tiles > 0) {
       ok = wait_warp(&bars->dq_done, 0, abort_flag);
