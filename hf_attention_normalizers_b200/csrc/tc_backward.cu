@@ -335,20 +335,37 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     bool ok = true;
     uint32_t sdc = 0;
 
-    // Loads one 32-column chunk of S and dP; applies the visibility mask.
-    auto chunk = [&](int t, int cidx, float (&sv)[32], float (&dv)[32]) {
+    // Loads one 32-column chunk of S and dP as 16 packed pairs: x = s zs -
+    // st0 (one packed FMA per pair; masked keys -> -inf, applied only on
+    // tiles the mask cuts) and dP.
+    const uint64_t zs2 = f2_pack(zs, zs), nst2 = f2_pack(-st0, -st0), il2 = f2_pack(inv_l, inv_l);
+    auto chunk = [&](int t, int cidx, uint64_t (&x)[16], uint64_t (&dv)[16]) {
       uint32_t rs[32], rd[32];
       tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
       tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
       tmem_wait_ld();
+#pragma unroll
+      for (int jp = 0; jp < 16; ++jp) {
+        x[jp] = ffma2(f2_pack(__uint_as_float(rs[2 * jp]), __uint_as_float(rs[2 * jp + 1])), zs2, nst2);
+        dv[jp] = f2_pack(__uint_as_float(rd[2 * jp]), __uint_as_float(rd[2 * jp + 1]));
+      }
       const int kb = k_lo + t * kBN + cidx * 32;
       const int lo = vis_lo - kb, hi = vis_hi - kb;
-      const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= 32);
+      if (!__all_sync(0xffffffffu, lo <= 0 && hi >= 32)) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        sv[j] = (full || (j >= lo && j < hi)) ? __uint_as_float(rs[j]) * zs : kNegInf;
-        dv[j] = __uint_as_float(rd[j]);
+        for (int jp = 0; jp < 16; ++jp) {
+          const int j = 2 * jp;
+          x[jp] = f2_pack(j >= lo && j < hi ? f2_lo(x[jp]) : kNegInf,
+                          j + 1 >= lo && j + 1 < hi ? f2_hi(x[jp]) : kNegInf);
+        }
       }
+    };
+    // Weights of a pair (w = dp/dz up to the factor the normalizer's backward
+    // folds in): softmax1 p = 2^x / l, sparsemax 1[x > 0], entmax15 (x)_+.
+    auto wpair = [&](uint64_t x) -> uint64_t {
+      if (NORM == HFAN_SOFTMAX1) return fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il2);
+      if (NORM == HFAN_SPARSEMAX) return f2_pack(f2_lo(x) > 0.f ? 1.f : 0.f, f2_hi(x) > 0.f ? 1.f : 0.f);
+      return f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
     };
 
     if (SPARSE) {
@@ -356,22 +373,24 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       for (int t = 0; t < n_tiles && ok; ++t) {
         if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
         tc_fence_after();
+        uint64_t num2 = 0, den2 = 0;
 #pragma unroll
         for (int cc = 0; cc < CPW; ++cc) {
-          float sv[32], dv[32];
-          chunk(t, wg * CPW + cc, sv, dv);
+          uint64_t x[16], dv[16];
+          chunk(t, wg * CPW + cc, x, dv);
           if (cc == CPW - 1) {  // S and dP are in registers: the next tile's MMAs may overwrite them
             tc_fence_before();
             warp_arrive(&bars->sdp_empty);
           }
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float w, pr;
-            weight<NORM>(sv[j], st0, inv_l, &w, &pr);
-            num = fmaf(w, dv[j], num);
-            den += w;
+          for (int jp = 0; jp < 16; ++jp) {
+            const uint64_t w = wpair(x[jp]);
+            num2 = ffma2(w, dv[jp], num2);
+            den2 = fadd2(den2, w);
           }
         }
+        num += f2_lo(num2) + f2_hi(num2);
+        den += f2_lo(den2) + f2_hi(den2);
         ++sdc;
       }
       // combine the warpgroups' column sums
@@ -384,20 +403,25 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
       tc_fence_after();
       uint32_t pk[COLS / 2];
+      const uint64_t nc2 = f2_pack(-c, -c);
 #pragma unroll
       for (int cc = 0; cc < CPW; ++cc) {
-        float sv[32], dv[32];
-        chunk(t, wg * CPW + cc, sv, dv);
+        uint64_t x[16], dv[16];
+        chunk(t, wg * CPW + cc, x, dv);
         if (cc == CPW - 1) {  // S and dP are in registers: the next tile's MMAs may overwrite them
           tc_fence_before();
           warp_arrive(&bars->sdp_empty);
         }
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float w0, w1, p0, p1;
-          weight<NORM>(sv[j], st0, inv_l, &w0, &p0);
-          weight<NORM>(sv[j + 1], st0, inv_l, &w1, &p1);
-          pk[cc * 16 + j / 2] = pack2<BF16>(w0 * (dv[j] - c), w1 * (dv[j + 1] - c));
+        for (int jp = 0; jp < 16; ++jp) {
+          // dS = w (dP - c)
+          const uint64_t g2 = fadd2(dv[jp], nc2);
+          uint64_t d2;
+          if (NORM == HFAN_SPARSEMAX)
+            d2 = f2_pack(f2_lo(x[jp]) > 0.f ? f2_lo(g2) : 0.f, f2_hi(x[jp]) > 0.f ? f2_hi(g2) : 0.f);
+          else
+            d2 = fmul2(wpair(x[jp]), g2);
+          pk[cc * 16 + jp] = pack2<BF16>(f2_lo(d2), f2_hi(d2));
         }
       }
       ++sdc;
