@@ -693,10 +693,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       const int m = m_lo + u % n_m;
       const int qbase = m * kBM;
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      if (wg == 0) {
-        st0s[row] = na;
+      if (wg == 0) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
+        const float sg = NORM == HFAN_SOFTMAX1 ? -1.f : 1.f;
+        st0s[row] = sg * na;
         st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
-        crs[row] = nc;
+        crs[row] = sg * nc;
       }
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
       fetch(u + 1);
@@ -720,6 +721,37 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           tc_fence_before();
           warp_arrive(&bars->sdp_empty);
         }
+        if constexpr (NORM == HFAN_SOFTMAX1) {
+        const int lo = c_lo - cidx * 32, hi = c_hi - cidx * 32;
+        const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= 32);
+        const uint64_t zs2 = f2_pack(zs, zs);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          // statistics of query columns e, e+1 (broadcast 8-byte loads)
+          const int col = cidx * 32 + e;
+          const uint64_t nst = *reinterpret_cast<const uint64_t*>(st0s + col);
+          const uint64_t nc2 = *reinterpret_cast<const uint64_t*>(crs + col);
+          uint64_t x = ffma2(f2_pack(__uint_as_float(rs[e]), __uint_as_float(rs[e + 1])), zs2, nst);
+          if (!full)
+            x = f2_pack(e >= lo && e < hi ? f2_lo(x) : kNegInf, e + 1 >= lo && e + 1 < hi ? f2_hi(x) : kNegInf);
+          const uint64_t g2 = fadd2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), nc2);
+          uint64_t pr, ds;
+          if (NORM == HFAN_SOFTMAX1) {
+            const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
+            pr = fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il);
+            ds = fmul2(pr, g2);
+          } else if (NORM == HFAN_SPARSEMAX) {
+            pr = f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
+            ds = f2_pack(f2_lo(x) > 0.f ? f2_lo(g2) : 0.f, f2_hi(x) > 0.f ? f2_hi(g2) : 0.f);
+          } else {
+            const uint64_t d = f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
+            pr = fmul2(d, d);
+            ds = fmul2(d, g2);
+          }
+          ppk[cc * 16 + e / 2] = pack2<BF16>(f2_lo(pr), f2_hi(pr));
+          dpk[cc * 16 + e / 2] = pack2<BF16>(f2_lo(ds), f2_hi(ds));
+        }
+        } else {
         const int lo = c_lo - cidx * 32, hi = c_hi - cidx * 32;
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
@@ -735,6 +767,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           }
           ppk[cc * 16 + e / 2] = pack2<BF16>(pv[0], pv[1]);
           dpk[cc * 16 + e / 2] = pack2<BF16>(dsv[0], dsv[1]);
+        }
         }
       }
       // P^T, then dS^T, through the shared buffer
