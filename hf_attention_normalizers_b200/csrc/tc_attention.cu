@@ -258,6 +258,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #ifndef HFAN_VOTE_ITERS
 #define HFAN_VOTE_ITERS 3
 #endif
+#ifndef HFAN_VOTE_MARGIN
+#define HFAN_VOTE_MARGIN 20
+#endif
 #ifndef HFAN_VOTE_PERIOD
 #define HFAN_VOTE_PERIOD 4
 #endif
@@ -631,7 +634,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         // (Sparsemax supports stay far below the capacity: no vote.)
         if (NORM != HFAN_ENTMAX15) continue;
         if ((t % HFAN_VOTE_PERIOD) != HFAN_VOTE_PERIOD - 1 && t != n_tiles - 1) continue;
-        if (named_bar_or(1, NT, ok && cd.n > CAPW - 20 && !cd.overflow)) {
+        if (named_bar_or(1, NT, ok && cd.n > CAPW - HFAN_VOTE_MARGIN && !cd.overflow)) {
           float t0 = cd.thr;
 #pragma unroll
           for (int w = 0; w < NWG; ++w) t0 = fmaxf(t0, xb[w * 128 + row]);
