@@ -718,14 +718,35 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         }
         named_bar_sync(1, NT);
         if (ctl->next_pass != kPassSweep) break;
+        // Besides the sums above the bound, a pending row buffers every
+        // score above it again: once they fit (the bound is close to tau),
+        // the exact solve on the buffers ends the row's sweeps.
+        // (Only rows whose previous count above the bound suggests they fit.)
         TauStats st{0.f, 0.f, 0.f, kPosInf};
+        cd.n = 0;
+        const bool refill = __any_sync(0xffffffffu, pending && sweep > 0 && support <= 0.75f * CAPW * NWG);
         for (int t = 0; t < n_tiles && ok; ++t) {
           if (!(ok = load_s(t))) break;
           if (pending) {
+            if (refill) {
 #pragma unroll
-            for (int j = 0; j < COLS; ++j) tau_accumulate(st, sreg[j] * zs, lower);
+              for (int j = 0; j < COLS; ++j) {
+                const float z = sreg[j] * zs;
+                tau_accumulate(st, z, lower);
+                if (z > lower) {
+                  if (cd.n < CAPW) cbuf[cd.n * 128 + row] = z;
+                  ++cd.n;
+                }
+              }
+            } else {
+              cd.n = CAPW + 1;
+#pragma unroll
+              for (int j = 0; j < COLS; ++j) tau_accumulate(st, sreg[j] * zs, lower);
+            }
           }
         }
+        volatile float* xo = xch + 6144;  // [NWG][128]: this warpgroup's buffer overflowed
+        xo[wg * 128 + row] = cd.n > CAPW ? 1.f : 0.f;
         // combine the warpgroups' sums; all then take the same step
         float* xt = xch;  // [NWG][128 rows][4], free again once the merge above was read
         xt[(wg * 128 + row) * 4 + 0] = st.cnt;
@@ -742,8 +763,16 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           all.s2 += o[2];
           all.zmin = fminf(all.zmin, o[3]);
         }
+        bool fits = pending && ok;
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) fits = fits && xo[w * 128 + row] == 0.f;
         named_bar_sync(1, NT);
-        if (pending && ok) {
+        float tb, sb;
+        if (union_solve(cd, lower, fits, 64, &tb, &sb)) {
+          tau = tb;
+          support = sb;
+          pending = false;
+        } else if (pending && ok) {
           support = all.cnt;
           pending = !tau_step(NORM, all, &lower, &tau);
         }
