@@ -198,30 +198,50 @@ def run_ours(args, rank, world, local_rank):
                         "fwd_bwd_tflops": round(3.5 * flops_rank / (fwd + bwd) / 1e9, 1)}
 
     # End to end through the public API: pinned host inputs copied in every
-    # step, autograd forward + backward, loss read back to the host.
+    # step, autograd forward + backward, loss read back to the host.  The
+    # copy of step i + 1 runs on a copy stream into the other of two device
+    # buffers while step i computes (double-buffered input prefetch).
     pinned = {k: v.pin_memory() for k, v in host.items()}
     fns = {"sparsemax": kernels.hopper_sparsemax_attention, "entmax15": kernels.hopper_entmax15_attention}
+    bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in host.items()} for _ in range(2)]
+    copy_s = torch.cuda.Stream(dev)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        q = pinned["q"].to(dev, non_blocking=True).requires_grad_(True)
-        k = pinned["k"].to(dev, non_blocking=True).requires_grad_(True)
-        v = pinned["v"].to(dev, non_blocking=True).requires_grad_(True)
-        do = pinned["do"].to(dev, non_blocking=True)
-        loss = 0.0
-        for name in NORMS:
-            o = fns[name](q, k, v, is_causal=True)
-            o.backward(do)
-            loss = loss + (o.float() * do.float()).sum()
-        return float(loss.item())
+    def issue_copy(i):
+        b = i % 2
+        with torch.cuda.stream(copy_s):
+            copy_s.wait_event(free[b])  # the buffer's previous step has finished with it
+            for k in host:
+                bufs[b][k].copy_(pinned[k], non_blocking=True)
+            ready[b].record(copy_s)
 
-    e2e_step()
+    def e2e_steps(n):
+        issue_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            b = i % 2
+            torch.cuda.current_stream().wait_event(ready[b])
+            q = bufs[b]["q"].detach().requires_grad_(True)
+            k = bufs[b]["k"].detach().requires_grad_(True)
+            v = bufs[b]["v"].detach().requires_grad_(True)
+            do = bufs[b]["do"]
+            loss = 0.0
+            for name in NORMS:
+                o = fns[name](q, k, v, is_causal=True)
+                o.backward(do)
+                loss = loss + (o.float() * do.float()).sum()
+            free[b].record()
+            float(loss.item())
+
+    e2e_steps(2)
     barrier()
     t0 = time.perf_counter()
-    e2e_steps = max(1, min(args.steps, 3))
-    for _ in range(e2e_steps):
-        e2e_step()
+    e2e_steps_n = max(2, min(args.steps, 5))
+    e2e_steps(e2e_steps_n)
     barrier()
-    e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps_n
     e2e_t = torch.tensor([e2e_ms], device=dev)
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
@@ -262,7 +282,7 @@ def run_ours(args, rank, world, local_rank):
                      "traffic": traffic, "traffic_unit": "bytes per launch (ncu, small case x16)"},
         "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                "path": "kernels.hopper_{sparsemax,entmax15}_attention + autograd, pinned host inputs"},
+                "path": "kernels.hopper_{sparsemax,entmax15}_attention + autograd, pinned host inputs copied every step (copy stream, double-buffered prefetch of the next step)"},
         "gpu_launches": args.steps * len(NORMS) * 3,
         "clocks": sampler.summary(),
     }
