@@ -715,34 +715,92 @@ __device__ __forceinline__ float block_min(float v, float* red) {
 }
 
 // One CTA per (sequence, query head): exact tau of the staged score row.
+// tau >= zmax - 1, so only the scores above zmax - 1 matter; they are
+// compacted (in index order, through a block scan) into a short list that
+// one warp iterates on.  Rows with more candidates than the list holds use
+// the whole staged row.
+constexpr int kTauCand = 4096;
+
 template <int NORM>
 __global__ void __launch_bounds__(512) decode_sparse_tau(AttnParams p, DecodeWs ws, int max_len) {
   extern __shared__ float zrow[];
   __shared__ float red[32];
+  __shared__ float cand[kTauCand];
+  __shared__ int wcount[16];
+  __shared__ float result[2];
   const int b = blockIdx.y, hq = blockIdx.x;
   const int L = p.seq_lens[b];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* srow = ws.scores + ((int64_t)b * p.hq + hq) * max_len;
   float zmax = kNegInf;
-  for (int t = threadIdx.x; t < L; t += blockDim.x) {
+  for (int t = tid; t < L; t += blockDim.x) {
     const float z = srow[t];
     zrow[t] = z;
     zmax = fmaxf(zmax, z);
   }
   zmax = block_max(zmax, red);
-  float t = zmax - 1.f, tau = kPosInf, support = 0.f;
+  float tau = kPosInf, support = 0.f;
   if (zmax > kNegInf) {
-    for (int it = 0; it < 64; ++it) {
-      TauStats st{0.f, 0.f, 0.f, kPosInf};
-      for (int j = threadIdx.x; j < L; j += blockDim.x) tau_accumulate(st, zrow[j], t);
-      st.cnt = block_sum(st.cnt, red);
-      st.s1 = block_sum(st.s1, red);
-      st.s2 = block_sum(st.s2, red);
-      st.zmin = block_min(st.zmin, red);
-      support = st.cnt;
-      if (tau_step(NORM, st, &t, &tau)) break;  // uniform: every thread sees the same sums
+    const float t0 = zmax - 1.f;
+    // thread tid owns the contiguous slice [tid * per, (tid + 1) * per)
+    const int per = (L + blockDim.x - 1) / blockDim.x;
+    const int j0 = min(L, tid * per), j1 = min(L, j0 + per);
+    int mine = 0;
+    for (int j = j0; j < j1; ++j) mine += zrow[j] > t0 ? 1 : 0;
+    // exclusive scan of the per-thread counts
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) wcount[warp] = incl;
+    __syncthreads();
+    int wbase = 0, total = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      if (w < warp) wbase += wcount[w];
+      total += wcount[w];
+    }
+    if (total <= kTauCand) {
+      int pos = wbase + incl - mine;
+      for (int j = j0; j < j1; ++j)
+        if (zrow[j] > t0) cand[pos++] = zrow[j];
+      __syncthreads();
+      if (warp == 0) {
+        float t = t0, tr = kPosInf, sup = 0.f;
+        for (int it = 0; it < 64; ++it) {
+          TauStats st{0.f, 0.f, 0.f, kPosInf};
+          for (int j = lane; j < total; j += 32) tau_accumulate(st, cand[j], t);
+          st.cnt = warp_sum(st.cnt);
+          st.s1 = warp_sum(st.s1);
+          st.s2 = warp_sum(st.s2);
+          st.zmin = warp_min(st.zmin);
+          sup = st.cnt;
+          if (tau_step(NORM, st, &t, &tr)) break;  // uniform: every lane holds the same sums
+        }
+        if (lane == 0) {
+          result[0] = tr;
+          result[1] = sup;
+        }
+      }
+      __syncthreads();
+      tau = result[0];
+      support = result[1];
+    } else {
+      float t = t0;
+      for (int it = 0; it < 64; ++it) {
+        TauStats st{0.f, 0.f, 0.f, kPosInf};
+        for (int j = tid; j < L; j += blockDim.x) tau_accumulate(st, zrow[j], t);
+        st.cnt = block_sum(st.cnt, red);
+        st.s1 = block_sum(st.s1, red);
+        st.s2 = block_sum(st.s2, red);
+        st.zmin = block_min(st.zmin, red);
+        support = st.cnt;
+        if (tau_step(NORM, st, &t, &tau)) break;  // uniform: every thread sees the same sums
+      }
     }
   }
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     ws.tau[(int64_t)b * p.hq + hq] = tau;
     const int64_t si = (int64_t)hq * p.rows_total + b;
     p.stats[si] = tau;
@@ -750,16 +808,18 @@ __global__ void __launch_bounds__(512) decode_sparse_tau(AttnParams p, DecodeWs 
   }
 }
 
+// The warp reads the scores of 32 keys at a time (coalesced, every head of
+// the group), ballots the keys with a nonzero probability for some head and
+// reads V rows only for those; lane l accumulates head dims [D/32 l, D/32 (l+1)).
 template <typename T, int D, int G, int NORM>
 __global__ void __launch_bounds__(256) decode_sparse_pv(AttnParams p, DecodeWs ws, int max_len) {
-  using LN = Lanes<D>;
+  constexpr int DL = D / 32;  // dims per lane (4 or 2)
   const int b = blockIdx.y, split = blockIdx.x;
   const int L = p.seq_lens[b];
   const int t0 = split * kChunk;
   if (t0 >= L) return;
   const int t1 = min(L, t0 + kChunk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int sub = lane / LN::LPT, li = lane % LN::LPT;
   const int* bt = page_row(p, b);
   const T* vp = static_cast<const T*>(p.v);
   for (int kvh = warp; kvh < p.hkv; kvh += nwarps) {
@@ -767,44 +827,53 @@ __global__ void __launch_bounds__(256) decode_sparse_pv(AttnParams p, DecodeWs w
 #pragma unroll
     for (int h = 0; h < G; ++h) tau[h] = ws.tau[(int64_t)b * p.hq + kvh * G + h];
     const float* srow = ws.scores + ((int64_t)b * p.hq + kvh * G) * max_len;
-    float acc[G][8];
+    float acc[G][DL];
 #pragma unroll
     for (int h = 0; h < G; ++h)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[h][i] = 0.f;
-    for (int t = t0 + sub; t < t1; t += LN::TPW) {  // no shuffles inside: per-group bound is fine
+      for (int i = 0; i < DL; ++i) acc[h][i] = 0.f;
+    for (int tb = t0; tb < t1; tb += 32) {  // warp-uniform bound (ballots, shuffles)
+      const int t = tb + lane;
       float pr[G];
       bool any = false;
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        pr[h] = sparse_prob(NORM, srow[(int64_t)h * max_len + t], tau[h]);
+        pr[h] = t < t1 ? sparse_prob(NORM, srow[(int64_t)h * max_len + t], tau[h]) : 0.f;
         any |= pr[h] > 0.f;
       }
-      if (!any) continue;
-      const int64_t tok = phys_token(p, bt, t);
-      if (tok < 0) continue;
-      float vx[8];
-      load8<T>(vp + tok * p.v_st + (int64_t)kvh * p.v_sh + li * 8, vx);
+      unsigned mask = __ballot_sync(0xffffffffu, any);
+      while (mask) {
+        const int src = __ffs(mask) - 1;
+        mask &= mask - 1;
+        float ps[G];
 #pragma unroll
-      for (int h = 0; h < G; ++h)
+        for (int h = 0; h < G; ++h) ps[h] = __shfl_sync(0xffffffffu, pr[h], src);
+        const int64_t tok = phys_token(p, bt, tb + src);
+        if (tok < 0) continue;
+        const T* vr = vp + tok * p.v_st + (int64_t)kvh * p.v_sh + lane * DL;
+        float vx[DL];
+        if constexpr (DL == 4) {
+          const uint2 u = *reinterpret_cast<const uint2*>(vr);
+          const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[h][i] = fmaf(pr[h], vx[i], acc[h][i]);
-    }
+          for (int i = 0; i < 4; ++i) vx[i] = to_f32<T>(e[i]);
+        } else {
+          const uint32_t u = *reinterpret_cast<const uint32_t*>(vr);
+          const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-    for (int o = LN::LPT; o < 32; o <<= 1)
+          for (int i = 0; i < DL; ++i) vx[i] = to_f32<T>(e[i]);
+        }
 #pragma unroll
-      for (int h = 0; h < G; ++h)
+        for (int h = 0; h < G; ++h)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], o);
-    if (sub == 0) {
-      const int64_t unit = ((int64_t)b * p.hkv + kvh) * ws.splits + split;
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float4* dst = reinterpret_cast<float4*>(ws.acc + (unit * G + h) * D + li * 8);
-        dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-        dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+          for (int i = 0; i < DL; ++i) acc[h][i] = fmaf(ps[h], vx[i], acc[h][i]);
       }
     }
+    const int64_t unit = ((int64_t)b * p.hkv + kvh) * ws.splits + split;
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+      for (int i = 0; i < DL; ++i) ws.acc[(unit * G + h) * D + lane * DL + i] = acc[h][i];
   }
 }
 
