@@ -38,7 +38,7 @@ namespace {
 
 constexpr int kChunk = 1024;   // keys per split
 constexpr int kUnroll = 4;      // key rows in flight per lane group
-constexpr int kMaxRow = 32768; // tau kernel stages at most this many keys per row
+constexpr int kMaxRow = 32768; // longest row the split decode serves (score workspace per row)
 
 struct DecodeWs {
   float* acc;     // [B, Hkv, splits, G, D]
@@ -714,16 +714,15 @@ __device__ __forceinline__ float block_min(float v, float* red) {
   return r;
 }
 
-// One CTA per (sequence, query head): exact tau of the staged score row.
+// One CTA per (sequence, query head): exact tau of the score row.
 // tau >= zmax - 1, so only the scores above zmax - 1 matter; they are
-// compacted (in index order, through a block scan) into a short list that
-// one warp iterates on.  Rows with more candidates than the list holds use
-// the whole staged row.
+// compacted (in index order, through a block scan) into a short shared-memory
+// list that one warp iterates on.  Rows with more candidates than the list
+// holds iterate over the whole row in global memory.
 constexpr int kTauCand = 4096;
 
 template <int NORM>
 __global__ void __launch_bounds__(512) decode_sparse_tau(AttnParams p, DecodeWs ws, int max_len) {
-  extern __shared__ float zrow[];
   __shared__ float red[32];
   __shared__ float cand[kTauCand];
   __shared__ int wcount[16];
@@ -732,12 +731,9 @@ __global__ void __launch_bounds__(512) decode_sparse_tau(AttnParams p, DecodeWs 
   const int L = p.seq_lens[b];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* srow = ws.scores + ((int64_t)b * p.hq + hq) * max_len;
+  const float* zrow = srow;
   float zmax = kNegInf;
-  for (int t = tid; t < L; t += blockDim.x) {
-    const float z = srow[t];
-    zrow[t] = z;
-    zmax = fmaxf(zmax, z);
-  }
+  for (int t = tid; t < L; t += blockDim.x) zmax = fmaxf(zmax, srow[t]);
   zmax = block_max(zmax, red);
   float tau = kPosInf, support = 0.f;
   if (zmax > kNegInf) {
@@ -952,21 +948,15 @@ cudaError_t run(const AttnParams& p, int max_len, void* workspace, cudaStream_t 
     decode_sm1_combine<T, D, G><<<grid_r, D, 0, s>>>(p, ws);
     return cudaGetLastError();
   }
-  const size_t tau_smem = (size_t)max_len * sizeof(float);
-  cudaError_t e;
   if (p.norm == HFAN_SPARSEMAX) {
-    e = cudaFuncSetAttribute(decode_sparse_tau<HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tau_smem);
-    if (e != cudaSuccess) return e;
     if (!launch_scores_tiled<T, D, G, HFAN_SPARSEMAX>(p, ws, max_len, grid_u, s))
       decode_sparse_scores<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
-    decode_sparse_tau<HFAN_SPARSEMAX><<<grid_r, 512, tau_smem, s>>>(p, ws, max_len);
+    decode_sparse_tau<HFAN_SPARSEMAX><<<grid_r, 512, 0, s>>>(p, ws, max_len);
     decode_sparse_pv<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
   } else {
-    e = cudaFuncSetAttribute(decode_sparse_tau<HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tau_smem);
-    if (e != cudaSuccess) return e;
     if (!launch_scores_tiled<T, D, G, HFAN_ENTMAX15>(p, ws, max_len, grid_u, s))
       decode_sparse_scores<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
-    decode_sparse_tau<HFAN_ENTMAX15><<<grid_r, 512, tau_smem, s>>>(p, ws, max_len);
+    decode_sparse_tau<HFAN_ENTMAX15><<<grid_r, 512, 0, s>>>(p, ws, max_len);
     decode_sparse_pv<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
   }
   decode_sparse_combine<T, D, G><<<grid_r, D, 0, s>>>(p, ws);
