@@ -236,7 +236,11 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
     if (z > c.thr) buf[live++ * 128 + row] = z;
   }
   c.n = live;
-  if (live > cap - 12) c.overflow = true;  // compaction no longer frees room for a chunk of appends
+  // Stop buffering once compaction no longer frees room for a chunk of
+  // appends.  Sparsemax (no cooperative vote) also stops when half the
+  // buffer stays live: the row's candidates are dense, and compacting on
+  // every chunk would cost more than the sweeps that settle such rows.
+  if (live > (NORM == HFAN_SPARSEMAX ? cap / 2 : cap - 12)) c.overflow = true;
   return c;
 }
 
