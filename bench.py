@@ -290,6 +290,12 @@ def run_ours(args, rank, world, local_rank):
         line["paged_decode"] = bench_decode(dev, hbm)
         line["varlen"] = bench_varlen(dev)
         line["prescaled_worst_case"] = bench_prescaled(t, flops_rank)
+        del t
+        torch.cuda.empty_cache()
+        try:
+            line["model_step"] = bench_model(dev)
+        except Exception as exc:  # the prefill/decode line above stands on its own
+            line["model_step"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     if args.cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
     return line
@@ -422,6 +428,91 @@ def bench_prescaled(t, flops, norms=NORMS):
     return out
 
 
+def bench_model(dev, steps=3, warmup=2):
+    """BASELINE configs[4], one data-parallel replica: Qwen3-1.7B-shaped
+    model (28 layers, hidden 2048, 16 query / 8 KV heads, D=128), random init
+    (seed 0), bf16, one sequence of 4096 random tokens; a training step =
+    forward + LM loss + backward + AdamW step.  Reports tokens/s per
+    normalizer routed through set_softmax_attention_backend(..., "sdpa"),
+    HF's own SDPA softmax as the reference point, the number of fused
+    attention calls per step, and the attention share (the fused kernels
+    timed alone at the model's shapes x 28 layers / step time)."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    from hf_attention_normalizers_b200 import _native as N
+    from hf_attention_normalizers_b200 import backends, ops
+
+    cfg = Qwen3Config(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, intermediate_size=6144, vocab_size=151936, rope_theta=1e6,
+                      max_position_embeddings=8192)
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = Qwen3ForCausalLM(cfg)
+    torch.set_default_dtype(prev)
+    model.train()
+    seq = 4096
+    ids = torch.randint(0, cfg.vocab_size, (1, seq), generator=torch.Generator().manual_seed(0)).to(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-5, foreach=True)
+    calls = {"n": 0}
+    real_fwd = ops.attn_fwd
+
+    def counting_fwd(*a, **k):
+        calls["n"] += 1
+        return real_fwd(*a, **k)
+
+    def step():
+        loss = model(input_ids=ids, labels=ids).loss
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    out = {"config": "BASELINE configs[4] (one replica)", "tokens_per_step": seq}
+    ops.attn_fwd = counting_fwd
+    try:
+        for norm in ("hf_sdpa_softmax", "softmax1", "sparsemax", "entmax15"):
+            if norm == "hf_sdpa_softmax":
+                model.config._attn_implementation = "sdpa"
+            else:
+                backends.set_softmax_attention_backend(model, "sdpa", norm)
+            for _ in range(warmup):
+                step()
+            torch.cuda.synchronize()
+            calls["n"] = 0
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            res = {"ms_per_step": round(ms, 2), "tokens_per_s": round(seq / ms * 1e3, 1),
+                   "fused_attention_calls_per_step": calls["n"] // steps}
+            if norm != "hf_sdpa_softmax":
+                nid = N.NORMALIZER_IDS[norm]
+                q = torch.randn(1, 16, seq, 128, device=dev, dtype=torch.bfloat16)
+                k = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
+                v = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
+                o, st = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                ops.attn_bwd(q, q, k, v, o, st, nid, 128 ** -0.5, True, -1)
+                torch.cuda.synchronize()
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record()
+                for _ in range(28):
+                    o, st = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                    ops.attn_bwd(q, q, k, v, o, st, nid, 128 ** -0.5, True, -1)
+                a1.record()
+                torch.cuda.synchronize()
+                res["attention_ms"] = round(a0.elapsed_time(a1), 2)
+                res["attention_share"] = round(a0.elapsed_time(a1) / ms, 3)
+            out[norm] = res
+    finally:
+        ops.attn_fwd = real_fwd
+    return out
+
+
 # --------------------------------------------------------------------------- CPU
 def cpu_sample(threads: int, rows: int):
     """One bounded sample of the workload through the CPU oracle.
@@ -505,6 +596,8 @@ def main():
     ap.add_argument("--decode-norms", default="softmax1,sparsemax,entmax15")
     ap.add_argument("--shape", default=None,
                     help="B,S,HQ,HKV override for small profiling cases (default: the BASELINE config)")
+    ap.add_argument("--model-step", action="store_true",
+                    help="only run the Qwen3-1.7B training-step measurement (BASELINE configs[4])")
     ap.add_argument("--profile-case", action="store_true",
                     help="run warmup+steps of the step only (no e2e, no phases): for ncu captures")
     args = ap.parse_args()
@@ -512,6 +605,11 @@ def main():
         global B, S, HQ, HKV
         B, S, HQ, HKV = (int(x) for x in args.shape.split(","))
 
+    if args.model_step:
+        import torch
+
+        print(json.dumps(bench_model(torch.device("cuda", 0))), flush=True)
+        return
     if args.decode_only:
         import torch
 
