@@ -26,6 +26,10 @@ size_t decode_static_scratch_bytes();
 cudaError_t decode_static_scratch(void** out);
 cudaError_t tc_attention_fwd(int dtype, const AttnParams& p, int max_q, cudaStream_t s);
 cudaError_t tc_attention_bwd(int dtype, const AttnParams& p, int max_q, int max_k, cudaStream_t s);
+// Paged prefill / backward through the tensor-core kernels (paged_tc.cu);
+// cudaErrorNotSupported when the shape is outside their envelope.
+cudaError_t paged_tc_fwd(int dtype, const AttnParams& p, cudaStream_t s);
+cudaError_t paged_tc_bwd(int dtype, const AttnParams& p, cudaStream_t s);
 }  // namespace hfan
 
 using namespace hfan;
@@ -240,7 +244,8 @@ int hfan_paged_fwd(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_c
   p.stats = stats;
   if (desc->len_q == 0 || desc->max_len_k == 0) return HFAN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = simt_attention_fwd(desc->dtype, p, desc->len_q, s);
+  cudaError_t e = paged_tc_fwd(desc->dtype, p, s);
+  if (e == cudaErrorNotSupported) e = simt_attention_fwd(desc->dtype, p, desc->len_q, s);
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_paged_fwd");
 }
 
@@ -256,7 +261,8 @@ int hfan_paged_bwd(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_c
   p.corr = corr;
   if (desc->len_q == 0 || desc->max_len_k == 0) return HFAN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = simt_attention_bwd(desc->dtype, p, desc->len_q, desc->max_len_k, s);
+  cudaError_t e = paged_tc_bwd(desc->dtype, p, s);
+  if (e == cudaErrorNotSupported) e = simt_attention_bwd(desc->dtype, p, desc->len_q, desc->max_len_k, s);
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_paged_bwd");
 }
 

@@ -38,6 +38,7 @@ struct AttnParams {
   int page_size, max_blocks;
   int64_t num_cache_tokens;
   int paged;
+  int lens_only;           // dense K/V whose per-sequence key lengths come from seq_lens
 
   float scale;
   int causal, window_left, norm;
@@ -56,7 +57,7 @@ __device__ __forceinline__ Geometry geometry(const AttnParams& p, int b) {
     g.q_start = b * p.len_q;
     g.q_len = p.len_q;
     g.k_start = 0;
-    g.k_len = p.paged ? p.seq_lens[b] : p.len_k;
+    g.k_len = (p.paged || p.lens_only) ? p.seq_lens[b] : p.len_k;
   }
   return g;
 }
