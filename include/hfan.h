@@ -132,7 +132,9 @@ typedef struct hfan_paged_desc {
  * their gradients: stride_batch is ignored, stride_token / stride_head address
  * [num_cache_tokens, heads_kv, D].  Stats as for hfan_attn_fwd with rows =
  * batch*len_q.  dk/dv must be zero-filled float32: pages shared between
- * sequences accumulate. */
+ * sequences accumulate.  16-bit caches with head_dim 64/128 and len_q > 1 run
+ * on the tensor-core kernels (pages gathered into stream-ordered scratch,
+ * released on `stream`); other shapes on the general kernels. */
 int hfan_paged_fwd(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_cache,
                    hfan_tensor value_cache, hfan_tensor o, float* stats, void* stream);
 
