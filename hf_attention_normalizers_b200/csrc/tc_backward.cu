@@ -482,10 +482,20 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 }
 
 // =========================================================== dk/dv kernel
+// One CTA per 128-key tile; units = (query head of the KV group, 64-row query
+// tile).  Per unit: S^T = K Q^T and dP^T = V dO^T (M = 128 keys, N = 64
+// queries) into one of two TMEM buffers, so that the next unit's products run
+// while the row warps turn this unit's into P^T and dS^T; those go to two
+// separate shared-memory tiles for dV += P^T dO and dK += dS^T Q (K = 64).
+// Q / dO tiles (64 rows) stream through a 4-stage ring.
+constexpr int kQB = 64;        // query rows per unit
+constexpr int kQStages = 4;    // Q / dO ring depth
+constexpr uint32_t kQHalf = kQB * 128u;  // one 64-row x 128-byte swizzled half tile
+
 struct KBars {
   uint64_t kv_full;
-  uint64_t qd_full[2], qd_empty[2];
-  uint64_t sdp_full, sdp_empty, pb_full, pb_empty, done;
+  uint64_t qd_full[kQStages], qd_empty[kQStages];
+  uint64_t sdp_full[2], sdp_empty[2], p_full, p_empty, done;
 };
 
 template <int HD>
@@ -493,11 +503,12 @@ struct KLayout {
   static constexpr int NH = HD / 64;
   static constexpr uint32_t K = 0;
   static constexpr uint32_t V = K + NH * kHalf;
-  static constexpr uint32_t Q = V + NH * kHalf;        // 2 stages
-  static constexpr uint32_t DO = Q + 2 * NH * kHalf;   // 2 stages
-  static constexpr uint32_t PB = DO + 2 * NH * kHalf;  // P^T, then dS^T
-  static constexpr uint32_t STATS = PB + 2 * kHalf;    // 3 x 128 floats
-  static constexpr uint32_t BARS = STATS + 3 * 128 * 4;
+  static constexpr uint32_t Q = V + NH * kHalf;                  // kQStages stages
+  static constexpr uint32_t DO = Q + kQStages * NH * kQHalf;     // kQStages stages
+  static constexpr uint32_t PP = DO + kQStages * NH * kQHalf;    // P^T  [128 keys][64 queries]
+  static constexpr uint32_t PD = PP + kHalf;                     // dS^T [128 keys][64 queries]
+  static constexpr uint32_t STATS = PD + kHalf;                  // 3 x 64 floats
+  static constexpr uint32_t BARS = STATS + 3 * kQB * 4;
   static constexpr uint32_t CTL = BARS + sizeof(KBars);
   static constexpr uint32_t TOTAL = CTL + 16 + 1024;
 };
@@ -510,9 +521,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   using L = KLayout<HD>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr int NH = L::NH;
-  constexpr uint32_t TILE = NH * kHalf;
-  constexpr uint32_t IDESC_S = idesc_f16(BF16, kBM, kBN, false, false);
-  constexpr uint32_t IDESC_ACC = idesc_f16(BF16, kBM, HD, false, true);
+  constexpr uint32_t TILE = NH * kHalf;     // K or V tile
+  constexpr uint32_t QTILE = NH * kQHalf;   // Q or dO tile (64 rows)
+  constexpr uint32_t IDESC_S = idesc_f16(BF16, kBN, kQB, false, false);
+  constexpr uint32_t IDESC_ACC = idesc_f16(BF16, kBN, HD, false, true);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -521,8 +533,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   int* abort_ptr = reinterpret_cast<int*>(smem + L::CTL + 4);
   volatile int* abort_flag = abort_ptr;
   float* st0s = reinterpret_cast<float*>(smem + L::STATS);
-  float* st1s = st0s + 128;
-  float* crs = st1s + 128;
+  float* st1s = st0s + kQB;
+  float* crs = st1s + kQB;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, kvh = blockIdx.y;
@@ -541,21 +553,23 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   if (p.causal) i_lo = max(0, k0 - off);
   int i_hi = g.q_len;
   if (p.window_left > 0) i_hi = min(i_hi, min(k0 + kBN, g.k_len) - 1 - off + p.window_left);
-  const int m_lo = i_lo / kBM;
-  const int m_hi = i_hi > i_lo ? (i_hi + kBM - 1) / kBM : m_lo;
+  const int m_lo = i_lo / kQB;
+  const int m_hi = i_hi > i_lo ? (i_hi + kQB - 1) / kQB : m_lo;
   const int n_m = m_hi - m_lo;
   const int n_units = groups * n_m;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kQStages; ++s) {
       mbar_init(&bars->qd_full[s], 1);
       mbar_init(&bars->qd_empty[s], 1);
     }
-    mbar_init(&bars->sdp_full, 1);
-    mbar_init(&bars->sdp_empty, Roles<HD>::ROW_THREADS / 32);
-    mbar_init(&bars->pb_full, Roles<HD>::ROW_THREADS / 32);
-    mbar_init(&bars->pb_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->sdp_full[s], 1);
+      mbar_init(&bars->sdp_empty[s], Roles<HD>::ROW_THREADS / 32);
+    }
+    mbar_init(&bars->p_full, Roles<HD>::ROW_THREADS / 32);
+    mbar_init(&bars->p_empty, 1);
     mbar_init(&bars->done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
@@ -565,6 +579,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // TMEM: S^T buffers [0, 64) and [64, 128), dP^T buffers [128, 192) and
+  // [192, 256), dV [256, 256 + HD), dK [256 + HD, 256 + 2 HD)
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dv = tmem + 256, tmem_dk = tmem + 256 + HD;
 
   if (warp == Roles<HD>::TMA_WARP) {
@@ -582,12 +598,14 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       for (int u = 0; u < n_units && ok; ++u) {
         const int hq = kvh * groups + u / n_m;
         const int m = m_lo + u % n_m;
-        const int s = u & 1;
-        if (!(ok = mbar_wait(&bars->qd_empty[s], ((u >> 1) & 1) ^ 1, abort_flag))) break;
-        mbar_arrive_expect_tx(&bars->qd_full[s], 2 * TILE);
+        const int s = u % kQStages;
+        if (!(ok = mbar_wait(&bars->qd_empty[s], ((u / kQStages) & 1) ^ 1, abort_flag))) break;
+        mbar_arrive_expect_tx(&bars->qd_full[s], 2 * QTILE);
         for (int hh = 0; hh < NH; ++hh) {
-          tma_load_4d(smem + L::Q + s * TILE + hh * kHalf, &tm_q, &bars->qd_full[s], 64 * hh, qtok0 + m * kBM, hq, bcoord);
-          tma_load_4d(smem + L::DO + s * TILE + hh * kHalf, &tm_do, &bars->qd_full[s], 64 * hh, qtok0 + m * kBM, hq, bcoord);
+          tma_load_4d(smem + L::Q + s * QTILE + hh * kQHalf, &tm_q, &bars->qd_full[s], 64 * hh, qtok0 + m * kQB, hq,
+                      bcoord);
+          tma_load_4d(smem + L::DO + s * QTILE + hh * kQHalf, &tm_do, &bars->qd_full[s], 64 * hh, qtok0 + m * kQB,
+                      hq, bcoord);
         }
       }
       if (!ok) {
@@ -596,29 +614,29 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       }
     }
   } else if (warp == Roles<HD>::MMA_WARP) {
-    // S^T and dP^T issuer; dV / dK have their own issuer warp.
+    // S^T and dP^T issuer
     if (lane == 0 && n_units > 0) {
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       bool ok = mbar_wait(&bars->kv_full, 0, abort_flag);
       for (int u = 0; u < n_units && ok; ++u) {
-        const int s = u & 1;
-        if (!(ok = mbar_wait(&bars->qd_full[s], (u >> 1) & 1, abort_flag))) break;
-        if (!(ok = mbar_wait(&bars->sdp_empty, (u & 1) ^ 1, abort_flag))) break;
+        const int s = u % kQStages, bf = u & 1;
+        if (!(ok = mbar_wait(&bars->qd_full[s], (u / kQStages) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(&bars->sdp_empty[bf], ((u >> 1) & 1) ^ 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t o = (kk >> 2) * kHalf + (kk & 3) * 32;
-          mma_f16_ss(tmem_s, sw128_desc(k_base + o, 16, 1024), sw128_desc(q_base + s * TILE + o, 16, 1024),
+          const uint32_t o = (kk >> 2) * kHalf + (kk & 3) * 32, oq = (kk >> 2) * kQHalf + (kk & 3) * 32;
+          mma_f16_ss(tmem_s + bf * kQB, sw128_desc(k_base + o, 16, 1024), sw128_desc(q_base + s * QTILE + oq, 16, 1024),
                      IDESC_S, kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t o = (kk >> 2) * kHalf + (kk & 3) * 32;
-          mma_f16_ss(tmem_dp, sw128_desc(v_base + o, 16, 1024), sw128_desc(do_base + s * TILE + o, 16, 1024),
-                     IDESC_S, kk > 0);
+          const uint32_t o = (kk >> 2) * kHalf + (kk & 3) * 32, oq = (kk >> 2) * kQHalf + (kk & 3) * 32;
+          mma_f16_ss(tmem_dp + bf * kQB, sw128_desc(v_base + o, 16, 1024),
+                     sw128_desc(do_base + s * QTILE + oq, 16, 1024), IDESC_S, kk > 0);
         }
-        mma_commit(&bars->sdp_full);
+        mma_commit(&bars->sdp_full[bf]);
       }
       if (!ok) {
         *abort_ptr = 1;
@@ -626,30 +644,31 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       }
     }
   } else if (warp == Roles<HD>::MMA2_WARP) {
-    // dV += P^T dO, then dK += dS^T Q, for every unit; the unit's Q / dO stage
-    // is released after both (its S^T / dP^T MMAs completed before P^T existed).
+    // dV += P^T dO and dK += dS^T Q per unit; then the P^T / dS^T tiles and
+    // the unit's Q / dO stage are free (the unit's S^T / dP^T products
+    // completed before P^T existed).
     if (lane == 0 && n_units > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
-      const uint32_t pb_base = smem_u32(smem + L::PB);
+      const uint32_t pp_base = smem_u32(smem + L::PP), pd_base = smem_u32(smem + L::PD);
       bool ok = true;
-      uint32_t pbc = 0;
       for (int u = 0; u < n_units && ok; ++u) {
-        const int s = u & 1;
-        for (int which = 0; which < 2 && ok; ++which) {
-          if (!(ok = mbar_wait(&bars->pb_full, pbc & 1, abort_flag))) break;
-          tc_fence_after();
-          const uint32_t bsrc = (which == 0 ? do_base : q_base) + s * TILE;
-          const uint32_t dst = which == 0 ? tmem_dv : tmem_dk;
+        const int s = u % kQStages;
+        if (!(ok = mbar_wait(&bars->p_full, u & 1, abort_flag))) break;
+        tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk) {
-            const uint64_t a = sw128_desc(pb_base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(bsrc + kk * 16 * 128, kHalf, 1024);
-            mma_f16_ss(dst, a, bd, IDESC_ACC, u > 0 || kk > 0);
-          }
-          mma_commit(&bars->pb_empty);
-          ++pbc;
+        for (int kk = 0; kk < kQB / 16; ++kk) {
+          // A = P^T / dS^T [128 keys x 64 queries], K-major; B = dO / Q tile,
+          // MN-major (rows = queries, 64-wide head-dim blocks kQHalf apart)
+          const uint64_t bo = sw128_desc(do_base + s * QTILE + kk * 16 * 128, kQHalf, 1024);
+          mma_f16_ss(tmem_dv, sw128_desc(pp_base + kk * 32, 16, 1024), bo, IDESC_ACC, u > 0 || kk > 0);
         }
-        if (ok) mma_commit(&bars->qd_empty[s]);
+#pragma unroll
+        for (int kk = 0; kk < kQB / 16; ++kk) {
+          const uint64_t bq = sw128_desc(q_base + s * QTILE + kk * 16 * 128, kQHalf, 1024);
+          mma_f16_ss(tmem_dk, sw128_desc(pd_base + kk * 32, 16, 1024), bq, IDESC_ACC, u > 0 || kk > 0);
+        }
+        mma_commit(&bars->p_empty);
+        mma_commit(&bars->qd_empty[s]);
       }
       if (ok) mma_commit(&bars->done);
       if (!ok) {
@@ -659,8 +678,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     }
   } else {
     constexpr int NWG = Roles<HD>::NWG;
-    constexpr int COLS = kBM / NWG;  // query columns per warpgroup
-    constexpr int CPW = COLS / 32;
+    constexpr int COLS = kQB / NWG;  // query columns per warpgroup (16 for HD = 128)
     const int wg = warp >> 2;         // warpgroup wg owns query columns [COLS wg, COLS (wg + 1))
     const int row = threadIdx.x & 127;  // key within the tile
     const int j = k0 + row;
@@ -668,19 +686,18 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const float zs = zscale<NORM>(p.scale);
     bool ok = true;
-    uint32_t pbc = 0;
     // The named barriers run on every iteration, even after a timeout, so that
     // no warp waits for one that has left the loop.
-    // Row statistics of a unit's 128 query rows: warpgroup 0 loads those of
-    // the next unit into registers while this one is processed, and stages
-    // them in shared memory between two barriers at the unit's start.
+    // Row statistics of a unit's 64 query rows: warpgroup 0 loads those of the
+    // next unit into registers while this one is processed, and stages them in
+    // shared memory between two barriers at the unit's start.
     float na = kPosInf, nb = 1.f, nc = 0.f;
     auto fetch = [&](int u_) {
       na = kPosInf;
       nb = 1.f;
       nc = 0.f;
-      if (wg != 0 || u_ >= n_units) return;
-      const int iq = (m_lo + u_ % n_m) * kBM + row;
+      if (wg != 0 || row >= kQB || u_ >= n_units) return;
+      const int iq = (m_lo + u_ % n_m) * kQB + row;
       if (iq < g.q_len) {
         const int64_t si = stat_index(p, g, kvh * groups + u_ / n_m, iq);
         na = p.stats[si];
@@ -691,9 +708,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     fetch(0);
     for (int u = 0; u < n_units; ++u) {
       const int m = m_lo + u % n_m;
-      const int qbase = m * kBM;
+      const int qbase = m * kQB;
+      const int bf = u & 1;
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      if (wg == 0) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
+      if (wg == 0 && row < kQB) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
         const float sg = NORM == HFAN_SOFTMAX1 ? -1.f : 1.f;
         st0s[row] = sg * na;
         st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
@@ -702,85 +720,72 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
       fetch(u + 1);
       if (!ok) continue;
-      if (!(ok = wait_warp(&bars->sdp_full, u & 1, abort_flag))) continue;
+      if (!(ok = wait_warp(&bars->sdp_full[bf], (u >> 1) & 1, abort_flag))) continue;
       tc_fence_after();
       // visible queries of this key: [c_lo, c_hi) relative to qbase
       const int jl = j - off;  // causal: query i sees key j iff i >= j - off
       int c_lo = p.causal ? jl - qbase : -1 << 30;
       int c_hi = key_ok ? g.q_len - qbase : -(1 << 30);
       if (p.window_left > 0) c_hi = min(c_hi, jl + p.window_left - qbase);
+      uint32_t rs[COLS], rd[COLS];
+      if constexpr (COLS == 16) {
+        tmem_ld16(tmem_s + bf * kQB + lane_addr + wg * COLS, rs);
+        tmem_ld16(tmem_dp + bf * kQB + lane_addr + wg * COLS, rd);
+      } else {
+        tmem_ld32(tmem_s + bf * kQB + lane_addr + wg * COLS, *reinterpret_cast<uint32_t(*)[32]>(rs));
+        tmem_ld32(tmem_dp + bf * kQB + lane_addr + wg * COLS, *reinterpret_cast<uint32_t(*)[32]>(rd));
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      warp_arrive(&bars->sdp_empty[bf]);  // the unit after next may reuse this buffer
       uint32_t ppk[COLS / 2], dpk[COLS / 2];
-#pragma unroll
-      for (int cc = 0; cc < CPW; ++cc) {
-        const int cidx = wg * CPW + cc;
-        uint32_t rs[32], rd[32];
-        tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
-        tmem_ld32(tmem_dp + lane_addr + cidx * 32, rd);
-        tmem_wait_ld();
-        if (cc == CPW - 1) {  // S^T and dP^T are in registers: the next unit's MMAs may overwrite them
-          tc_fence_before();
-          warp_arrive(&bars->sdp_empty);
-        }
-        if constexpr (NORM == HFAN_SOFTMAX1) {
-        const int lo = c_lo - cidx * 32, hi = c_hi - cidx * 32;
-        const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= 32);
+      const int cb = wg * COLS;
+      const int lo = c_lo - cb, hi = c_hi - cb;
+      if constexpr (NORM == HFAN_SOFTMAX1) {
+        const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= COLS);
         const uint64_t zs2 = f2_pack(zs, zs);
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
+        for (int e = 0; e < COLS; e += 2) {
           // statistics of query columns e, e+1 (broadcast 8-byte loads)
-          const int col = cidx * 32 + e;
+          const int col = cb + e;
           const uint64_t nst = *reinterpret_cast<const uint64_t*>(st0s + col);
           const uint64_t nc2 = *reinterpret_cast<const uint64_t*>(crs + col);
+          const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
           uint64_t x = ffma2(f2_pack(__uint_as_float(rs[e]), __uint_as_float(rs[e + 1])), zs2, nst);
           if (!full)
             x = f2_pack(e >= lo && e < hi ? f2_lo(x) : kNegInf, e + 1 >= lo && e + 1 < hi ? f2_hi(x) : kNegInf);
           const uint64_t g2 = fadd2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), nc2);
-          uint64_t pr, ds;
-          if (NORM == HFAN_SOFTMAX1) {
-            const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
-            pr = fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il);
-            ds = fmul2(pr, g2);
-          } else if (NORM == HFAN_SPARSEMAX) {
-            pr = f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
-            ds = f2_pack(f2_lo(x) > 0.f ? f2_lo(g2) : 0.f, f2_hi(x) > 0.f ? f2_hi(g2) : 0.f);
-          } else {
-            const uint64_t d = f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
-            pr = fmul2(d, d);
-            ds = fmul2(d, g2);
-          }
-          ppk[cc * 16 + e / 2] = pack2<BF16>(f2_lo(pr), f2_hi(pr));
-          dpk[cc * 16 + e / 2] = pack2<BF16>(f2_lo(ds), f2_hi(ds));
+          const uint64_t pr = fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il);
+          const uint64_t ds = fmul2(pr, g2);
+          ppk[e / 2] = pack2<BF16>(f2_lo(pr), f2_hi(pr));
+          dpk[e / 2] = pack2<BF16>(f2_lo(ds), f2_hi(ds));
         }
-        } else {
-        const int lo = c_lo - cidx * 32, hi = c_hi - cidx * 32;
+      } else {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
+        for (int e = 0; e < COLS; e += 2) {
           float pv[2], dsv[2];
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            const int col = cidx * 32 + e + x;
+            const int col = cb + e + x;
             const bool vis = (e + x) >= lo && (e + x) < hi;
             float w = 0.f, pr = 0.f;
             if (vis) weight<NORM>(__uint_as_float(rs[e + x]) * zs, st0s[col], st1s[col], &w, &pr);
             pv[x] = pr;
             dsv[x] = w * (__uint_as_float(rd[e + x]) - crs[col]);
           }
-          ppk[cc * 16 + e / 2] = pack2<BF16>(pv[0], pv[1]);
-          dpk[cc * 16 + e / 2] = pack2<BF16>(dsv[0], dsv[1]);
-        }
+          ppk[e / 2] = pack2<BF16>(pv[0], pv[1]);
+          dpk[e / 2] = pack2<BF16>(dsv[0], dsv[1]);
         }
       }
-      // P^T, then dS^T, through the shared buffer
-      for (int which = 0; which < 2 && ok; ++which) {
-        if (pbc > 0) {
-          if (!(ok = wait_warp(&bars->pb_empty, (pbc - 1) & 1, abort_flag))) break;
-        }
-        store_chunks_sw128<COLS / 8>(smem + L::PB, row, wg * (COLS / 8), which == 0 ? ppk : dpk);
-        fence_proxy_async_smem();
-        tc_fence_before();
-        warp_arrive(&bars->pb_full);
-        ++pbc;
+      // P^T and dS^T tiles are free once the previous unit's dV / dK completed
+      if (u > 0) {
+        if (!(ok = wait_warp(&bars->p_empty, (u - 1) & 1, abort_flag))) continue;
       }
+      store_chunks_sw128<COLS / 8>(smem + L::PP, row, wg * (COLS / 8), ppk);
+      store_chunks_sw128<COLS / 8>(smem + L::PD, row, wg * (COLS / 8), dpk);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      warp_arrive(&bars->p_full);
     }
     if (ok && n_units > 0) {
       ok = wait_warp(&bars->done, 0, abort_flag);
@@ -859,11 +864,16 @@ cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t
       !make_map(&mk, p.k, BF16, HD, tk, p.hkv, batch, p.k_st, p.k_sh, varlen ? tk * p.k_st : p.k_sb) ||
       !make_map(&mv, p.v, BF16, HD, tk, p.hkv, batch, p.v_st, p.v_sh, varlen ? tk * p.v_st : p.v_sb))
     return cudaErrorInvalidValue;
+  // the dK/dV kernel streams 64-row Q / dO tiles
+  CUtensorMap mq64, mdo64;
+  if (!make_map(&mq64, p.q, BF16, HD, tq, p.hq, batch, p.q_st, p.q_sh, varlen ? tq * p.q_st : p.q_sb, kQB) ||
+      !make_map(&mdo64, p.dout, BF16, HD, tq, p.hq, batch, p.do_st, p.do_sh, varlen ? tq * p.do_st : p.do_sb, kQB))
+    return cudaErrorInvalidValue;
   cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
                            Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
   if (e != cudaSuccess) return e;
   return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
-                  Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+                  Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq64, mdo64, mk, mv, p);
 }
 
 template <int HD, bool BF16>

@@ -152,12 +152,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 4-D map (dim, token, head, batch) with a 64 x 128 x 1 x 1 box, 128-byte swizzle.
 inline bool make_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t tokens, int heads, int batch,
-              int64_t st, int64_t sh, int64_t sb) {
+              int64_t st, int64_t sh, int64_t sb, int box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
