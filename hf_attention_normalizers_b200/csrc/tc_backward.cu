@@ -507,8 +507,8 @@ struct KLayout {
   static constexpr uint32_t DO = Q + kQStages * NH * kQHalf;     // kQStages stages
   static constexpr uint32_t PP = DO + kQStages * NH * kQHalf;    // P^T  [128 keys][64 queries]
   static constexpr uint32_t PD = PP + kHalf;                     // dS^T [128 keys][64 queries]
-  static constexpr uint32_t STATS = PD + kHalf;                  // 3 x 64 floats
-  static constexpr uint32_t BARS = STATS + 3 * kQB * 4;
+  static constexpr uint32_t STATS = PD + kHalf;                  // 2 buffers x 3 x 64 floats
+  static constexpr uint32_t BARS = STATS + 2 * 3 * kQB * 4;
   static constexpr uint32_t CTL = BARS + sizeof(KBars);
   static constexpr uint32_t TOTAL = CTL + 16 + 1024;
 };
@@ -532,9 +532,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::CTL);
   int* abort_ptr = reinterpret_cast<int*>(smem + L::CTL + 4);
   volatile int* abort_flag = abort_ptr;
-  float* st0s = reinterpret_cast<float*>(smem + L::STATS);
-  float* st1s = st0s + kQB;
-  float* crs = st1s + kQB;
+  float* stats_smem = reinterpret_cast<float*>(smem + L::STATS);  // [2][3][kQB]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, kvh = blockIdx.y;
@@ -688,9 +686,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     bool ok = true;
     // The named barriers run on every iteration, even after a timeout, so that
     // no warp waits for one that has left the loop.
-    // Row statistics of a unit's 64 query rows: warpgroup 0 loads those of the
-    // next unit into registers while this one is processed, and stages them in
-    // shared memory between two barriers at the unit's start.
+    // Row statistics of a unit's 64 query rows, double-buffered in shared
+    // memory: after the barrier that starts unit u (every warp is done with
+    // unit u - 1 and its buffer), warpgroup 0 stages unit u + 1's (loaded into
+    // registers during unit u - 1) in the other buffer; the barrier that starts
+    // unit u + 1 publishes them.
     float na = kPosInf, nb = 1.f, nc = 0.f;
     auto fetch = [&](int u_) {
       na = kPosInf;
@@ -705,20 +705,28 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         nc = p.corr[si];
       }
     };
+    auto stage = [&](int buf) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
+      if (wg == 0 && row < kQB) {
+        float* sb_ = stats_smem + buf * 3 * kQB;
+        const float sg = NORM == HFAN_SOFTMAX1 ? -1.f : 1.f;
+        sb_[row] = sg * na;
+        sb_[kQB + row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
+        sb_[2 * kQB + row] = sg * nc;
+      }
+    };
     fetch(0);
+    stage(0);
+    fetch(1);
     for (int u = 0; u < n_units; ++u) {
       const int m = m_lo + u % n_m;
       const int qbase = m * kQB;
       const int bf = u & 1;
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      if (wg == 0 && row < kQB) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
-        const float sg = NORM == HFAN_SOFTMAX1 ? -1.f : 1.f;
-        st0s[row] = sg * na;
-        st1s[row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
-        crs[row] = sg * nc;
-      }
-      named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      fetch(u + 1);
+      stage(bf ^ 1);  // unit u + 1
+      fetch(u + 2);
+      const float* st0s = stats_smem + bf * 3 * kQB;
+      const float* st1s = st0s + kQB;
+      const float* crs = st1s + kQB;
       if (!ok) continue;
       if (!(ok = wait_warp(&bars->sdp_full[bf], (u >> 1) & 1, abort_flag))) continue;
       tc_fence_after();
