@@ -487,15 +487,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 // queries) into one of two TMEM buffers, so that the next unit's products run
 // while the row warps turn this unit's into P^T and dS^T; those go to two
 // separate shared-memory tiles for dV += P^T dO and dK += dS^T Q (K = 64).
-// Q / dO tiles (64 rows) stream through a 4-stage ring.
+// Q / dO tiles (64 rows) stream through a 3-stage ring; the P^T / dS^T
+// tiles are double-buffered, so that the row warps never wait for the
+// previous unit's dV / dK.
 constexpr int kQB = 64;        // query rows per unit
-constexpr int kQStages = 4;    // Q / dO ring depth
+constexpr int kQStages = 3;    // Q / dO ring depth
 constexpr uint32_t kQHalf = kQB * 128u;  // one 64-row x 128-byte swizzled half tile
 
 struct KBars {
   uint64_t kv_full;
   uint64_t qd_full[kQStages], qd_empty[kQStages];
-  uint64_t sdp_full[2], sdp_empty[2], p_full, p_empty, done;
+  uint64_t sdp_full[2], sdp_empty[2], p_full[2], p_empty[2], done;
 };
 
 template <int HD>
@@ -505,9 +507,9 @@ struct KLayout {
   static constexpr uint32_t V = K + NH * kHalf;
   static constexpr uint32_t Q = V + NH * kHalf;                  // kQStages stages
   static constexpr uint32_t DO = Q + kQStages * NH * kQHalf;     // kQStages stages
-  static constexpr uint32_t PP = DO + kQStages * NH * kQHalf;    // P^T  [128 keys][64 queries]
-  static constexpr uint32_t PD = PP + kHalf;                     // dS^T [128 keys][64 queries]
-  static constexpr uint32_t STATS = PD + kHalf;                  // 2 buffers x 3 x 64 floats
+  static constexpr uint32_t PP = DO + kQStages * NH * kQHalf;    // 2 x P^T  [128 keys][64 queries]
+  static constexpr uint32_t PD = PP + 2 * kHalf;                 // 2 x dS^T [128 keys][64 queries]
+  static constexpr uint32_t STATS = PD + 2 * kHalf;              // 2 buffers x 3 x 64 floats
   static constexpr uint32_t BARS = STATS + 2 * 3 * kQB * 4;
   static constexpr uint32_t CTL = BARS + sizeof(KBars);
   static constexpr uint32_t TOTAL = CTL + 16 + 1024;
@@ -566,8 +568,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       mbar_init(&bars->sdp_full[s], 1);
       mbar_init(&bars->sdp_empty[s], Roles<HD>::ROW_THREADS / 32);
     }
-    mbar_init(&bars->p_full, Roles<HD>::ROW_THREADS / 32);
-    mbar_init(&bars->p_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->p_full[s], Roles<HD>::ROW_THREADS / 32);
+      mbar_init(&bars->p_empty[s], 1);
+    }
     mbar_init(&bars->done, 1);
     *abort_ptr = 0;
     fence_barrier_init();
@@ -650,22 +654,22 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       const uint32_t pp_base = smem_u32(smem + L::PP), pd_base = smem_u32(smem + L::PD);
       bool ok = true;
       for (int u = 0; u < n_units && ok; ++u) {
-        const int s = u % kQStages;
-        if (!(ok = mbar_wait(&bars->p_full, u & 1, abort_flag))) break;
+        const int s = u % kQStages, pb = u & 1;
+        if (!(ok = mbar_wait(&bars->p_full[pb], (u >> 1) & 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kQB / 16; ++kk) {
           // A = P^T / dS^T [128 keys x 64 queries], K-major; B = dO / Q tile,
           // MN-major (rows = queries, 64-wide head-dim blocks kQHalf apart)
           const uint64_t bo = sw128_desc(do_base + s * QTILE + kk * 16 * 128, kQHalf, 1024);
-          mma_f16_ss(tmem_dv, sw128_desc(pp_base + kk * 32, 16, 1024), bo, IDESC_ACC, u > 0 || kk > 0);
+          mma_f16_ss(tmem_dv, sw128_desc(pp_base + pb * kHalf + kk * 32, 16, 1024), bo, IDESC_ACC, u > 0 || kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < kQB / 16; ++kk) {
           const uint64_t bq = sw128_desc(q_base + s * QTILE + kk * 16 * 128, kQHalf, 1024);
-          mma_f16_ss(tmem_dk, sw128_desc(pd_base + kk * 32, 16, 1024), bq, IDESC_ACC, u > 0 || kk > 0);
+          mma_f16_ss(tmem_dk, sw128_desc(pd_base + pb * kHalf + kk * 32, 16, 1024), bq, IDESC_ACC, u > 0 || kk > 0);
         }
-        mma_commit(&bars->p_empty);
+        mma_commit(&bars->p_empty[pb]);
         mma_commit(&bars->qd_empty[s]);
       }
       if (ok) mma_commit(&bars->done);
@@ -785,15 +789,16 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           dpk[e / 2] = pack2<BF16>(dsv[0], dsv[1]);
         }
       }
-      // P^T and dS^T tiles are free once the previous unit's dV / dK completed
-      if (u > 0) {
-        if (!(ok = wait_warp(&bars->p_empty, (u - 1) & 1, abort_flag))) continue;
+      // P^T / dS^T tile pair u & 1 is free once unit u - 2's dV / dK completed
+      const int pb = u & 1;
+      if (u >= 2) {
+        if (!(ok = wait_warp(&bars->p_empty[pb], ((u >> 1) & 1) ^ 1, abort_flag))) continue;
       }
-      store_chunks_sw128<COLS / 8>(smem + L::PP, row, wg * (COLS / 8), ppk);
-      store_chunks_sw128<COLS / 8>(smem + L::PD, row, wg * (COLS / 8), dpk);
+      store_chunks_sw128<COLS / 8>(smem + L::PP + pb * kHalf, row, wg * (COLS / 8), ppk);
+      store_chunks_sw128<COLS / 8>(smem + L::PD + pb * kHalf, row, wg * (COLS / 8), dpk);
       fence_proxy_async_smem();
       tc_fence_before();
-      warp_arrive(&bars->p_full);
+      warp_arrive(&bars->p_full[pb]);
     }
     if (ok && n_units > 0) {
       ok = wait_warp(&bars->done, 0, abort_flag);
