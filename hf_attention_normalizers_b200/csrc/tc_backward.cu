@@ -712,7 +712,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     auto stage = [&](int buf) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
       if (wg == 0 && row < kQB) {
         float* sb_ = stats_smem + buf * 3 * kQB;
-        const float sg = NORM == HFAN_SOFTMAX1 ? -1.f : 1.f;
+        const float sg = -1.f;
         sb_[row] = sg * na;
         sb_[kQB + row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
         sb_[2 * kQB + row] = sg * nc;
@@ -753,40 +753,34 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       uint32_t ppk[COLS / 2], dpk[COLS / 2];
       const int cb = wg * COLS;
       const int lo = c_lo - cb, hi = c_hi - cb;
-      if constexpr (NORM == HFAN_SOFTMAX1) {
+      {
         const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= COLS);
         const uint64_t zs2 = f2_pack(zs, zs);
 #pragma unroll
         for (int e = 0; e < COLS; e += 2) {
-          // statistics of query columns e, e+1 (broadcast 8-byte loads)
+          // statistics of query columns e, e+1 (broadcast 8-byte loads; staged negated)
           const int col = cb + e;
           const uint64_t nst = *reinterpret_cast<const uint64_t*>(st0s + col);
           const uint64_t nc2 = *reinterpret_cast<const uint64_t*>(crs + col);
-          const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
           uint64_t x = ffma2(f2_pack(__uint_as_float(rs[e]), __uint_as_float(rs[e + 1])), zs2, nst);
           if (!full)
             x = f2_pack(e >= lo && e < hi ? f2_lo(x) : kNegInf, e + 1 >= lo && e + 1 < hi ? f2_hi(x) : kNegInf);
           const uint64_t g2 = fadd2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), nc2);
-          const uint64_t pr = fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il);
-          const uint64_t ds = fmul2(pr, g2);
+          uint64_t pr, ds;
+          if (NORM == HFAN_SOFTMAX1) {
+            const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
+            pr = fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il);
+            ds = fmul2(pr, g2);
+          } else if (NORM == HFAN_SPARSEMAX) {
+            pr = f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
+            ds = f2_pack(f2_lo(x) > 0.f ? f2_lo(g2) : 0.f, f2_hi(x) > 0.f ? f2_hi(g2) : 0.f);
+          } else {
+            const uint64_t d = f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
+            pr = fmul2(d, d);
+            ds = fmul2(d, g2);
+          }
           ppk[e / 2] = pack2<BF16>(f2_lo(pr), f2_hi(pr));
           dpk[e / 2] = pack2<BF16>(f2_lo(ds), f2_hi(ds));
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < COLS; e += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const int col = cb + e + x;
-            const bool vis = (e + x) >= lo && (e + x) < hi;
-            float w = 0.f, pr = 0.f;
-            if (vis) weight<NORM>(__uint_as_float(rs[e + x]) * zs, st0s[col], st1s[col], &w, &pr);
-            pv[x] = pr;
-            dsv[x] = w * (__uint_as_float(rd[e + x]) - crs[col]);
-          }
-          ppk[e / 2] = pack2<BF16>(pv[0], pv[1]);
-          dpk[e / 2] = pack2<BF16>(dsv[0], dsv[1]);
         }
       }
       // P^T / dS^T tile pair u & 1 is free once unit u - 2's dV / dK completed
