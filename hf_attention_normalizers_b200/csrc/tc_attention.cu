@@ -73,6 +73,11 @@ constexpr int kBN = 128;           // keys per tile
 template <int HD>
 constexpr int ring_stages() { return HD == 128 ? 5 : 8; }
 constexpr int kScanStages = 2;
+#ifndef HFAN_CW
+#define HFAN_CW 8
+#endif
+constexpr int kCW = HFAN_CW;                          // keys per chunk of the scan's gate
+constexpr int kCompactRoom = kCW > 12 ? kCW : 12;     // free slots a compaction must leave
 constexpr int kMaxStages = 8;
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
 constexpr float kRescaleLog2 = 8.f;
@@ -240,7 +245,7 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
   // appends.  Sparsemax (no cooperative vote) also stops when half the
   // buffer stays live: the row's candidates are dense, and compacting on
   // every chunk would cost more than the sweeps that settle such rows.
-  if (live > (NORM == HFAN_SPARSEMAX ? cap / 2 : cap - 12)) c.overflow = true;
+  if (live > (NORM == HFAN_SPARSEMAX ? cap / 2 : cap - kCompactRoom)) c.overflow = true;
   return c;
 }
 
@@ -576,11 +581,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         DIAG_LAP(dw);
         if (ok) {
         // chunk maxima (8 keys each) gate the candidate appends
-        float cm[COLS / 8];
+        float cm[COLS / kCW];
         float tm = kNegInf;
 #pragma unroll
-        for (int c = 0; c < COLS / 8; ++c) {
-          const float m8 = max_n<8>(sreg + c * 8);
+        for (int c = 0; c < COLS / kCW; ++c) {
+          const float m8 = max_n<kCW>(sreg + c * kCW);
           cm[c] = m8;
           tm = fmaxf(tm, m8);
           float x = m8;
@@ -608,15 +613,15 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         DIAG_LAP(dt);
         if (HFAN_EXP != 1 && !cd.overflow && tm > cd.thr_s) {
 #pragma unroll
-          for (int c = 0; c < COLS / 8; ++c) {
+          for (int c = 0; c < COLS / kCW; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
-              if (cd.n > CAPW - 8) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
+              if (cd.n > CAPW - kCW) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
               if (!cd.overflow) {
                 // predicated appends: every value is written at slot n, and n
                 // only advances past the candidates
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  const float x = sreg[c * 8 + e];
+                for (int e = 0; e < kCW; ++e) {
+                  const float x = sreg[c * kCW + e];
                   cbuf[cd.n * 128 + row] = x * zs;
                   cd.n += x > cd.thr_s ? 1 : 0;
                 }
@@ -655,7 +660,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
               if (z > cd.thr) cbuf[live++ * 128 + row] = z;
             }
             cd.n = live;
-            if (live > CAPW - 12) cd.overflow = true;
+            if (live > CAPW - kCompactRoom) cd.overflow = true;
           }
           xb[wg * 128 + row] = cd.thr;
         }
