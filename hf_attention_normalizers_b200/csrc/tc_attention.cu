@@ -31,22 +31,19 @@
 #include "tc_ptx.cuh"
 #include "tc_common.cuh"
 
+// Diagnostics (compiled in with -DHFAN_DIAG only): per-CTA clock64 sums of
+// the scan / solve / final phases and counters of compactions and sweeps,
+// read back with hfan_diag_read.  The product build contains none of it.
 #ifdef HFAN_DIAG
 __device__ unsigned long long g_hfan_diag[16];
 extern "C" int hfan_diag_read(unsigned long long* out) {
   return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 16);
-}
-__device__ long long g_hfan_tl[2][128][8];
-extern "C" int hfan_tl_read(long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, g_hfan_tl, sizeof(long long) * 2 * 128 * 8);
 }
 extern "C" int hfan_diag_clear() {
   unsigned long long z[16] = {0};
   return (int)cudaMemcpyToSymbol(g_hfan_diag, z, sizeof(z));
 }
 #define DIAG_ADD(i, v) atomicAdd(&g_hfan_diag[i], (unsigned long long)(v))
-#define TL(slot, t, k) \
-  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (t) < 128) g_hfan_tl[slot][t][k] = clock64()
 #define DIAG_T(acc, stmt)               \
   do {                                  \
     const long long t0_ = clock64();    \
@@ -56,7 +53,6 @@ extern "C" int hfan_diag_clear() {
 #else
 #define DIAG_ADD(i, v) ((void)0)
 #define DIAG_T(acc, stmt) stmt
-#define TL(slot, t, k) ((void)0)
 #endif
 
 namespace hfan {
@@ -273,10 +269,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #ifndef HFAN_VOTE_PERIOD
 #define HFAN_VOTE_PERIOD 4
 #endif
-#ifndef HFAN_EXP
-#define HFAN_EXP 0
-#endif
-  constexpr bool SCAN = SPARSE && HFAN_EXP != 2 && HFAN_EXP != 5 && HFAN_EXP != 6;
+  constexpr bool SCAN = SPARSE;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -483,12 +476,6 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       const int sb = sc & 1;
       if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
-      if (HFAN_EXP == 6) {
-        tc_fence_before();
-        warp_arrive(&bars->s_empty[sb]);
-        ++sc;
-        return true;
-      }
       uint32_t r[COLS / 32][32];
 #pragma unroll
       for (int c = 0; c < COLS / 32; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + wg * COLS + c * 32, r[c]);
@@ -611,7 +598,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           }
         }
         DIAG_LAP(dt);
-        if (HFAN_EXP != 1 && !cd.overflow && tm > cd.thr_s) {
+        if (!cd.overflow && tm > cd.thr_s) {
 #pragma unroll
           for (int c = 0; c < COLS / kCW; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
@@ -801,9 +788,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     long long dg_s = 0, dg_pv = 0;
 #endif
     for (int t = 0; t < n_tiles && (ok || !SPARSE); ++t) {
-      if (threadIdx.x == 0) TL(1, t, 0);
       if (ok) DIAG_T(dg_s, ok = load_s(t));
-      if (threadIdx.x == 0) TL(1, t, 1);
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
@@ -831,7 +816,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           l2 = fadd2(l2, f2_pack(e0, e1));
         }
         l += f2_lo(l2) + f2_hi(l2);
-      } else if (HFAN_EXP != 5 && HFAN_EXP != 6) {
+      } else {
         const uint64_t zs2 = f2_pack(zs, zs), nt2 = f2_pack(ntau, ntau);
 #pragma unroll
         for (int j = 0; j < COLS; j += 2) {
@@ -867,7 +852,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       // this warpgroup's COLS keys of the P row -> TMEM columns
       // [COLS/2 wg, COLS/2 (wg + 1)) of buffer pb, packed in key order
 #pragma unroll
-      for (int c = 0; c < COLS / 32 && HFAN_EXP != 6; ++c) {
+      for (int c = 0; c < COLS / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
@@ -876,7 +861,6 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(&bars->p_full[pb]);
-      if (threadIdx.x == 0) TL(1, t, 2);
       ++pc;
     }
     if (ok && n_tiles > 0) {
