@@ -330,3 +330,37 @@ def test_paged_prefill_tensor_core_route_matches_oracle(norm, shared):
     for label, a, e in zip(("o", "dq", "dkc", "dvc"), (o, q.grad, kc.grad, vc.grad), refs):
         assert_close(a, e, torch.bfloat16, f"paged-tc/{norm}/{label}")
     assert N.device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_hf_continuous_batching_paged_attention_interface(norm):
+    """HF `paged_attention` interface (continuous batching): the cache update
+    hands back the packed keys/values of every sequence and one varlen launch
+    serves the batch (a prefill chunk, a decode token and a full prefill)."""
+    from hf_attention_normalizers_b200 import backends
+
+    gen = torch.Generator().manual_seed(44)
+    lens_q = torch.tensor([5, 1, 64])
+    lens_k = torch.tensor([40, 300, 64])
+    cu_q = torch.cat([torch.zeros(1, dtype=torch.long), lens_q.cumsum(0)])
+    cu_k = torch.cat([torch.zeros(1, dtype=torch.long), lens_k.cumsum(0)])
+    tq, tk, hq, hkv, d = int(cu_q[-1]), int(cu_k[-1]), 8, 2, 128
+    q = torch.randn(1, hq, tq, d, generator=gen).to(torch.bfloat16).cuda()
+    k_all = torch.randn(1, hkv, tk, d, generator=gen).to(torch.bfloat16).cuda()
+    v_all = torch.randn(1, hkv, tk, d, generator=gen).to(torch.bfloat16).cuda()
+
+    class Cache:
+        def update(self, k, v, layer_idx, **kw):
+            return k_all, v_all
+
+    class Module:
+        layer_idx = 0
+        scaling = d ** -0.5
+
+    fn = {"softmax1": backends.softmax_1, "sparsemax": backends.sparsemax, "entmax15": backends.entmax15}[norm]
+    o, _ = backends.paged_normalizer_attention_forward(
+        Module(), q, k_all[:, :, :1], v_all[:, :, :1], None, cache=Cache(), cu_seq_lens_q=cu_q.cuda(),
+        cu_seq_lens_k=cu_k.cuda(), max_seqlen_q=int(lens_q.max()), max_seqlen_k=int(lens_k.max()), softmax_fn=fn)
+    ref = oracle.varlen_forward(_np(q[0].transpose(0, 1)), _np(k_all[0].transpose(0, 1)), _np(v_all[0].transpose(0, 1)),
+                                cu_q.numpy(), cu_k.numpy(), norm)
+    assert_close(o, ref, torch.bfloat16, f"hf-paged/{norm}")
