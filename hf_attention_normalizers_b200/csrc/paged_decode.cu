@@ -995,8 +995,8 @@ size_t decode_workspace_bytes(const AttnParams& p, int max_len) { return ws_layo
 
 // ---------------------------------------------------------------------------
 // Allocation-free variant.  Some callers cannot allocate device memory at the
-// point where they decode: code running inside a CUDA graph capture or on an
-// inference server's hot path, and embedders that own the GPU allocator and
+// point where they decode: code running on an inference server's hot path,
+// and embedders that own the GPU allocator and
 // forbid allocations behind their back.  For them the scratch lives in this
 // fixed device array instead of a caller workspace.  It is loaded with the
 // library and held by every GPU that loads it until the process exits.

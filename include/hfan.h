@@ -158,8 +158,8 @@ int hfan_paged_decode(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor ke
 
 /* Allocation-free paged decode.  This entry point has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory when they
- * decode: code being captured into a CUDA graph or running on a serving hot
- * path, and embedders that own the GPU allocator.  It does exactly what
+ * decode: code running on a serving hot path, and embedders that own the GPU
+ * allocator.  It does exactly what
  * hfan_paged_decode does, but its scratch is a fixed 64 MiB device array
  * inside the library (every GPU that loads the library holds it until the
  * process exits), so the caller passes only inputs and outputs.
