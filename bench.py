@@ -65,19 +65,32 @@ class ClockSampler:
         self.lines = []
 
     def __enter__(self):
+        self.t0 = self.t1 = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait for its first sample so
+            # that the timed region is covered from its first step
+            deadline = time.time() + 5.0
+            while not self.lines and time.time() < deadline:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def start(self):
+        self.t0 = time.time()
+
+    def stop(self):
+        self.t1 = time.time()
+        time.sleep(0.15)  # the sample that covers the end of the region
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -90,7 +103,11 @@ class ClockSampler:
     def summary(self):
         sm, smax, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        lines = self.lines
+        if self.t0 is not None and self.t1 is not None:
+            window = [x for x in lines if self.t0 <= x[0] <= self.t1 + 0.11]
+            lines = window or lines
+        for _, line in lines:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 8:
                 continue
@@ -159,11 +176,13 @@ def run_ours(args, rank, world, local_rank):
     with sampler:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
+        sampler.start()
         e0.record()
         for _ in range(args.steps):
             step()
         e1.record()
         barrier()
+        sampler.stop()
     if args.profile_case:
         return None
     ms = e0.elapsed_time(e1) / args.steps
@@ -584,7 +603,7 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
