@@ -250,6 +250,7 @@ def run_ours(args, rank, world, local_rank):
             for name in NORMS:
                 o = fns[name](q, k, v, is_causal=True)
                 o.backward(do)
+                gather(o.detach(), q.grad, k.grad, v.grad)  # as in step(): outputs and gradients all-gathered
                 loss = loss + torch.sum(o * do, dtype=torch.float32)
             free[b].record()
             float(loss.item())
