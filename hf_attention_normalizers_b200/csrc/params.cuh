@@ -39,6 +39,7 @@ struct AttnParams {
   int64_t num_cache_tokens;
   int paged;
   int lens_only;           // dense K/V whose per-sequence key lengths come from seq_lens
+  int tile_lpt;            // tensor-core kernels: hand tiles out longest-first across the whole grid
 
   float scale;
   int causal, window_left, norm;

@@ -277,8 +277,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + L::CTL);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z, h = blockIdx.y;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const uint3 tile = tile_coords(p.tile_lpt);
+  const int b = tile.z, h = tile.y;
+  const int qt = gridDim.x - 1 - tile.x;  // longest causal rows first
   const Geometry g = geometry(p, b);
   const int q0 = qt * kBM;
   if (q0 >= g.q_len) return;
@@ -953,22 +954,24 @@ cudaError_t launch_fwd(const AttnParams& p, int max_q, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const size_t smem = Layout<HD>::TOTAL;
   dim3 grid((max_q + kBM - 1) / kBM, p.hq, p.batch);
+  AttnParams pl = p;  // query tiles re-read K and V
+  pl.tile_lpt = (varlen ? tk_n : (int64_t)p.batch * tk_n) * p.hkv * HD * 4 <= kLptMaxReread;
   cudaError_t e;
   switch (p.norm) {
     case HFAN_SOFTMAX1:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
       break;
     case HFAN_SPARSEMAX:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
       break;
     default:
       e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, p);
+      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
       break;
   }
   return cudaGetLastError();

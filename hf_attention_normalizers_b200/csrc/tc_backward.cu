@@ -102,8 +102,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   volatile int* abort_flag = abort_ptr;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z, h = blockIdx.y;
-  const int qt = gridDim.x - 1 - blockIdx.x;
+  const uint3 tile = tile_coords(p.tile_lpt);
+  const int b = tile.z, h = tile.y;
+  const int qt = gridDim.x - 1 - tile.x;
   const Geometry g = geometry(p, b);
   const int q0 = qt * kBM;
   if (q0 >= g.q_len) return;
@@ -537,9 +538,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   float* stats_smem = reinterpret_cast<float*>(smem + L::STATS);  // [2][3][kQB]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z, kvh = blockIdx.y;
+  const uint3 tile = tile_coords(p.tile_lpt);  // key tile 0 carries the most causal rows
+  const int b = tile.z, kvh = tile.y;
   const Geometry g = geometry(p, b);
-  const int k0 = blockIdx.x * kBN;
+  const int k0 = tile.x * kBN;
   if (k0 >= g.k_len) return;
   const int groups = p.hq / p.hkv;
   const bool varlen = p.cu_q != nullptr;
@@ -876,11 +878,14 @@ cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t
   if (!make_map(&mq64, p.q, BF16, HD, tq, p.hq, batch, p.q_st, p.q_sh, varlen ? tq * p.q_st : p.q_sb, kQB) ||
       !make_map(&mdo64, p.dout, BF16, HD, tq, p.hq, batch, p.do_st, p.do_sh, varlen ? tq * p.do_st : p.do_sb, kQB))
     return cudaErrorInvalidValue;
+  AttnParams pq = p, pk = p;  // query tiles re-read K and V; key tiles re-read Q and dO
+  pq.tile_lpt = (int64_t)batch * tk * p.hkv * HD * 4 <= kLptMaxReread;
+  pk.tile_lpt = (int64_t)batch * tq * p.hq * HD * 4 <= kLptMaxReread;
   cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
-                           Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, p);
+                           Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, pq);
   if (e != cudaSuccess) return e;
   return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
-                  Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq64, mdo64, mk, mv, p);
+                  Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq64, mdo64, mk, mv, pk);
 }
 
 template <int HD, bool BF16>

@@ -169,5 +169,26 @@ inline bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr
 inline bool stride_ok(int64_t s) { return s > 0 && (s % 8) == 0 && s < ((int64_t)1 << 38); }
 
 
+// Tile coordinates of this CTA.  Blocks are dispatched in increasing linear
+// id (x fastest).  In the default order every (head, batch) column of tiles
+// is handed out whole, so on a grid of a few waves the heaviest tiles of the
+// last heads start late and the kernel ends on a long tail.  With `lpt` the
+// tile index x becomes the slowest-varying coordinate: all heads' tiles of
+// one weight class are handed out before any lighter class (longest
+// processing time first list scheduling; heads of one KV group stay
+// adjacent).  That spreads the CTAs in flight over every head, so the host
+// enables it only when the operand that CTAs re-read from L2 is small.
+__device__ __forceinline__ uint3 tile_coords(int lpt) {
+  if (!lpt) return make_uint3(blockIdx.x, blockIdx.y, blockIdx.z);
+  const unsigned yz = gridDim.y * gridDim.z;
+  const unsigned lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const unsigned r = lin % yz;
+  return make_uint3(lin / yz, r % gridDim.y, r / gridDim.y);
+}
+
+// Longest-first order is allowed when the re-read operand (K/V for query
+// tiles, Q/dO for key tiles) fits in about a third of L2.
+constexpr int64_t kLptMaxReread = 40ll << 20;
+
 }  // namespace tc
 }  // namespace hfan
