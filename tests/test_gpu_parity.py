@@ -243,6 +243,26 @@ def test_long_key_row_beyond_old_single_block_limit(norm):
 
 
 @pytest.mark.parametrize("norm", NORMS)
+def test_tile_orders_agree(norm):
+    """The tensor-core kernels hand tiles out longest-first across heads when
+    the operand they re-read is at most 40 MB, else head by head.  Eight heads
+    of 12288 tokens (K/V and Q/dO 50 MB each) take the head-major order; each
+    head alone (6 MB) takes the longest-first one.  Heads are independent and
+    the kernels deterministic, so both runs agree bit for bit; the last query
+    tile is also checked against the oracle."""
+    q, k, v, do = _inputs((1, 8, 12288, 128), (1, 8, 12288, 128), torch.bfloat16, seed=21)
+    whole = _run_dense(norm, q, k, v, do)
+    for h in range(8):
+        sl = slice(h, h + 1)
+        one = _run_dense(norm, q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(),
+                         do[:, sl].contiguous())
+        for label, a, b in zip(("o", "dq", "dk", "dv"), whole, one):
+            assert torch.equal(a[:, sl], b), f"{norm}/head {h}/{label}"
+    ref = oracle.attention_forward(_np(q[:, :2, -128:]), _np(k[:, :2]), _np(v[:, :2]), norm, causal=True)
+    assert_close(whole[0][:, :2, -128:], ref, torch.bfloat16, f"{norm}/last tile")
+
+
+@pytest.mark.parametrize("norm", NORMS)
 def test_torch_compile_fullgraph_bf16(norm):
     def attention(q, k, v):
         return KERNELS[norm](q, k, v, is_causal=True)
