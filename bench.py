@@ -272,9 +272,9 @@ def run_ours(args, rank, world, local_rank):
         return None
     burst, sustained, hbm, peak_kind = peaks()
     # Dominant single launch: the entmax15 forward (tc_fwd_kernel).  Its DRAM
-    # traffic comes from the ncu capture summarised in
-    # profiles/tc_kernels_qwen3_8b_small_case.md (25.24 MB read on a case with
-    # 1/16 of the (batch x head) units, scaled by 16).
+    # traffic comes from one ncu capture of `bench.py --shape 1,8192,8,2
+    # --profile-case` (dram__bytes_read.sum + dram__bytes_write.sum = 25.24 MB
+    # on that case, 1/16 of the (batch x head) units; scaled by 16).
     dom = phases["entmax15"]
     achieved = flops_rank / dom["fwd_ms"] / 1e9
     traffic = 25.24e6 * 16 if (B, S, HQ, HKV) == (4, 8192, 32, 8) and world == 1 else None
