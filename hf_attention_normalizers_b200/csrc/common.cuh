@@ -69,14 +69,22 @@ __device__ __forceinline__ float warp_min(float v) {
 //     step on f(t) = sum (z - t)_+^a - 1 (convex and decreasing, so Newton from
 //     the left never overshoots): sparsemax t <- tc (Michelot's iteration),
 //     entmax15 t <- t + (s2 - 1) / (2 s1).
+//
+// The sums may be taken relative to any fixed reference r instead of t
+// (s1 = sum (z - r), s2 = sum (z - r)^2 over the same set S = {z > t}); the
+// closed form is then evaluated around r.  With r = the row maximum the result
+// depends only on the set S and the order of summation, not on the lower
+// bound t that found S; the tensor-core forward uses that to make tau
+// bit-reproducible, and it is the reference's own form (vutils works on
+// X - max).
 // ---------------------------------------------------------------------------
 struct TauStats {
   float cnt, s1, s2, zmin;
 };
 
-__device__ __forceinline__ void tau_accumulate(TauStats& st, float z, float t) {
+__device__ __forceinline__ void tau_accumulate_ref(TauStats& st, float z, float t, float r) {
   if (z > t) {
-    float d = z - t;
+    float d = z - r;
     st.cnt += 1.f;
     st.s1 += d;
     st.s2 += d * d;
@@ -84,24 +92,40 @@ __device__ __forceinline__ void tau_accumulate(TauStats& st, float z, float t) {
   }
 }
 
-// Returns true when t is resolved; writes the exact threshold to *tau.  On
-// false, *t holds the refined lower bound for the next sweep and *tau the
-// current closed-form estimate.
-__device__ __forceinline__ bool tau_step(int norm, const TauStats& st, float* t, float* tau) {
-  float cnt = fmaxf(st.cnt, 1.f);
+__device__ __forceinline__ void tau_accumulate(TauStats& st, float z, float t) { tau_accumulate_ref(st, z, t, t); }
+
+// Sums taken around r.  Returns true when t is resolved and writes the exact
+// threshold to *tau.  On false, *t holds the refined lower bound for the next
+// sweep and *tau the current closed-form estimate.
+__device__ __forceinline__ bool tau_step_ref(int norm, const TauStats& st, float r, float* t, float* tau) {
+  const float cnt = fmaxf(st.cnt, 1.f);
   float tc;
   if (norm == HFAN_SPARSEMAX) {
-    tc = *t + (st.s1 - 1.f) / cnt;
+    tc = r + (st.s1 - 1.f) / cnt;
   } else {
-    float disc = fmaxf(st.s1 * st.s1 - cnt * (st.s2 - 1.f), 0.f);
-    tc = *t + (st.s1 - sqrtf(disc)) / cnt;
+    const float disc = fmaxf(st.s1 * st.s1 - cnt * (st.s2 - 1.f), 0.f);
+    tc = r + (st.s1 - sqrtf(disc)) / cnt;
   }
   *tau = tc;
   if (st.zmin >= tc) return true;
-  float nt = (norm == HFAN_SPARSEMAX) ? tc : *t + (st.s2 - 1.f) / (2.f * fmaxf(st.s1, 1e-30f));
+  float nt;
+  if (norm == HFAN_SPARSEMAX) {
+    nt = tc;
+  } else {
+    // Newton step on sum (z - t)^2 - 1: the sums around t from those around r
+    const float dl = r - *t;
+    const float s1t = st.s1 + st.cnt * dl;
+    const float s2t = st.s2 + dl * (2.f * st.s1 + st.cnt * dl);
+    nt = *t + (s2t - 1.f) / (2.f * fmaxf(s1t, 1e-30f));
+  }
   // Guard against a rounding stall: the next bound must strictly grow.
   *t = fmaxf(nt, nextafterf(*t, kPosInf));
   return false;
+}
+
+// Sums taken around t itself.
+__device__ __forceinline__ bool tau_step(int norm, const TauStats& st, float* t, float* tau) {
+  return tau_step_ref(norm, st, *t, t, tau);
 }
 
 __device__ __forceinline__ float sparse_prob(int norm, float z, float tau) {
@@ -139,6 +163,7 @@ enum DeviceError : int {
   kDevOk = 0,
   kDevBadPage = 1,
   kDevWaitTimeout = 2,
+  kDevBadLength = 3,
 };
 
 }  // namespace hfan

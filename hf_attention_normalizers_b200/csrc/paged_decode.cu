@@ -100,7 +100,7 @@ template <typename T, int D, int G>
 __global__ void __launch_bounds__(256, 2) decode_sm1_split(AttnParams p, DecodeWs ws) {
   using LN = Lanes<D>;
   const int b = blockIdx.y, split = blockIdx.x;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int t0 = split * kChunk;
   if (t0 >= L) return;
   const int t1 = min(L, t0 + kChunk);
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(288, 1)
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   const int b = blockIdx.y, split = blockIdx.x;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int t0 = split * kChunk;
   if (t0 >= L) return;
   const int t1 = min(L, t0 + kChunk);
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(288, 1)
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   const int b = blockIdx.y, split = blockIdx.x;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int t0 = split * kChunk;
   if (t0 >= L) return;
   const int t1 = min(L, t0 + kChunk);
@@ -605,7 +605,7 @@ template <typename T, int D, int G>
 __global__ void decode_sm1_combine(AttnParams p, DecodeWs ws) {
   const int b = blockIdx.y, hq = blockIdx.x;
   const int kvh = hq / G, h = hq % G;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int ns = (L + kChunk - 1) / kChunk;
   const int64_t base = ((int64_t)b * p.hkv + kvh) * ws.splits;
   float M = 0.f;  // the implicit zero logit
@@ -636,7 +636,7 @@ template <typename T, int D, int G, int NORM>
 __global__ void __launch_bounds__(256, 3) decode_sparse_scores(AttnParams p, DecodeWs ws, int max_len) {
   using LN = Lanes<D>;
   const int b = blockIdx.y, split = blockIdx.x;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int t0 = split * kChunk;
   if (t0 >= L) return;
   const int t1 = min(L, t0 + kChunk);
@@ -728,7 +728,7 @@ __global__ void __launch_bounds__(512) decode_sparse_tau(AttnParams p, DecodeWs 
   __shared__ int wcount[16];
   __shared__ float result[2];
   const int b = blockIdx.y, hq = blockIdx.x;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* srow = ws.scores + ((int64_t)b * p.hq + hq) * max_len;
   const float* zrow = srow;
@@ -811,7 +811,7 @@ template <typename T, int D, int G, int NORM>
 __global__ void __launch_bounds__(256) decode_sparse_pv(AttnParams p, DecodeWs ws, int max_len) {
   constexpr int DL = D / 32;  // dims per lane (4 or 2)
   const int b = blockIdx.y, split = blockIdx.x;
-  const int L = p.seq_lens[b];
+  const int L = seq_len_k(p, b);
   const int t0 = split * kChunk;
   if (t0 >= L) return;
   const int t1 = min(L, t0 + kChunk);
@@ -877,7 +877,7 @@ template <typename T, int D, int G>
 __global__ void decode_sparse_combine(AttnParams p, DecodeWs ws) {
   const int b = blockIdx.y, hq = blockIdx.x;
   const int kvh = hq / G, h = hq % G;
-  const int ns = (p.seq_lens[b] + kChunk - 1) / kChunk;
+  const int ns = (seq_len_k(p, b) + kChunk - 1) / kChunk;
   const int64_t base = ((int64_t)b * p.hkv + kvh) * ws.splits;
   T* orow = static_cast<T*>(p.o) + (int64_t)b * p.o_sb + (int64_t)hq * p.o_sh;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {

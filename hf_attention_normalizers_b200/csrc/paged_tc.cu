@@ -40,7 +40,7 @@ __global__ void gather_pages(AttnParams p, uint4* kd, uint4* vd, int lmax) {
     const int h = (int)((x / ((int64_t)chunks * lmax)) % p.hkv);
     const int b = (int)(x / ((int64_t)chunks * lmax * p.hkv));
     uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-    if (t < p.seq_lens[b]) {
+    if (t < seq_len_k(p, b)) {
       const int64_t row = cache_row(p, b, t);
       if (row >= 0) {
         const uint16_t* kc = static_cast<const uint16_t*>(p.k);
@@ -65,7 +65,7 @@ __global__ void scatter_grads(AttnParams p, const T* dkd, const T* dvd, int lmax
     const int t = (int)((x / p.d) % lmax);
     const int h = (int)((x / ((int64_t)p.d * lmax)) % p.hkv);
     const int b = (int)(x / ((int64_t)p.d * lmax * p.hkv));
-    if (t >= p.seq_lens[b]) continue;
+    if (t >= seq_len_k(p, b)) continue;
     const int64_t row = cache_row(p, b, t);
     if (row < 0) continue;
     atomicAdd(dk + row * p.dk_st + (int64_t)h * p.dk_sh + e, to_f32<T>(dkd[x]));

@@ -47,6 +47,17 @@ struct AttnParams {
   int* dev_status;       // first device-side error, see DeviceError
 };
 
+// Key count of sequence b in the paged and lens_only layouts, clamped to the
+// declared maximum len_k: a larger entry would index past the sequence's
+// block-table row and past its per-row scratch.  A clamped length records
+// kDevBadLength in the device status word.
+__device__ __forceinline__ int seq_len_k(const AttnParams& p, int b) {
+  const int L = p.seq_lens[b];
+  if (L >= 0 && L <= p.len_k) return L;
+  if (p.dev_status) atomicCAS(p.dev_status, kDevOk, kDevBadLength);
+  return L < 0 ? 0 : p.len_k;
+}
+
 __device__ __forceinline__ Geometry geometry(const AttnParams& p, int b) {
   Geometry g;
   if (p.cu_q != nullptr) {
@@ -58,7 +69,7 @@ __device__ __forceinline__ Geometry geometry(const AttnParams& p, int b) {
     g.q_start = b * p.len_q;
     g.q_len = p.len_q;
     g.k_start = 0;
-    g.k_len = (p.paged || p.lens_only) ? p.seq_lens[b] : p.len_k;
+    g.k_len = (p.paged || p.lens_only) ? seq_len_k(p, b) : p.len_k;
   }
   return g;
 }

@@ -504,13 +504,19 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // the same step; bar.red.or both synchronises and tells whether any row is
     // still iterating.  Every row thread must call it.  Returns true with the
     // exact root of the union in *out, or false with a lower bound of it.
-    auto union_solve = [&](const Cand& cdr, float t0, bool active, int max_iter, float* out, float* sup) -> bool {
+    // With around_max the sums are taken around zref (the row maximum, the
+    // same in every run), so that the exact root depends only on the support
+    // and the fixed summation order (buffer order within a warpgroup, then
+    // warpgroup order), not on the lower bound the search started from.
+    auto union_solve = [&](const Cand& cdr, float t0, bool active, int max_iter, float* out, float* sup,
+                           bool around_max = false, float zref = 0.f) -> bool {
       bool done = !active, exact = false;
       float tsol = t0;
       for (int it = 0;; ++it) {
         TauStats st{0.f, 0.f, 0.f, kPosInf};
+        const float rr = around_max ? zref : tsol;
         if (!done)
-          for (int e = 0; e < cdr.n; ++e) tau_accumulate(st, cbuf[e * 128 + row], tsol);
+          for (int e = 0; e < cdr.n; ++e) tau_accumulate_ref(st, cbuf[e * 128 + row], tsol, rr);
         float* xi = xch + 2048 + (it & 1) * (NWG * 512);  // [2][NWG][128][4]
         xi[(wg * 128 + row) * 4 + 0] = st.cnt;
         xi[(wg * 128 + row) * 4 + 1] = st.s1;
@@ -531,7 +537,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         float r;
         if (all.cnt == 0.f || it >= max_iter - 1) {
           done = true;
-        } else if (tau_step(NORM, all, &tsol, &r)) {
+        } else if (tau_step_ref(NORM, all, rr, &tsol, &r)) {
           done = true;
           exact = true;
           tsol = r;
@@ -686,7 +692,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       const bool empty = !(zrow > kNegInf);
       bool pending = !empty && ovf;  // overflowing rows go to whole-row sweeps
       float tsol = lower;
-      if (union_solve(cd, lower, !empty && !ovf, 64, &tsol, &support)) {
+      if (union_solve(cd, lower, !empty && !ovf, 64, &tsol, &support, true, zrow)) {
         tau = tsol;
       } else if (!empty && !ovf) {
         pending = true;  // did not converge: sweep the row
@@ -729,7 +735,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #pragma unroll
               for (int j = 0; j < COLS; ++j) {
                 const float z = sreg[j] * zs;
-                tau_accumulate(st, z, lower);
+                tau_accumulate_ref(st, z, lower, zrow);
                 if (z > lower) {
                   if (cd.n < CAPW) cbuf[cd.n * 128 + row] = z;
                   ++cd.n;
@@ -738,7 +744,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             } else {
               cd.n = CAPW + 1;
 #pragma unroll
-              for (int j = 0; j < COLS; ++j) tau_accumulate(st, sreg[j] * zs, lower);
+              for (int j = 0; j < COLS; ++j) tau_accumulate_ref(st, sreg[j] * zs, lower, zrow);
             }
           }
         }
@@ -765,13 +771,13 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         for (int w = 0; w < NWG; ++w) fits = fits && xo[w * 128 + row] == 0.f;
         named_bar_sync(1, NT);
         float tb, sb;
-        if (union_solve(cd, lower, fits, 64, &tb, &sb)) {
+        if (union_solve(cd, lower, fits, 64, &tb, &sb, true, zrow)) {
           tau = tb;
           support = sb;
           pending = false;
         } else if (pending && ok) {
           support = all.cnt;
-          pending = !tau_step(NORM, all, &lower, &tau);
+          pending = !tau_step_ref(NORM, all, zrow, &lower, &tau);
         }
       }
     }

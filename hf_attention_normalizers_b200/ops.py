@@ -152,6 +152,31 @@ def _attn_backward(ctx, do, dstats):
 torch.library.register_autograd("hfan::attn_fwd", _attn_backward, setup_context=_attn_setup)
 
 
+def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, normalizer: int, scale: float,
+                  causal: bool, window_left: int = -1) -> None:
+    """Forward into caller-owned outputs: ``o`` any [B, Hq, S, D] view with unit
+    D stride (for example one rank's slice of a head-major gather buffer), ``stats``
+    float32 [2, Hq, B * S].  No autograd; no allocation."""
+    _require_cuda(q, k, v, o, stats)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _ptr(stats),
+                                      _stream(q)), "hfan_attn_fwd")
+
+
+def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, corr: Tensor,
+                  dq: Tensor, dk: Tensor, dv: Tensor, normalizer: int, scale: float, causal: bool,
+                  window_left: int = -1) -> None:
+    """Backward into caller-owned gradient views (unit D stride) and a float32
+    [Hq, B * S] row-correction buffer.  No autograd; no allocation."""
+    _require_cuda(do, q, k, v, o, dq, dk, dv)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    with torch.cuda.device(q.device):
+        N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
+                                      _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
+                "hfan_attn_bwd")
+
+
 # ---------------------------------------------------------------------------
 # varlen
 # ---------------------------------------------------------------------------

@@ -172,6 +172,8 @@ int hfan_paged_decode(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor ke
  *     contents (every kernel overwrites the scratch it later reads, so nothing
  *     needs clearing).  Calls that overlap on the GPU (different streams, or
  *     different threads) race on it: serialise them.
+ *   - The looked-up address is kept for the life of the process: do not call
+ *     cudaDeviceReset on a device while this library is loaded.
  *   - Nothing here calls cudaMalloc, cudaFree or an allocating library. */
 int hfan_paged_decode_static(const hfan_paged_desc* desc, hfan_tensor q, hfan_tensor key_cache,
                              hfan_tensor value_cache, hfan_tensor o, float* stats, void* stream);
@@ -185,7 +187,8 @@ int hfan_rownorm_bwd(int32_t normalizer, int32_t dtype, int64_t rows, int64_t n,
                      void* dx, int64_t ld_dx, void* stream);
 
 /* Synchronises `stream`, then reads the device status word of the current
- * device (0 = no error, 1 = out-of-range page id, 2 = bounded wait expired)
+ * device (0 = no error, 1 = out-of-range page id, 2 = bounded wait expired,
+ * 3 = a sequence_lengths entry outside [0, max_len_k], clamped into that range)
  * into *out; clear != 0 resets it. */
 int hfan_device_status(int* out, int clear, void* stream);
 

@@ -242,33 +242,41 @@ def test_long_key_row_beyond_old_single_block_limit(norm):
     assert all(torch.isfinite(t).all() for t in (q.grad, k.grad, v.grad))
 
 
+TILE_ORDER_CASES = [
+    # (Hq, Hkv): whole tensor vs one KV group at a time
+    (8, 8),   # K/V and Q/dO 50 MB each: head-major whole, longest-first per head
+    (16, 4),  # K/V 25 MB (longest-first both ways, GQA heads adjacent); Q/dO 100 MB:
+              # the dK/dV kernel runs head-major whole and longest-first per group
+]
+
+
+@pytest.mark.parametrize("heads", TILE_ORDER_CASES)
 @pytest.mark.parametrize("norm", NORMS)
-def test_tile_orders_agree(norm):
+def test_tile_orders_agree(norm, heads):
     """The tensor-core kernels hand tiles out longest-first across heads when
-    the operand they re-read is at most 40 MB, else head by head.  Eight heads
-    of 12288 tokens (K/V and Q/dO 50 MB each) take the head-major order; each
-    head alone (6 MB) takes the longest-first one.  Heads are independent, so
-    both runs agree: softmax1 bit for bit; the sparse normalizers to within
-    the rounding of a threshold whose candidate sums can run in another order
-    (max difference <= 1e-2 of the largest value, mean <= 1e-5 of it).  The
-    last query tile is also checked against the oracle."""
-    q, k, v, do = _inputs((1, 8, 12288, 128), (1, 8, 12288, 128), torch.bfloat16, seed=21)
+    the operand they re-read is at most 40 MB, else head by head.  A whole
+    12288-token tensor and each of its KV groups alone take different orders;
+    heads are independent, so both runs agree bit for bit, for every
+    normalizer (the sparse threshold is summed in a fixed order around the row
+    maximum).  The whole tensor run twice is bit-identical too.  The last query
+    tile is also checked against the oracle."""
+    hq, hkv = heads
+    grp = hq // hkv
+    q, k, v, do = _inputs((1, hq, 12288, 128), (1, hkv, 12288, 128), torch.bfloat16, seed=21 + hq)
     whole = _run_dense(norm, q, k, v, do)
-    for h in range(8):
-        sl = slice(h, h + 1)
-        one = _run_dense(norm, q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(),
-                         do[:, sl].contiguous())
+    again = _run_dense(norm, q, k, v, do)
+    for label, a, b in zip(("o", "dq", "dk", "dv"), whole, again):
+        assert torch.equal(a, b), f"{norm}/rerun/{label}"
+    del again
+    for kh in range(hkv):
+        qs, ks = slice(kh * grp, (kh + 1) * grp), slice(kh, kh + 1)
+        one = _run_dense(norm, q[:, qs].contiguous(), k[:, ks].contiguous(), v[:, ks].contiguous(),
+                         do[:, qs].contiguous())
         for label, a, b in zip(("o", "dq", "dk", "dv"), whole, one):
-            a = a[:, sl]
-            if norm == "softmax1":
-                assert torch.equal(a, b), f"{norm}/head {h}/{label}"
-                continue
-            err = (a.double() - b.double()).abs()
-            top = float(b.double().abs().max()) + 1e-12
-            assert float(err.max()) <= 1e-2 * top and float(err.mean()) <= 1e-5 * top, \
-                f"{norm}/head {h}/{label}: max {float(err.max()):.3e} mean {float(err.mean()):.3e} top {top:.3e}"
-    ref = oracle.attention_forward(_np(q[:, :2, -128:]), _np(k[:, :2]), _np(v[:, :2]), norm, causal=True)
-    assert_close(whole[0][:, :2, -128:], ref, torch.bfloat16, f"{norm}/last tile")
+            a = a[:, qs] if label in ("o", "dq") else a[:, ks]
+            assert torch.equal(a, b), f"{norm}/group {kh}/{label}"
+    ref = oracle.attention_forward(_np(q[:, :grp, -128:]), _np(k[:, :1]), _np(v[:, :1]), norm, causal=True)
+    assert_close(whole[0][:, :grp, -128:], ref, torch.bfloat16, f"{norm}/last tile")
 
 
 @pytest.mark.parametrize("norm", NORMS)

@@ -1,6 +1,8 @@
 """Multi-rank host logic on CPU (gloo, world size 2): each rank computes the
-oracle attention of its KV-head block and the head all-gather reassembles the
-single-process result exactly."""
+oracle attention of its shard and the all-gather reassembles the
+single-process result exactly.  Dense / varlen prefill shard by KV-head group
+(head all-gather); paged decode shards the batch by greedy LPT on context
+length, each rank holding a compact pool of its own pages (batch all-gather)."""
 
 import os
 
@@ -10,7 +12,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from hf_attention_normalizers_b200.sharding import gather_heads, kv_group_shard
+from hf_attention_normalizers_b200.sharding import (gather_batch, gather_heads, kv_group_shard, lpt_partition,
+                                                    shard_paged_batch)
 
 
 def test_kv_group_shard_partitions_heads():
@@ -52,4 +55,61 @@ def test_two_rank_gloo_gather_matches_single_process(tmp_path):
     path = str(tmp_path / "result")
     port = 29500 + os.getpid() % 1000
     mp.spawn(_worker, args=(2, port, path), nprocs=2, join=True)
+    assert open(path).read() == "ok"
+
+
+def test_lpt_partition_balances_config4_contexts():
+    """BASELINE configs[3] contexts (seed 0): per-rank key counts within 1%."""
+    lens = torch.randint(1024, 32769, (256,), generator=torch.Generator().manual_seed(0)).tolist()
+    for world in (1, 2, 4, 8):
+        parts = lpt_partition(lens, world)
+        assert sorted(i for p in parts for i in p) == list(range(256))
+        loads = [sum(lens[i] for i in p) for p in parts]
+        assert max(loads) <= 1.01 * sum(lens) / world
+    assert lpt_partition([5, 1, 5, 3], 2) == [[0, 3], [1, 2]]
+
+
+def _paged_case():
+    g = torch.Generator().manual_seed(3)
+    bs, hkv, hq, d = 4, 2, 4, 8
+    lens = torch.tensor([9, 1, 17, 4, 12, 7, 3], dtype=torch.int64)
+    pages = [(int(x) + bs - 1) // bs for x in lens]
+    perm = torch.randperm(sum(pages), generator=g)
+    table = torch.zeros(len(lens), max(pages), dtype=torch.int64)
+    off = 0
+    for i, n in enumerate(pages):
+        table[i, :n] = perm[off:off + n]
+        off += n
+    kc = torch.randn(sum(pages) * bs, hkv, d, generator=g, dtype=torch.float64)
+    vc = torch.randn(sum(pages) * bs, hkv, d, generator=g, dtype=torch.float64)
+    q = torch.randn(len(lens), hq, 1, d, generator=g, dtype=torch.float64)
+    return q, kc, vc, table, lens, bs
+
+
+def _decode_worker(rank, world, port, result_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import oracle
+
+    q, kc, vc, table, lens, bs = _paged_case()
+    parts = lpt_partition(lens.tolist(), world)
+    ok = True
+    for name in ("softmax1", "sparsemax", "entmax15"):
+        sh = shard_paged_batch(kc, vc, table, lens, bs, parts[rank])
+        assert sh.key_cache.shape[0] == sum((int(lens[i]) + bs - 1) // bs for i in parts[rank]) * bs
+        o = oracle.paged_forward(q[list(sh.rows)].numpy(), sh.key_cache.numpy(), sh.value_cache.numpy(),
+                                 sh.block_table.numpy(), sh.seq_lens.numpy(), bs, name)
+        full = gather_batch(torch.from_numpy(o), parts)
+        ref = oracle.paged_forward(q.numpy(), kc.numpy(), vc.numpy(), table.numpy(), lens.numpy(), bs, name)
+        ok = ok and np.array_equal(full.numpy(), ref)
+    if rank == 0:
+        with open(result_path, "w") as f:
+            f.write("ok" if ok else "mismatch")
+    dist.destroy_process_group()
+
+
+def test_two_rank_gloo_lpt_decode_matches_single_process(tmp_path):
+    path = str(tmp_path / "result")
+    port = 30500 + os.getpid() % 1000
+    mp.spawn(_decode_worker, args=(2, port, path), nprocs=2, join=True)
     assert open(path).read() == "ok"
