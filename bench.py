@@ -151,18 +151,62 @@ def run_ours(args, rank, world, local_rank):
     t = {k: v.to(dev) for k, v in host.items()}
     flops_rank = causal_flops(B, hq, S, D)
 
-    def gather(*tensors):
-        if world == 1:
-            return
-        for x in tensors:
-            gather_heads(x, 1)
+    # Multi-GPU: every output and gradient is written by the kernels straight
+    # into this rank's block of a rank-major gather buffer [world, B, H_rank,
+    # S, D] (no packing copy) and all-gathered in place on NCCL's stream while
+    # the next kernels run.  Two buffer sets (by step parity): a set is
+    # rewritten only after the gathers that read it two steps earlier are done.
+    corr = torch.empty((hq, B * S), dtype=torch.float32, device=dev)
+    stats = {n: torch.empty((2, hq, B * S), dtype=torch.float32, device=dev) for n in NORMS}
+    masks = {n: torch.empty((ops.mask_words(N.NORMALIZER_IDS[n], hq, B, S, S),), dtype=torch.int32, device=dev)
+             for n in NORMS}
+    if world > 1:
+        from hf_attention_normalizers_b200.sharding import gather_heads_into
+
+        def gbuf(h):
+            return torch.empty((world, B, h, S, D), dtype=torch.bfloat16, device=dev)
+
+        sets = [{n: {"o": gbuf(hq), "dq": gbuf(hq), "dk": gbuf(hkv), "dv": gbuf(hkv)} for n in NORMS}
+                for _ in range(2)]
+        pending = [[], []]
+    state = {"i": 0}
 
     def step():
+        if world == 1:
+            for name in NORMS:
+                nid = N.NORMALIZER_IDS[name]
+                o, st, mk = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
+                ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1)
+            return
+        par = state["i"] % 2
+        state["i"] += 1
+        for w in pending[par]:
+            w.wait()  # the compute stream waits for the gathers of step i - 2
+        pending[par] = []
         for name in NORMS:
             nid = N.NORMALIZER_IDS[name]
-            o, st = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
-            dq, dk, dv = ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, nid, scale, True, -1)
-            gather(o, dq, dk, dv)
+            bf = sets[par][name]
+            o = bf["o"][rank]
+            ops.attn_fwd_into(t["q"], t["k"], t["v"], o, stats[name], nid, scale, True, mask=masks[name])
+            pending[par].append(gather_heads_into(bf["o"], async_op=True))
+            ops.attn_bwd_into(t["do"], t["q"], t["k"], t["v"], o, stats[name], corr, bf["dq"][rank],
+                              bf["dk"][rank], bf["dv"][rank], nid, scale, True, mask=masks[name])
+            for x in ("dq", "dk", "dv"):
+                pending[par].append(gather_heads_into(bf[x], async_op=True))
+
+    def drain():
+        if world > 1:
+            for par in range(2):
+                for w in pending[par]:
+                    w.wait()
+                pending[par] = []
+
+    def gather(*tensors):
+        if world == 1:
+            return []
+        from hf_attention_normalizers_b200.sharding import gather_stacked
+
+        return [gather_stacked(x, async_op=True)[1] for x in tensors]
 
     def barrier():
         if world > 1:
@@ -171,6 +215,7 @@ def run_ours(args, rank, world, local_rank):
 
     for _ in range(args.warmup):
         step()
+    drain()
     barrier()
     sampler = ClockSampler(local_rank)
     with sampler:
@@ -180,6 +225,7 @@ def run_ours(args, rank, world, local_rank):
         e0.record()
         for _ in range(args.steps):
             step()
+        drain()  # the last gathers belong to the timed region
         e1.record()
         barrier()
         sampler.stop()
@@ -198,7 +244,7 @@ def run_ours(args, rank, world, local_rank):
     phases = {}
     for name in NORMS:
         nid = N.NORMALIZER_IDS[name]
-        o, st = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
+        o, st, mk = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         reps = 3
         torch.cuda.synchronize()
@@ -207,14 +253,17 @@ def run_ours(args, rank, world, local_rank):
             ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
         ev[1].record()
         for _ in range(reps):
-            ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, nid, scale, True, -1)
+            ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1)
         ev[2].record()
         torch.cuda.synchronize()
         fwd = ev[0].elapsed_time(ev[1]) / reps
         bwd = ev[1].elapsed_time(ev[2]) / reps
         phases[name] = {"fwd_ms": round(fwd, 3), "bwd_ms": round(bwd, 3),
                         "fwd_tflops": round(flops_rank / fwd / 1e9, 1),
-                        "fwd_bwd_tflops": round(3.5 * flops_rank / (fwd + bwd) / 1e9, 1)}
+                        "fwd_bwd_tflops": round(3.5 * flops_rank / (fwd + bwd) / 1e9, 1),
+                        # share of the visible (64-row block, key tile) pairs whose
+                        # probabilities are all zero: the backward skips them
+                        "skipped_tile_frac": round(ops.tile_mask_skipped_fraction(mk, hq, B, S, S), 4)}
 
     # End to end through the public API: pinned host inputs copied in every
     # step, autograd forward + backward, loss read back to the host.  The
@@ -247,11 +296,16 @@ def run_ours(args, rank, world, local_rank):
             v = bufs[b]["v"].detach().requires_grad_(True)
             do = bufs[b]["do"]
             loss = 0.0
+            works = []
             for name in NORMS:
                 o = fns[name](q, k, v, is_causal=True)
                 o.backward(do)
-                gather(o.detach(), q.grad, k.grad, v.grad)  # as in step(): outputs and gradients all-gathered
+                # as in step(): outputs and gradients all-gathered (rank-major, no repacking)
+                works += gather(o.detach(), q.grad, k.grad, v.grad)
                 loss = loss + torch.sum(o * do, dtype=torch.float32)
+                q.grad = k.grad = v.grad = None
+            for w in works:
+                w.wait()
             free[b].record()
             float(loss.item())
 
@@ -268,16 +322,16 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = float(e2e_t.item())
     h2d = sum(x.numel() * x.element_size() for x in host.values())
 
-    if rank != 0:
-        return None
     burst, sustained, hbm, peak_kind = peaks()
     # Dominant single launch: the entmax15 forward (tc_fwd_kernel).  Its DRAM
-    # traffic comes from one ncu capture of `bench.py --shape 1,8192,8,2
-    # --profile-case` (dram__bytes_read.sum + dram__bytes_write.sum = 25.24 MB
-    # on that case, 1/16 of the (batch x head) units; scaled by 16).
+    # traffic comes from one ncu capture of `bench.py --shape 1,8192,32,8
+    # --profile-case` (Q+K+V+O = 168 MB, larger than L2): dram__bytes_read.sum
+    # + dram__bytes_write.sum = 101.5 + 35.7 MB on that case, one quarter of
+    # the config's (batch) units, so x4.  Reads are Q+K+V once; part of O is
+    # still in L2 when the launch ends.
     dom = phases["entmax15"]
     achieved = flops_rank / dom["fwd_ms"] / 1e9
-    traffic = 25.24e6 * 16 if (B, S, HQ, HKV) == (4, 8192, 32, 8) and world == 1 else None
+    traffic = 137.2e6 * 4 if (B, S, HQ, HKV) == (4, 8192, 32, 8) and world == 1 else None
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -299,65 +353,113 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"kernel": "tc_fwd_kernel<128,bf16,entmax15> (entmax15 forward, one launch)",
                      "bound": "tensor", "achieved": round(achieved, 1), "peak": sustained, "unit": "TFLOP/s",
                      "frac": round(achieved / sustained, 3), "peak_kind": f"{peak_kind} bf16 sustained",
-                     "traffic": traffic, "traffic_unit": "bytes per launch (ncu, small case x16)"},
+                     "traffic": traffic,
+                     "traffic_unit": "DRAM bytes per launch (ncu, B=1 case larger than L2, x4 batches)",
+                     "algorithmic_bytes": 2 * (B * HQ + B * HKV) * S * D * 2},
         "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "path": "kernels.hopper_{sparsemax,entmax15}_attention + autograd, pinned host inputs copied every step (copy stream, double-buffered prefetch of the next step)"},
         "gpu_launches": args.steps * len(NORMS) * 3,
         "clocks": sampler.summary(),
     }
+    extra = {}
     if args.decode:
-        line["paged_decode"] = bench_decode(dev, hbm)
-        line["varlen"] = bench_varlen(dev)
-        line["prescaled_worst_case"] = bench_prescaled(t, flops_rank)
+        if world > 1:
+            del sets
+        extra["paged_decode"] = bench_decode(dev, hbm, world=world, rank=rank)
+        extra["varlen"] = bench_varlen(dev, world=world, rank=rank)
+        if world == 1:
+            extra["prescaled_worst_case"] = bench_prescaled(t, flops_rank)
         del t
+        for bufs_ in (bufs,):
+            bufs_.clear()
         torch.cuda.empty_cache()
         try:
-            line["model_step"] = bench_model(dev)
+            extra["model_step"] = bench_model(dev, world=world, rank=rank)
         except Exception as exc:  # the prefill/decode line above stands on its own
-            line["model_step"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            extra["model_step"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    if rank != 0:
+        return None
+    line.update(extra)
     if args.cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
     return line
 
 
-def bench_decode(dev, hbm_peak, bsz=256, norms=("softmax1", "sparsemax", "entmax15")):
+def _max_over_ranks(ms, dev, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return ms
+    x = torch.tensor([ms], device=dev)
+    dist.all_reduce(x, op=dist.ReduceOp.MAX)
+    return float(x.item())
+
+
+def bench_decode(dev, hbm_peak, bsz=256, norms=("softmax1", "sparsemax", "entmax15"), world=1, rank=0):
     """paged decode, batch 256, contexts U[1024, 32768]
     (seed 0), 32-token pages in a randomly permuted pool (seed 1), 32 query /
     8 KV heads, D=128, bf16, one query token per sequence.  Reported as
     algorithmic GB/s: every valid page's K and V bytes plus q, o and the block
-    table, divided by the device time of one call."""
+    table, divided by the device time of one call.
+
+    With N ranks the batch is sharded by greedy LPT on context length; each
+    rank holds only its sequences' pages (its own pool and block table) and
+    the outputs are all-gathered back into batch order (2 MB) inside the timed
+    call.  Whole-job GB/s = all sequences' bytes / the slowest rank's time."""
     import torch
 
     from hf_attention_normalizers_b200 import _native as N
     from hf_attention_normalizers_b200 import ops
+    from hf_attention_normalizers_b200.sharding import batch_gather_order, gather_batch, lpt_partition
 
     page, hq, hkv, d = 32, 32, 8, 128
-    lens = torch.randint(1024, 32769, (bsz,), generator=torch.Generator().manual_seed(0))
+    lens_all = torch.randint(1024, 32769, (bsz,), generator=torch.Generator().manual_seed(0))
+    parts = lpt_partition(lens_all.tolist(), world)
+    mine = parts[rank]
+    lens = lens_all[mine]
     npages = [(int(x) + page - 1) // page for x in lens]
     pool = sum(npages)
-    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(1)).int()
-    table = torch.zeros(bsz, 1024, dtype=torch.int32)
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(1 + rank)).int()
+    table = torch.zeros(len(mine), 1024, dtype=torch.int32)
     off = 0
     for i, n in enumerate(npages):
         table[i, :n] = perm[off:off + n]
         off += n
-    gen = torch.Generator(device=dev).manual_seed(2)
+    gen = torch.Generator(device=dev).manual_seed(2 + rank)
     kc = torch.randn(pool * page, hkv, d, device=dev, generator=gen, dtype=torch.bfloat16)
     vc = torch.randn(pool * page, hkv, d, device=dev, generator=gen, dtype=torch.bfloat16)
-    q = torch.randn(bsz, hq, 1, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    qg = torch.Generator(device=dev).manual_seed(3)
+    q_all = torch.randn(bsz, hq, 1, d, device=dev, generator=qg, dtype=torch.bfloat16)
+    q = q_all[torch.tensor(mine, device=dev)].contiguous()
     table_d, lens_d = table.to(dev), lens.int().to(dev)
     max_len = int(lens.max())
-    kv_bytes = pool * page * hkv * d * 2 * 2
-    alg = kv_bytes + 2 * q.numel() * 2 + table.numel() * 4 + bsz * 4
+    pool_all = sum((int(x) + page - 1) // page for x in lens_all)
+    kv_bytes = pool_all * page * hkv * d * 2 * 2
+    alg = kv_bytes + 2 * q_all.numel() * 2 + bsz * 1024 * 4 + bsz * 4
+    order = batch_gather_order(parts) if world > 1 else None
     out = {"config": "BASELINE configs[3]" if bsz == 256 else f"configs[3] shape, batch {bsz}",
            "kv_gb": round(kv_bytes / 1e9, 3)}
+    if world > 1:
+        out["sharding"] = (f"batch by greedy LPT on context length over {world} ranks; per-rank pool and "
+                           "block table; outputs all-gathered (inside the timed call)")
+        out["rank0_kv_gb"] = round(pool * page * hkv * d * 4 / 1e9, 3)
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
-        f = lambda: ops.paged_fwd(q, kc, vc, table_d, lens_d, page, max_len, nid, d ** -0.5, True)
+
+        def f():
+            o, _ = ops.paged_fwd(q, kc, vc, table_d, lens_d, page, max_len, nid, d ** -0.5, True)
+            if world > 1:
+                gather_batch(o, parts, order=order)
+
         for _ in range(3):
             f()
         torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 5
         e0.record()
@@ -365,45 +467,67 @@ def bench_decode(dev, hbm_peak, bsz=256, norms=("softmax1", "sparsemax", "entmax
             f()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / reps
+        ms = _max_over_ranks(e0.elapsed_time(e1) / reps, dev, world)
         gbs = alg / (ms * 1e-3) / 1e9
-        out[name] = {"ms": round(ms, 3), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 3)}
+        out[name] = {"ms": round(ms, 3), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak / world, 3)}
+        if name != "softmax1":
+            # DRAM bytes of a sparse call: K once, the score rows, and V only for
+            # support keys -- 0.59 of the algorithmic bytes in an ncu capture of
+            # the same shape with 16 sequences (dram__bytes_read + write)
+            dram = 0.59 * alg
+            out[name]["dram_GB/s"] = round(dram / (ms * 1e-3) / 1e9, 1)
+            out[name]["dram_frac"] = round(dram / (ms * 1e-3) / 1e9 / hbm_peak / world, 3)
     out["note"] = ("sparsemax/entmax15 read V only for keys in the support, so their algorithmic GB/s "
-                   "can exceed the DRAM bandwidth")
+                   "can exceed the DRAM bandwidth; dram_GB/s / dram_frac count the bytes that reach DRAM "
+                   "(ncu ratio 0.59 of the algorithmic bytes); fractions are per GPU")
     return out
 
 
-def bench_varlen(dev, norms=("softmax1", "entmax15")):
+def bench_varlen(dev, norms=("softmax1", "entmax15"), world=1, rank=0):
     """64 packed sequences with lengths U[128, 4096]
     (seed 0), cu_seqlens_k = cu_seqlens_q, 16 query / 8 KV heads, D=128, bf16
-    N(0,1) (seed 0), causal; forward and backward device times per normalizer
-    through the varlen ops, in algorithmic TFLOP/s (fwd = 4 Hq D sum L(L+1)/2)."""
+    N(0,1) (seeded, generated on the device), causal; forward and backward
+    device times per normalizer through the varlen ops, in algorithmic TFLOP/s
+    (fwd = 4 Hq D sum L(L+1)/2).  With N ranks the KV-head groups are sharded
+    and o, dq, dk, dv are all-gathered (rank-major, inside the timed region);
+    the figures are whole-job, over the slowest rank's time."""
     import torch
 
     from hf_attention_normalizers_b200 import _native as N
     from hf_attention_normalizers_b200 import ops
+    from hf_attention_normalizers_b200.sharding import gather_stacked, kv_group_shard
 
-    hq, hkv, d = 16, 8, 128
+    HQv, HKVv, d = 16, 8, 128
+    sh = kv_group_shard(HQv, HKVv, world, rank)
+    hq, hkv = sh.q_hi - sh.q_lo, sh.kv_hi - sh.kv_lo
     lens = torch.randint(128, 4097, (64,), generator=torch.Generator().manual_seed(0))
     cu = torch.zeros(65, dtype=torch.int32)
     cu[1:] = torch.cumsum(lens, 0).int()
     tot, mx = int(cu[-1]), int(lens.max())
-    gen = torch.Generator(device="cpu").manual_seed(0)
-    q = torch.randn(tot, hq, d, generator=gen).to(torch.bfloat16).to(dev)
-    k = torch.randn(tot, hkv, d, generator=gen).to(torch.bfloat16).to(dev)
-    v = torch.randn(tot, hkv, d, generator=gen).to(torch.bfloat16).to(dev)
-    do = torch.randn(tot, hq, d, generator=gen).to(torch.bfloat16).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(10 + rank)
+    q = torch.randn(tot, hq, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    k = torch.randn(tot, hkv, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    v = torch.randn(tot, hkv, d, device=dev, generator=gen, dtype=torch.bfloat16)
+    do = torch.randn(tot, hq, d, device=dev, generator=gen, dtype=torch.bfloat16)
     cu_d = cu.to(dev)
-    flops = 4.0 * hq * d * float(sum(int(x) * (int(x) + 1) / 2 for x in lens))
+    flops = 4.0 * HQv * d * float(sum(int(x) * (int(x) + 1) / 2 for x in lens))
     out = {"config": "BASELINE configs[2]", "tokens": tot, "fwd_flop": flops}
+    if world > 1:
+        out["sharding"] = f"KV-head groups over {world} ranks; o, dq, dk, dv all-gathered"
+
+    def gathers(*xs):
+        if world == 1:
+            return []
+        return [gather_stacked(x, async_op=True)[1] for x in xs]
+
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
         fwd = lambda: ops.varlen_fwd(q, k, v, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
-        o, st = fwd()
-        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
+        o, st, mk = fwd()
+        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, mk, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
         bwd()
         torch.cuda.synchronize()
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         reps = 5
         ev[0].record()
         for _ in range(reps):
@@ -412,11 +536,24 @@ def bench_varlen(dev, norms=("softmax1", "entmax15")):
         for _ in range(reps):
             bwd()
         ev[2].record()
+        works = []
+        for _ in range(reps):  # the sharded step: forward, backward and the gathers
+            o2, _, _ = fwd()
+            works += gathers(o2)
+            works += gathers(*bwd())
+        for w in works:
+            w.wait()
+        ev[3].record()
         torch.cuda.synchronize()
-        f_ms, b_ms = ev[0].elapsed_time(ev[1]) / reps, ev[1].elapsed_time(ev[2]) / reps
+        f_ms = _max_over_ranks(ev[0].elapsed_time(ev[1]) / reps, dev, world)
+        b_ms = _max_over_ranks(ev[1].elapsed_time(ev[2]) / reps, dev, world)
+        s_ms = _max_over_ranks(ev[2].elapsed_time(ev[3]) / reps, dev, world)
         out[name] = {"fwd_ms": round(f_ms, 3), "bwd_ms": round(b_ms, 3),
                      "fwd_tflops": round(flops / f_ms / 1e9, 1),
                      "fwd_bwd_tflops": round(3.5 * flops / (f_ms + b_ms) / 1e9, 1)}
+        if world > 1:
+            out[name]["step_ms_with_gathers"] = round(s_ms, 3)
+            out[name]["step_tflops_with_gathers"] = round(3.5 * flops / s_ms / 1e9, 1)
     return out
 
 
@@ -433,22 +570,24 @@ def bench_prescaled(t, flops, norms=NORMS):
     out = {}
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
-        o, st = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
+        o, st, mk = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record()
         ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
         ev[1].record()
-        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, nid, D ** -0.5, True, -1)
+        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, mk, nid, D ** -0.5, True, -1)
         ev[2].record()
         torch.cuda.synchronize()
         f_ms, b_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
         out[name] = {"fwd_ms": round(f_ms, 3), "bwd_ms": round(b_ms, 3),
-                     "fwd_bwd_tflops": round(3.5 * flops / (f_ms + b_ms) / 1e9, 1)}
+                     "fwd_bwd_tflops": round(3.5 * flops / (f_ms + b_ms) / 1e9, 1),
+                     "skipped_tile_frac": round(ops.tile_mask_skipped_fraction(mk, qs.shape[1], qs.shape[0],
+                                                                               qs.shape[2], ks.shape[2]), 4)}
     return out
 
 
-def bench_model(dev, steps=3, warmup=2):
+def bench_model(dev, steps=3, warmup=2, world=1, rank=0):
     """BASELINE configs[4], one data-parallel replica: Qwen3-1.7B-shaped
     model (28 layers, hidden 2048, 16 query / 8 KV heads, D=128), random init
     (seed 0), bf16, one sequence of 4096 random tokens; a training step =
@@ -456,7 +595,10 @@ def bench_model(dev, steps=3, warmup=2):
     normalizer routed through set_softmax_attention_backend(..., "sdpa"),
     HF's own SDPA softmax as the reference point, the number of fused
     attention calls per step, and the attention share (the fused kernels
-    timed alone at the model's shapes x 28 layers / step time)."""
+    timed alone at the model's shapes x 28 layers / step time).  With N ranks
+    the model is data-parallel (DistributedDataParallel, NCCL all-reduce of the
+    gradients overlapped with the backward), one 4096-token sequence per rank;
+    tokens/s is whole-job over the slowest rank's step time."""
     import torch
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
@@ -474,22 +616,31 @@ def bench_model(dev, steps=3, warmup=2):
     torch.set_default_dtype(prev)
     model.train()
     seq = 4096
-    ids = torch.randint(0, cfg.vocab_size, (1, seq), generator=torch.Generator().manual_seed(0)).to(dev)
+    ids = torch.randint(0, cfg.vocab_size, (1, seq), generator=torch.Generator().manual_seed(rank)).to(dev)
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index], gradient_as_bucket_view=True)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-5, foreach=True)
-    calls = {"n": 0}
+    calls = {"n": 0, "skipped": []}
     real_fwd = ops.attn_fwd
 
     def counting_fwd(*a, **k):
         calls["n"] += 1
-        return real_fwd(*a, **k)
+        out_ = real_fwd(*a, **k)
+        if len(calls["skipped"]) < 28:  # the support masks of one step's layers (the model's activations)
+            q_, k_ = a[0], a[1]
+            calls["skipped"].append((out_[2], q_.shape[1], q_.shape[0], q_.shape[2], k_.shape[2]))
+        return out_
 
     def step():
-        loss = model(input_ids=ids, labels=ids).loss
+        loss = net(input_ids=ids, labels=ids).loss
         loss.backward()
         opt.step()
         opt.zero_grad(set_to_none=True)
 
-    out = {"config": "BASELINE configs[4] (one replica)", "tokens_per_step": seq}
+    out = {"config": "BASELINE configs[4]" + (f", data-parallel over {world} GPUs (DDP)" if world > 1
+                                                else " (one replica)"),
+           "tokens_per_step": seq * world}
     ops.attn_fwd = counting_fwd
     try:
         for norm in ("hf_sdpa_softmax", "softmax1", "sparsemax", "entmax15"):
@@ -501,28 +652,32 @@ def bench_model(dev, steps=3, warmup=2):
                 step()
             torch.cuda.synchronize()
             calls["n"] = 0
+            calls["skipped"] = []
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(steps):
                 step()
             e1.record()
             torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / steps
-            res = {"ms_per_step": round(ms, 2), "tokens_per_s": round(seq / ms * 1e3, 1),
+            ms = _max_over_ranks(e0.elapsed_time(e1) / steps, dev, world)
+            res = {"ms_per_step": round(ms, 2), "tokens_per_s": round(world * seq / ms * 1e3, 1),
                    "fused_attention_calls_per_step": calls["n"] // steps}
+            if norm in ("sparsemax", "entmax15") and calls["skipped"]:
+                fr = [ops.tile_mask_skipped_fraction(*x) for x in calls["skipped"]]
+                res["skipped_tile_frac_mean_over_layers"] = round(sum(fr) / len(fr), 4)
             if norm != "hf_sdpa_softmax":
                 nid = N.NORMALIZER_IDS[norm]
                 q = torch.randn(1, 16, seq, 128, device=dev, dtype=torch.bfloat16)
                 k = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
                 v = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
-                o, st = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
-                ops.attn_bwd(q, q, k, v, o, st, nid, 128 ** -0.5, True, -1)
+                o, st, mk = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1)
                 torch.cuda.synchronize()
                 a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a0.record()
                 for _ in range(28):
-                    o, st = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
-                    ops.attn_bwd(q, q, k, v, o, st, nid, 128 ** -0.5, True, -1)
+                    o, st, mk = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                    ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1)
                 a1.record()
                 torch.cuda.synchronize()
                 res["attention_ms"] = round(a0.elapsed_time(a1), 2)
@@ -646,11 +801,14 @@ def main():
             import torch
             import torch.distributed as dist
 
-            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
+            # NCCL's communicator lines (rank count, transports) go to the log
+            # ahead of the JSON line, which is printed last
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
         args.cpu_baseline = args.cpu_baseline and rank == 0 and world == 1 and not args.shape
-        args.decode = args.decode and world == 1 and not args.shape
+        args.decode = args.decode and not args.shape
         line = run_ours(args, rank, world, local_rank)
         if world > 1:
             import torch.distributed as dist

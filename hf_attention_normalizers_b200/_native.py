@@ -48,6 +48,9 @@ class AttnDesc(ctypes.Structure):
         ("causal", ctypes.c_int32),
         ("window_left", ctypes.c_int32),
         ("grad_dtype", ctypes.c_int32),
+        ("tile_mask", ctypes.c_void_p),
+        ("dropout_p", ctypes.c_float),
+        ("dropout_seed", ctypes.c_void_p),
     ]
 
 
@@ -77,6 +80,7 @@ _T = HfanTensor
 _P = ctypes.c_void_p
 SIGNATURES = {
     "hfan_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _T, _T, _T, _T, _P, _P]),
+    "hfan_attn_tile_mask_words": (ctypes.c_int64, [ctypes.POINTER(AttnDesc)]),
     "hfan_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _T, _T, _T, _T, _T, _P, _P, _T, _T, _T, _P]),
     "hfan_paged_fwd": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _P, _P]),
     "hfan_paged_bwd": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _T, _P, _P, _T, _T, _T, _P]),
@@ -92,7 +96,7 @@ SIGNATURES = {
     "hfan_abi_version": (ctypes.c_int, []),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 def library_path() -> str:

@@ -56,17 +56,24 @@ def _fused_name(softmax_fn) -> Optional[str]:
     return _FUSED_NAMES.get(softmax_fn)
 
 
-def _fused_bshd(query, key, value, normalizer, scale, is_causal, window_left=None) -> torch.Tensor:
+def _fused_bshd(query, key, value, normalizer, scale, is_causal, window_left=None,
+                dropout_p: float = 0.0) -> torch.Tensor:
     """Fused attention: q [B,Hq,S,D], k/v [B,Hkv,L,D] -> [B,S,Hq,D] contiguous."""
     from . import ops
+    from .kernels._fused import dropout_seed
 
     if query.shape[1] % key.shape[1] != 0:
         raise ValueError("Query heads must be divisible by key/value heads.")
     actual_scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
     window = -1 if window_left is None else int(window_left)
-    o, _ = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
-                        window, True)
+    o, _, _ = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
+                           window, True, float(dropout_p), dropout_seed(query, dropout_p))
     return o
+
+
+def _fused_dropout_ok(query: torch.Tensor, dropout_p: float) -> bool:
+    """Fused dropout runs on the 16-bit tensor-core kernels (head_dim 64 / 128)."""
+    return dropout_p == 0.0 or (query.dtype in (torch.float16, torch.bfloat16) and query.shape[-1] in (64, 128))
 
 
 def _repeat_kv(x: torch.Tensor, groups: int) -> torch.Tensor:
@@ -132,11 +139,12 @@ def sdpa_attention_forward(module: nn.Module, query: torch.Tensor, key: torch.Te
     name = _fused_name(softmax_fn)
     training = getattr(module, "training", False)
     square = query.shape[2] == key.shape[2]
-    if (name is not None and attention_mask is None and (dropout == 0.0 or not training) and query.is_cuda
+    drop = dropout if training else 0.0
+    if (name is not None and attention_mask is None and _fused_dropout_ok(query, drop) and query.is_cuda
             and (not is_causal or square)):
         # (the fused causal mask is bottom-right aligned; it equals this path's
         # top-left tril when the lengths agree)
-        return _fused_bshd(query, key, value, name, scaling, is_causal, kwargs.get("sliding_window")), None
+        return _fused_bshd(query, key, value, name, scaling, is_causal, kwargs.get("sliding_window"), drop), None
     out = scaled_dot_product_attention(query, key, value, softmax_fn=softmax_fn, attn_mask=attention_mask,
                                        dropout_p=dropout, scale=scaling, is_causal=is_causal,
                                        training=training, enable_gqa=key.shape[1] != query.shape[1])
@@ -179,15 +187,17 @@ def _fused_adapter(normalizer: str, label: str):
         sliding_window = kwargs.pop("sliding_window", None)
         for unused in ("block_n", "bisection_steps", "max_block_n"):
             kwargs.pop(unused, None)
-        if attention_mask is not None or not query.is_cuda:
+        drop = dropout if getattr(module, "training", False) else 0.0
+        check_dropout(drop)
+        if attention_mask is not None or not query.is_cuda or not _fused_dropout_ok(query, drop):
+            # (dropout on 32-bit inputs or other head sizes: materialised path)
             return sdpa_attention_forward(module, query, key, value, attention_mask, softmax_fn=fn,
                                           dropout=dropout, scaling=scaling, is_causal=is_causal, **kwargs)
         if query.shape[-3] % key.shape[-3] != 0:
             raise ValueError("Query heads must be divisible by key/value heads.")
         if is_causal is None:
             is_causal = query.shape[-2] > 1 and getattr(module, "is_causal", True)
-        check_dropout(dropout if getattr(module, "training", False) else 0.0)
-        return _fused_bshd(query, key, value, normalizer, scaling, is_causal, sliding_window), None
+        return _fused_bshd(query, key, value, normalizer, scaling, is_causal, sliding_window, drop), None
 
     forward.__name__ = label
     return forward

@@ -2,6 +2,7 @@
 // packing, kernel selection and error reporting.
 #include <cstdarg>
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -116,6 +117,16 @@ void set_grads(AttnParams& p, const hfan_tensor& d_o, const hfan_tensor& dq, con
   set_tensor(dv, &p.dv, &p.dv_sb, &p.dv_sh, &p.dv_st);
 }
 
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Words of the key-tile support mask (0: the request takes none).
+int64_t mask_words(const hfan_attn_desc& d) {
+  if (d.normalizer == HFAN_SOFTMAX1 || d.len_q <= 0 || d.len_k <= 0) return 0;
+  const int64_t tiles = ceil_div(d.len_k, 128);
+  if (tiles > 32 * 32) return 0;
+  return (int64_t)d.heads_q * d.batch * 2 * ceil_div(d.len_q, 128) * ((tiles + 31) / 32);
+}
+
 int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   if (desc == nullptr) return fail(HFAN_ERR_INVALID, "null descriptor");
   int rc = check_common(desc->dtype, desc->normalizer, desc->batch, desc->heads_q, desc->heads_kv,
@@ -140,6 +151,23 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   p.norm = desc->normalizer;
   p.grad_f32 = desc->grad_dtype == HFAN_FLOAT32;
   if (desc->cu_seqlens_q && desc->total_q < 0) return fail(HFAN_ERR_INVALID, "total_q must be >= 0");
+  if (!(desc->dropout_p >= 0.f && desc->dropout_p < 1.f)) return fail(HFAN_ERR_INVALID, "dropout_p must be in [0, 1).");
+  if (desc->dropout_p > 0.f) {
+    if (desc->dropout_seed == nullptr) return fail(HFAN_ERR_INVALID, "dropout_seed is required when dropout_p > 0");
+    if (desc->cu_seqlens_q != nullptr)
+      return fail(HFAN_ERR_UNSUPPORTED, "fused dropout is available for the dense layout only");
+    p.drop_thr24 = (uint32_t)std::ceil((double)desc->dropout_p * 16777216.0);
+    if (p.drop_thr24 == 0u) p.drop_thr24 = 1u;  // p > 0 but below 2^-24: drop the words below 1
+    p.drop_scale = 1.f / (1.f - desc->dropout_p);
+    p.drop_seed = desc->dropout_seed;
+  }
+  if (desc->tile_mask != nullptr) {
+    if (mask_words(*desc) == 0)
+      return fail(HFAN_ERR_INVALID, "tile_mask given for a request that takes none (see hfan_attn_tile_mask_words)");
+    p.tile_mask = desc->tile_mask;
+    p.mask_words = (int)((ceil_div(desc->len_k, 128) + 31) / 32);
+    p.mask_qb = 2 * (int)ceil_div(desc->len_q, 128);
+  }
   return HFAN_OK;
 }
 
@@ -209,10 +237,20 @@ int hfan_attn_fwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan
   p.stats = stats;
   if (desc->len_q == 0 || desc->len_k == 0 || p.rows_total == 0) return HFAN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = tc_supported(desc->dtype, p) ? tc_attention_fwd(desc->dtype, p, desc->len_q, s)
-                                                : simt_attention_fwd(desc->dtype, p, desc->len_q, s);
+  cudaError_t e;
+  if (tc_supported(desc->dtype, p)) {
+    e = tc_attention_fwd(desc->dtype, p, desc->len_q, s);
+  } else if (p.drop_thr24 != 0u) {
+    return fail(HFAN_ERR_UNSUPPORTED, "fused dropout needs 16-bit inputs with head_dim 64 or 128");
+  } else {
+    // the general kernels track no support: every tile counts as live
+    e = p.tile_mask ? cudaMemsetAsync(p.tile_mask, 0xff, mask_words(*desc) * 4, s) : cudaSuccess;
+    if (e == cudaSuccess) e = simt_attention_fwd(desc->dtype, p, desc->len_q, s);
+  }
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_attn_fwd");
 }
+
+int64_t hfan_attn_tile_mask_words(const hfan_attn_desc* desc) { return desc ? mask_words(*desc) : 0; }
 
 int hfan_attn_bwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan_tensor v,
                   hfan_tensor o, hfan_tensor d_o, const float* stats, float* corr,
@@ -231,6 +269,8 @@ int hfan_attn_bwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = tc_supported(desc->dtype, p) ? tc_attention_bwd(desc->dtype, p, desc->len_q, desc->len_k, s)
                                                 : cudaErrorNotSupported;
+  if (e == cudaErrorNotSupported && p.drop_thr24 != 0u)
+    return fail(HFAN_ERR_UNSUPPORTED, "fused dropout needs 16-bit inputs and gradients with head_dim 64 or 128");
   if (e == cudaErrorNotSupported) e = simt_attention_bwd(desc->dtype, p, desc->len_q, desc->len_k, s);
   return e == cudaSuccess ? HFAN_OK : cuda_fail(e, "hfan_attn_bwd");
 }

@@ -167,3 +167,43 @@ enum DeviceError : int {
 };
 
 }  // namespace hfan
+
+namespace hfan {
+
+// ---------------------------------------------------------------------------
+// Dropout mask: a counter-based generator, so that the forward and both
+// backward kernels regenerate the same keep bits from the saved seed instead
+// of storing a [B, H, Lq, Lk] mask (the reference does the same with Triton's
+// tl.rand, kernels/softmax1_hopper.py:105-110, sparse_entmax_hopper.py:141-145).
+//
+// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC 2011): ten rounds of two 32x32->64-bit products with the
+// multipliers 0xD2511F53 / 0xCD9E8D57, the key bumped by the Weyl constants
+// 0x9E3779B9 / 0xBB67AE85 between rounds.
+//
+// Element (row r, key j), r = (b * heads_q + h) * len_q + i: counter
+// (j / 4, r lo, r hi, 0), key (seed lo, seed hi), word j % 4; its top 24 bits
+// u give keep = u >= ceil(p 2^24) (i.e. uniform >= p).  Four consecutive keys
+// of a row share one generator call.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// Keep bits (bit e = key 4 g + e) of one group of four keys of row r.
+__device__ __forceinline__ uint32_t dropout_keep4(uint64_t r, uint32_t g, uint32_t seed_lo, uint32_t seed_hi,
+                                                  uint32_t thr24) {
+  const uint4 x = philox4x32_10(make_uint4(g, (uint32_t)r, (uint32_t)(r >> 32), 0u), seed_lo, seed_hi);
+  return ((x.x >> 8) >= thr24 ? 1u : 0u) | ((x.y >> 8) >= thr24 ? 2u : 0u) | ((x.z >> 8) >= thr24 ? 4u : 0u) |
+         ((x.w >> 8) >= thr24 ? 8u : 0u);
+}
+
+}  // namespace hfan

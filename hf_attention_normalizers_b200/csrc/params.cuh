@@ -40,6 +40,19 @@ struct AttnParams {
   int paged;
   int lens_only;           // dense K/V whose per-sequence key lengths come from seq_lens
   int tile_lpt;            // tensor-core kernels: hand tiles out longest-first across the whole grid
+  // Sparse normalizers: key tiles with support, one bit per (query head,
+  // sequence, 64-row block, 128-key tile), written by the tensor-core forward
+  // and read by the backward to skip tiles whose probabilities are all zero.
+  // Word ((h * batch + b) * mask_qb + block) * mask_words + tile / 32; null: none.
+  uint32_t* tile_mask;
+  int mask_words, mask_qb;
+  // Dropout (dense layout, tensor-core kernels): an element survives when the
+  // top 24 bits of its generator word are >= drop_thr24 (= ceil(p 2^24); 0: no
+  // dropout) and is then scaled by drop_scale = 1 / (1 - p).  The seed is read
+  // from device memory (see dropout_keep4 in common.cuh).
+  uint32_t drop_thr24;
+  float drop_scale;
+  const int64_t* drop_seed;
 
   float scale;
   int causal, window_left, norm;

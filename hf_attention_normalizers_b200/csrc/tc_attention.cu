@@ -106,7 +106,8 @@ struct Layout {
   static constexpr uint32_t CTL = BARS + sizeof(Bars);
   static constexpr uint32_t XCH_FLOATS = 6144 + 4 * 128;             // warpgroup exchange
   static constexpr uint32_t XCH = (CTL + sizeof(Ctl) + 15) & ~15u;
-  static constexpr uint32_t TOTAL = XCH + XCH_FLOATS * 4 + 1024;      // + alignment slack
+  static constexpr uint32_t MASK = XCH + XCH_FLOATS * 4;               // [2 row halves][kMaskWordsMax] key-tile bits
+  static constexpr uint32_t TOTAL = MASK + 2 * kMaskWordsMax * 4 + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ void record_error(const AttnParams& p, Ctl* ctl, int code) {
@@ -246,7 +247,7 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
 }
 
 // ------------------------------------------------------------------ kernel
-template <int HD, bool BF16, int NORM>
+template <int HD, bool BF16, int NORM, bool DROP>
 __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
@@ -275,6 +276,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + L::BARS);
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + L::CTL);
+  // Key tiles with any p > 0, per 64-row half of the tile (sparse final pass):
+  // set by the row warps and written to p.tile_mask for the backward.
+  uint32_t* sbits = reinterpret_cast<uint32_t*>(smem + L::MASK);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint3 tile = tile_coords(p.tile_lpt);
@@ -296,6 +300,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
   k_lo = (k_lo / kBN) * kBN;
   const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kBN - 1) / kBN : 0;
+  const int kt0 = k_lo / kBN;  // absolute index of the first key tile
+  // the support bits of every key tile fit in shared memory (and are wanted)
+  const bool track = SPARSE && p.tile_mask != nullptr && kt0 + n_tiles <= 32 * kMaskWordsMax;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
@@ -315,6 +322,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     ctl->abort = 0;
     ctl->next_pass = kPassFinal;
     ctl->any_pending = 0;
+    for (int w = 0; w < 2 * kMaskWordsMax; ++w) sbits[w] = 0u;
     fence_barrier_init();
   }
   if (warp == Roles<HD>::MMA_WARP) tmem_alloc(&ctl->tmem_base, 512);
@@ -789,6 +797,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // ---- final pass: P and O
     float m_ref = 0.f, l = wg == 0 ? 1.f : 0.f;  // the implicit zero logit counts once
     const float ntau = -tau;
+    // Dropout: P V uses p * keep / (1 - p_drop); the softmax1 denominator and
+    // the sparse thresholds use the undropped probabilities.
+    constexpr bool drop = DROP;  // a separate instantiation: no cost without dropout
+    uint32_t seed_lo = 0u, seed_hi = 0u;
+    uint64_t drow = 0;
+    if (drop) {
+      const uint64_t sd = (uint64_t)*p.drop_seed;
+      seed_lo = (uint32_t)sd;
+      seed_hi = (uint32_t)(sd >> 32);
+      drow = ((uint64_t)b * p.hq + h) * p.len_q + (row_ok ? i : 0);
+    }
     // softmax1 meets a named barrier on every tile, so after a timeout the loop
     // keeps running (with the work skipped) instead of leaving it.
 #ifdef HFAN_DIAG
@@ -832,6 +851,21 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           if (NORM != HFAN_SPARSEMAX) d = fmul2(d, d);
           sreg[j] = f2_lo(d);
           sreg[j + 1] = f2_hi(d);
+        }
+        if (track) {  // this warp's 32 rows x COLS keys: any p > 0 sets the tile's bit for its 64-row half
+          const unsigned bal = __ballot_sync(0xffffffffu, max_n<COLS>(sreg) > 0.f);
+          const int kt = kt0 + t;
+          if (lane == 0 && bal != 0u)
+            atomicOr(&sbits[((warp & 3) >> 1) * kMaskWordsMax + (kt >> 5)], 1u << (kt & 31));
+        }
+      }
+      if (drop) {
+        const int kb = k_lo + t * kBN + wg * COLS;  // a multiple of 4: groups of four keys
+#pragma unroll
+        for (int g4 = 0; g4 < COLS / 4; ++g4) {
+          const uint32_t keep = dropout_keep4(drow, (uint32_t)((kb >> 2) + g4), seed_lo, seed_hi, p.drop_thr24);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sreg[4 * g4 + e] *= ((keep >> e) & 1u) ? p.drop_scale : 0.f;
         }
       }
       if (!ok) continue;
@@ -882,6 +916,14 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     }
 #endif
     if (!ok) record_error(p, ctl, kDevWaitTimeout);
+    if (SPARSE && track && p.tile_mask != nullptr) {
+      named_bar_sync(1, NT);  // every row warp's support bits are in
+      if (threadIdx.x < 2 * p.mask_words) {
+        const int half = threadIdx.x / p.mask_words, w = threadIdx.x % p.mask_words;
+        p.tile_mask[((int64_t)(h * p.batch + b) * p.mask_qb + 2 * qt + half) * p.mask_words + w] =
+            sbits[half * kMaskWordsMax + w];
+      }
+    }
     if (!SPARSE) {
       // total denominator of the row
       float* xl = xch + 2 * NWG * 128;
@@ -962,24 +1004,26 @@ cudaError_t launch_fwd(const AttnParams& p, int max_q, cudaStream_t stream) {
   dim3 grid((max_q + kBM - 1) / kBM, p.hq, p.batch);
   AttnParams pl = p;  // query tiles re-read K and V
   pl.tile_lpt = (varlen ? tk_n : (int64_t)p.batch * tk_n) * p.hkv * HD * 4 <= kLptMaxReread;
+  auto go = [&](auto kernel) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kernel<<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
+    return cudaSuccess;
+  };
+  const bool drop = p.drop_thr24 != 0u;
   cudaError_t e;
   switch (p.norm) {
     case HFAN_SOFTMAX1:
-      e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
+      e = drop ? go(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1, true>) : go(tc_fwd_kernel<HD, BF16, HFAN_SOFTMAX1, false>);
       break;
     case HFAN_SPARSEMAX:
-      e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
+      e = drop ? go(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX, true>) : go(tc_fwd_kernel<HD, BF16, HFAN_SPARSEMAX, false>);
       break;
     default:
-      e = cudaFuncSetAttribute(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, Roles<HD, 2>::THREADS, smem, stream>>>(tq, tk, tv, pl);
+      e = drop ? go(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15, true>) : go(tc_fwd_kernel<HD, BF16, HFAN_ENTMAX15, false>);
       break;
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -60,6 +60,7 @@ __device__ __forceinline__ void weight(float z, float st0, float inv_l, float* w
 
 // =========================================================== dq kernel
 constexpr int kQStagesK = 3;  // K stays resident until its dQ MMA: one stage deeper than V
+constexpr int kTileListMax = 512;  // key tiles a dQ CTA can skip over (65536 keys)
 constexpr int kQStagesV = 2;
 
 struct QBars {
@@ -77,10 +78,11 @@ struct QLayout {
   static constexpr uint32_t V = K + kQStagesK * NH * kHalf;
   static constexpr uint32_t BARS = V + kQStagesV * NH * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(QBars);
-  static constexpr uint32_t TOTAL = CTL + 16 + 1024;
+  static constexpr uint32_t LIST = CTL + 16;                   // [kTileListMax] active key tiles, increasing
+  static constexpr uint32_t TOTAL = LIST + kTileListMax * 2 + 1024;
 };
 
-template <int HD, bool BF16, int NORM>
+template <int HD, bool BF16, int NORM, bool DROP>
 __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -99,6 +101,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   QBars* bars = reinterpret_cast<QBars*>(smem + L::BARS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::CTL);
   int* abort_ptr = reinterpret_cast<int*>(smem + L::CTL + 4);
+  int* nact_ptr = reinterpret_cast<int*>(smem + L::CTL + 8);
+  uint16_t* tlist = reinterpret_cast<uint16_t*>(smem + L::LIST);
   volatile int* abort_flag = abort_ptr;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -121,6 +125,34 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
   k_lo = (k_lo / kBN) * kBN;
   const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kBN - 1) / kBN : 0;
+  // Sparse normalizers skip the key tiles where every probability of the 128
+  // rows is zero (no S, dP or dQ work: w = 0 there).  Warp 0 ORs the
+  // forward's bits of the two 64-row blocks (lane = word) and writes the
+  // active tiles, relative to k_lo, in increasing order to tlist.
+  const int kt0 = k_lo / kBN;
+  const bool use_mask = SPARSE && p.tile_mask != nullptr && kt0 + n_tiles <= kTileListMax;
+  if (warp == 0) {
+    uint32_t bits = 0u;
+    if (use_mask && lane < p.mask_words) {
+      const uint32_t* m = p.tile_mask + ((int64_t)(h * p.batch + b) * p.mask_qb + 2 * qt) * p.mask_words;
+      bits = m[lane] | m[p.mask_words + lane];
+      const int lo = kt0 - 32 * lane, hi = kt0 + n_tiles - 32 * lane;  // keep tiles [kt0, kt0 + n_tiles)
+      if (lo > 0) bits = lo >= 32 ? 0u : bits & (~0u << lo);
+      if (hi < 32) bits = hi <= 0 ? 0u : bits & (~0u >> (32 - hi));
+    }
+    const int c = __popc(bits);
+    int pre = c;  // inclusive prefix sum over the lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, pre, o);
+      if (lane >= o) pre += y;
+    }
+    const int total = __shfl_sync(0xffffffffu, pre, 31);
+    int pos = pre - c;
+    for (uint32_t rest = bits; rest != 0u; rest &= rest - 1u)
+      tlist[pos++] = (uint16_t)(32 * lane + __ffs(rest) - 1 - kt0);
+    if (lane == 0) *nact_ptr = use_mask ? total : n_tiles;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->qd_full, 1);
@@ -150,9 +182,13 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   // TMEM: S [0, 128), dP [128, 256), dQ [256, 256 + HD), dS double buffer
   // [384, 512) as packed 16-bit pairs (the A operand of the dQ MMA)
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dq = tmem + 256, tmem_ds = tmem + 384;
+  // Active key tiles (relative index t, in increasing order): every role walks
+  // the same list; ring stages and buffer parities count list positions.
+  const int n_act = *nact_ptr;
+  auto tile_at = [&](int a) -> int { return use_mask ? (int)tlist[a] : a; };
 
   if (warp == Roles<HD>::TMA_WARP) {
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0 && n_act > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
       prefetch_tmap(&tm_k);
@@ -165,8 +201,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       bool ok = true;
       uint32_t kc = 0;
       for (int pass = 0; pass < NPASS && ok; ++pass) {
-        for (int t = 0; t < n_tiles && ok; ++t) {
-          const int kb = k_lo + t * kBN;
+        for (int a = 0; a < n_act && ok; ++a) {
+          const int kb = k_lo + tile_at(a) * kBN;
           const int ks = kc % kQStagesK, vs = kc % kQStagesV;
           if (!(ok = mbar_wait(&bars->k_empty[ks], ((kc / kQStagesK) & 1) ^ 1, abort_flag))) break;
           mbar_arrive_expect_tx(&bars->k_full[ks], TILE);
@@ -189,14 +225,14 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   } else if (warp == Roles<HD>::MMA_WARP) {
     // S and dP issuer (every pass).  dQ has its own issuer warp, so that the
     // waits of one overlap the tensor work of the other.
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0 && n_act > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
       bool ok = mbar_wait(&bars->qd_full, 0, abort_flag);
       uint32_t kc = 0, sdc = 0;
       for (int pass = 0; pass < NPASS && ok; ++pass) {
         const bool last = pass == NPASS - 1;
-        for (int t = 0; t < n_tiles && ok; ++t) {
+        for (int a = 0; a < n_act && ok; ++a) {
           const int s = kc % kQStagesK, vs = kc % kQStagesV;
           if (!(ok = mbar_wait(&bars->k_full[s], (kc / kQStagesK) & 1, abort_flag))) break;
           if (!(ok = mbar_wait(&bars->v_full[vs], (kc / kQStagesV) & 1, abort_flag))) break;
@@ -231,11 +267,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // dQ += dS K issuer (last pass).  K(t) sits in stage ((NPASS - 1) n + t) % 3;
     // it was loaded before S(t), which preceded dS(t).  dS(t) is read from
     // TMEM buffer t & 1.
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0 && n_act > 0) {
       const uint32_t k_base = smem_u32(smem + L::K);
       bool ok = true;
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        const int s = ((NPASS - 1) * n_tiles + t) % kQStagesK;
+      for (int t = 0; t < n_act && ok; ++t) {  // t: position in the active list
+        const int s = ((NPASS - 1) * n_act + t) % kQStagesK;
         const int db = t & 1;
         if (!(ok = mbar_wait(&bars->ds_full[db], (t >> 1) & 1, abort_flag))) break;
         tc_fence_after();
@@ -340,6 +376,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // st0 (one packed FMA per pair; masked keys -> -inf, applied only on
     // tiles the mask cuts) and dP.
     const uint64_t zs2 = f2_pack(zs, zs), nst2 = f2_pack(-st0, -st0), il2 = f2_pack(inv_l, inv_l);
+    // Dropout: the gradient reaching p is dP keep / (1 - p_drop) (same keep
+    // bits as the forward, regenerated from the seed).
+    constexpr bool drop = DROP;  // a separate instantiation: no cost without dropout
+    uint32_t seed_lo = 0u, seed_hi = 0u;
+    uint64_t drow = 0;
+    if (drop) {
+      const uint64_t sd = (uint64_t)*p.drop_seed;
+      seed_lo = (uint32_t)sd;
+      seed_hi = (uint32_t)(sd >> 32);
+      drow = ((uint64_t)b * p.hq + h) * p.len_q + (row_ok ? i : 0);
+    }
     auto chunk = [&](int t, int cidx, uint64_t (&x)[16], uint64_t (&dv)[16]) {
       uint32_t rs[32], rd[32];
       tmem_ld32(tmem_s + lane_addr + cidx * 32, rs);
@@ -351,6 +398,16 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         dv[jp] = f2_pack(__uint_as_float(rd[2 * jp]), __uint_as_float(rd[2 * jp + 1]));
       }
       const int kb = k_lo + t * kBN + cidx * 32;
+      if (drop) {
+#pragma unroll
+        for (int g4 = 0; g4 < 8; ++g4) {
+          const uint32_t keep = dropout_keep4(drow, (uint32_t)((kb >> 2) + g4), seed_lo, seed_hi, p.drop_thr24);
+          const float k0 = (keep & 1u) ? p.drop_scale : 0.f, k1 = (keep & 2u) ? p.drop_scale : 0.f;
+          const float k2 = (keep & 4u) ? p.drop_scale : 0.f, k3 = (keep & 8u) ? p.drop_scale : 0.f;
+          dv[2 * g4] = fmul2(dv[2 * g4], f2_pack(k0, k1));
+          dv[2 * g4 + 1] = fmul2(dv[2 * g4 + 1], f2_pack(k2, k3));
+        }
+      }
       const int lo = vis_lo - kb, hi = vis_hi - kb;
       if (!__all_sync(0xffffffffu, lo <= 0 && hi >= 32)) {
 #pragma unroll
@@ -371,7 +428,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 
     if (SPARSE) {
       float num = 0.f, den = 0.f;
-      for (int t = 0; t < n_tiles && ok; ++t) {
+      for (int a = 0; a < n_act && ok; ++a) {
+        const int t = tile_at(a);
         if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
         tc_fence_after();
         uint64_t num2 = 0, den2 = 0;
@@ -400,7 +458,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     }
     if (row_ok && wg == 0) p.corr[si] = c;
 
-    for (int t = 0; t < n_tiles && ok; ++t) {
+    for (int a = 0; a < n_act && ok; ++a) {
+      const int t = tile_at(a);
       if (!(ok = wait_warp(&bars->sdp_full, sdc & 1, abort_flag))) break;
       tc_fence_after();
       uint32_t pk[COLS / 2];
@@ -426,10 +485,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         }
       }
       ++sdc;
-      // dS(t) -> TMEM buffer t & 1, free once dQ(t - 2) has completed
-      const int db = t & 1;
-      if (t >= 2) {
-        if (!(ok = wait_warp(&bars->ds_empty[db], ((t >> 1) & 1) ^ 1, abort_flag))) break;
+      // dS of list position a -> TMEM buffer a & 1, free once the dQ of
+      // position a - 2 has completed
+      const int db = a & 1;
+      if (a >= 2) {
+        if (!(ok = wait_warp(&bars->ds_empty[db], ((a >> 1) & 1) ^ 1, abort_flag))) break;
         tc_fence_after();
       }
 #pragma unroll
@@ -438,7 +498,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       tc_fence_before();
       warp_arrive(&bars->ds_full[db]);
     }
-    if (ok && n_tiles > 0) {
+    if (ok && n_act > 0) {
       ok = wait_warp(&bars->dq_done, 0, abort_flag);
       tc_fence_after();
     }
@@ -451,11 +511,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     for (int cc = 0; cc < 1; ++cc) {
       const int cidx = wg;  // warpgroup wg stores head-dim columns [32 wg, 32 wg + 32)
       uint32_t r[32];
-      if (n_tiles > 0) {
+      if (n_act > 0) {
         tmem_ld32(tmem_dq + lane_addr + cidx * 32, r);
         tmem_wait_ld();
       }
-      if (n_tiles == 0 || !ok) {
+      if (n_act == 0 || !ok) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) r[j] = 0u;
       }
@@ -494,6 +554,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 constexpr int kQB = 64;        // query rows per unit
 constexpr int kQStages = 3;    // Q / dO ring depth
 constexpr uint32_t kQHalf = kQB * 128u;  // one 64-row x 128-byte swizzled half tile
+constexpr int kUnitWords = 64;           // support bits of up to 2048 units per key tile
 
 struct KBars {
   uint64_t kv_full;
@@ -513,10 +574,11 @@ struct KLayout {
   static constexpr uint32_t STATS = PD + 2 * kHalf;              // 2 buffers x 3 x 64 floats
   static constexpr uint32_t BARS = STATS + 2 * 3 * kQB * 4;
   static constexpr uint32_t CTL = BARS + sizeof(KBars);
-  static constexpr uint32_t TOTAL = CTL + 16 + 1024;
+  static constexpr uint32_t MASK = CTL + 16;                   // [kUnitWords] units with support
+  static constexpr uint32_t TOTAL = MASK + kUnitWords * 4 + 1024;
 };
 
-template <int HD, bool BF16, int NORM>
+template <int HD, bool BF16, int NORM, bool DROP>
 __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -559,6 +621,25 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   const int m_hi = i_hi > i_lo ? (i_hi + kQB - 1) / kQB : m_lo;
   const int n_m = m_hi - m_lo;
   const int n_units = groups * n_m;
+  // Sparse normalizers skip the units whose probabilities against this key
+  // tile are all zero (the forward's bit of (query head, 64-row block, tile)).
+  uint32_t* ubits = reinterpret_cast<uint32_t*>(smem + L::MASK);
+  const bool use_mask = NORM != HFAN_SOFTMAX1 && p.tile_mask != nullptr && n_units <= 32 * kUnitWords;
+  if (use_mask) {
+    const int kt = tile.x;
+    for (int wi = warp; wi < (n_units + 31) / 32; wi += blockDim.x / 32) {
+      const int u = wi * 32 + lane;
+      bool bit = false;
+      if (u < n_units) {
+        const int hq = kvh * groups + u / n_m, m = m_lo + u % n_m;
+        const uint32_t word =
+            p.tile_mask[((int64_t)(hq * p.batch + b) * p.mask_qb + m) * p.mask_words + (kt >> 5)];
+        bit = ((word >> (kt & 31)) & 1u) != 0u;
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, bit);
+      if (lane == 0) ubits[wi] = bal;
+    }
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
@@ -586,9 +667,20 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   // TMEM: S^T buffers [0, 64) and [64, 128), dP^T buffers [128, 192) and
   // [192, 256), dV [256, 256 + HD), dK [256 + HD, 256 + 2 HD)
   const uint32_t tmem_s = tmem, tmem_dp = tmem + 128, tmem_dv = tmem + 256, tmem_dk = tmem + 256 + HD;
+  // Active units in increasing order; every role walks the same list, and
+  // ring stages and buffer parities count list positions.
+  const uint32_t* ubits_or_all = use_mask ? ubits : nullptr;
+  const bool has_units = BitWalk(ubits_or_all, n_units).next() < n_units;
+  // number of active units (the MMA issuers count list positions only)
+  auto count_units = [&]() -> int {
+    if (!use_mask) return n_units;
+    int c = 0;
+    for (int w = 0; w < (n_units + 31) / 32; ++w) c += __popc(ubits[w]);
+    return c;
+  };
 
   if (warp == Roles<HD>::TMA_WARP) {
-    if (lane == 0 && n_units > 0) {
+    if (lane == 0 && has_units) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_do);
       prefetch_tmap(&tm_k);
@@ -599,11 +691,12 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         tma_load_4d(smem + L::V + hh * kHalf, &tm_v, &bars->kv_full, 64 * hh, ktok, kvh, bcoord);
       }
       bool ok = true;
-      for (int u = 0; u < n_units && ok; ++u) {
+      BitWalk walk(ubits_or_all, n_units);
+      for (int a = 0, u = walk.next(); u < n_units && ok; ++a, u = walk.next()) {
         const int hq = kvh * groups + u / n_m;
         const int m = m_lo + u % n_m;
-        const int s = u % kQStages;
-        if (!(ok = mbar_wait(&bars->qd_empty[s], ((u / kQStages) & 1) ^ 1, abort_flag))) break;
+        const int s = a % kQStages;
+        if (!(ok = mbar_wait(&bars->qd_empty[s], ((a / kQStages) & 1) ^ 1, abort_flag))) break;
         mbar_arrive_expect_tx(&bars->qd_full[s], 2 * QTILE);
         for (int hh = 0; hh < NH; ++hh) {
           tma_load_4d(smem + L::Q + s * QTILE + hh * kQHalf, &tm_q, &bars->qd_full[s], 64 * hh, qtok0 + m * kQB, hq,
@@ -619,14 +712,15 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     }
   } else if (warp == Roles<HD>::MMA_WARP) {
     // S^T and dP^T issuer
-    if (lane == 0 && n_units > 0) {
+    if (lane == 0 && has_units) {
       const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       bool ok = mbar_wait(&bars->kv_full, 0, abort_flag);
-      for (int u = 0; u < n_units && ok; ++u) {
-        const int s = u % kQStages, bf = u & 1;
-        if (!(ok = mbar_wait(&bars->qd_full[s], (u / kQStages) & 1, abort_flag))) break;
-        if (!(ok = mbar_wait(&bars->sdp_empty[bf], ((u >> 1) & 1) ^ 1, abort_flag))) break;
+      const int n_act = count_units();
+      for (int a = 0; a < n_act && ok; ++a) {
+        const int s = a % kQStages, bf = a & 1;
+        if (!(ok = mbar_wait(&bars->qd_full[s], (a / kQStages) & 1, abort_flag))) break;
+        if (!(ok = mbar_wait(&bars->sdp_empty[bf], ((a >> 1) & 1) ^ 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -651,25 +745,26 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // dV += P^T dO and dK += dS^T Q per unit; then the P^T / dS^T tiles and
     // the unit's Q / dO stage are free (the unit's S^T / dP^T products
     // completed before P^T existed).
-    if (lane == 0 && n_units > 0) {
+    if (lane == 0 && has_units) {
       const uint32_t q_base = smem_u32(smem + L::Q), do_base = smem_u32(smem + L::DO);
       const uint32_t pp_base = smem_u32(smem + L::PP), pd_base = smem_u32(smem + L::PD);
       bool ok = true;
-      for (int u = 0; u < n_units && ok; ++u) {
-        const int s = u % kQStages, pb = u & 1;
-        if (!(ok = mbar_wait(&bars->p_full[pb], (u >> 1) & 1, abort_flag))) break;
+      const int n_act = count_units();
+      for (int a = 0; a < n_act && ok; ++a) {
+        const int s = a % kQStages, pb = a & 1;
+        if (!(ok = mbar_wait(&bars->p_full[pb], (a >> 1) & 1, abort_flag))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kQB / 16; ++kk) {
           // A = P^T / dS^T [128 keys x 64 queries], K-major; B = dO / Q tile,
           // MN-major (rows = queries, 64-wide head-dim blocks kQHalf apart)
           const uint64_t bo = sw128_desc(do_base + s * QTILE + kk * 16 * 128, kQHalf, 1024);
-          mma_f16_ss(tmem_dv, sw128_desc(pp_base + pb * kHalf + kk * 32, 16, 1024), bo, IDESC_ACC, u > 0 || kk > 0);
+          mma_f16_ss(tmem_dv, sw128_desc(pp_base + pb * kHalf + kk * 32, 16, 1024), bo, IDESC_ACC, a > 0 || kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < kQB / 16; ++kk) {
           const uint64_t bq = sw128_desc(q_base + s * QTILE + kk * 16 * 128, kQHalf, 1024);
-          mma_f16_ss(tmem_dk, sw128_desc(pd_base + pb * kHalf + kk * 32, 16, 1024), bq, IDESC_ACC, u > 0 || kk > 0);
+          mma_f16_ss(tmem_dk, sw128_desc(pd_base + pb * kHalf + kk * 32, 16, 1024), bq, IDESC_ACC, a > 0 || kk > 0);
         }
         mma_commit(&bars->p_empty[pb]);
         mma_commit(&bars->qd_empty[s]);
@@ -689,6 +784,13 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     const bool key_ok = j < g.k_len;
     const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const float zs = zscale<NORM>(p.scale);
+    constexpr bool drop = DROP;  // a separate instantiation: no cost without dropout
+    uint32_t seed_lo = 0u, seed_hi = 0u;
+    if (drop) {
+      const uint64_t sd = (uint64_t)*p.drop_seed;
+      seed_lo = (uint32_t)sd;
+      seed_hi = (uint32_t)(sd >> 32);
+    }
     bool ok = true;
     // The named barriers run on every iteration, even after a timeout, so that
     // no warp waits for one that has left the loop.
@@ -720,21 +822,24 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         sb_[2 * kQB + row] = sg * nc;
       }
     };
-    fetch(0);
+    // u: the unit of list position a; u1, u2: the next two active units
+    BitWalk walk(ubits_or_all, n_units);
+    int u = walk.next(), u1 = walk.next(), u2 = walk.next();
+    fetch(u);
     stage(0);
-    fetch(1);
-    for (int u = 0; u < n_units; ++u) {
+    fetch(u1);
+    for (int a = 0; u < n_units; ++a, u = u1, u1 = u2, u2 = walk.next()) {
       const int m = m_lo + u % n_m;
       const int qbase = m * kQB;
-      const int bf = u & 1;
+      const int bf = a & 1;
       named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      stage(bf ^ 1);  // unit u + 1
-      fetch(u + 2);
+      stage(bf ^ 1);  // unit u1
+      fetch(u2);
       const float* st0s = stats_smem + bf * 3 * kQB;
       const float* st1s = st0s + kQB;
       const float* crs = st1s + kQB;
       if (!ok) continue;
-      if (!(ok = wait_warp(&bars->sdp_full[bf], (u >> 1) & 1, abort_flag))) continue;
+      if (!(ok = wait_warp(&bars->sdp_full[bf], (a >> 1) & 1, abort_flag))) continue;
       tc_fence_after();
       // visible queries of this key: [c_lo, c_hi) relative to qbase
       const int jl = j - off;  // causal: query i sees key j iff i >= j - off
@@ -767,7 +872,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           uint64_t x = ffma2(f2_pack(__uint_as_float(rs[e]), __uint_as_float(rs[e + 1])), zs2, nst);
           if (!full)
             x = f2_pack(e >= lo && e < hi ? f2_lo(x) : kNegInf, e + 1 >= lo && e + 1 < hi ? f2_hi(x) : kNegInf);
-          const uint64_t g2 = fadd2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), nc2);
+          uint64_t g2, ks2 = 0;
+          if (drop) {  // keep / (1 - p_drop) of (query row, this key), as in the forward
+            const uint64_t r0 = ((uint64_t)b * p.hq + (kvh * groups + u / n_m)) * p.len_q + (qbase + col);
+            const uint32_t jg = (uint32_t)(j >> 2), js = (uint32_t)(j & 3);
+            const uint32_t w0 = (dropout_keep4(r0, jg, seed_lo, seed_hi, p.drop_thr24) >> js) & 1u;
+            const uint32_t w1 = (dropout_keep4(r0 + 1, jg, seed_lo, seed_hi, p.drop_thr24) >> js) & 1u;
+            ks2 = f2_pack(w0 ? p.drop_scale : 0.f, w1 ? p.drop_scale : 0.f);
+            g2 = ffma2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), ks2, nc2);
+          } else {
+            g2 = fadd2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), nc2);
+          }
           uint64_t pr, ds;
           if (NORM == HFAN_SOFTMAX1) {
             const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
@@ -781,14 +896,15 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             pr = fmul2(d, d);
             ds = fmul2(d, g2);
           }
+          if (drop) pr = fmul2(pr, ks2);  // dV takes the dropped probabilities
           ppk[e / 2] = pack2<BF16>(f2_lo(pr), f2_hi(pr));
           dpk[e / 2] = pack2<BF16>(f2_lo(ds), f2_hi(ds));
         }
       }
-      // P^T / dS^T tile pair u & 1 is free once unit u - 2's dV / dK completed
-      const int pb = u & 1;
-      if (u >= 2) {
-        if (!(ok = wait_warp(&bars->p_empty[pb], ((u >> 1) & 1) ^ 1, abort_flag))) continue;
+      // P^T / dS^T tile pair a & 1 is free once the dV / dK of list position a - 2 completed
+      const int pb = a & 1;
+      if (a >= 2) {
+        if (!(ok = wait_warp(&bars->p_empty[pb], ((a >> 1) & 1) ^ 1, abort_flag))) continue;
       }
       store_chunks_sw128<COLS / 8>(smem + L::PP + pb * kHalf, row, wg * (COLS / 8), ppk);
       store_chunks_sw128<COLS / 8>(smem + L::PD + pb * kHalf, row, wg * (COLS / 8), dpk);
@@ -796,7 +912,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       tc_fence_before();
       warp_arrive(&bars->p_full[pb]);
     }
-    if (ok && n_units > 0) {
+    if (ok && has_units) {
       ok = wait_warp(&bars->done, 0, abort_flag);
       tc_fence_after();
     }
@@ -819,11 +935,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       T* dst = which == 0 ? dvrow : dkrow;
       {
         uint32_t r[32];
-        if (n_units > 0) {
+        if (has_units) {
           tmem_ld32(src + lane_addr + cidx * 32, r);
           tmem_wait_ld();
         }
-        if (n_units == 0 || !ok) {
+        if (!has_units || !ok) {
 #pragma unroll
           for (int x = 0; x < 32; ++x) r[x] = 0u;
         }
@@ -881,10 +997,17 @@ cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t
   AttnParams pq = p, pk = p;  // query tiles re-read K and V; key tiles re-read Q and dO
   pq.tile_lpt = (int64_t)batch * tk * p.hkv * HD * 4 <= kLptMaxReread;
   pk.tile_lpt = (int64_t)batch * tq * p.hq * HD * 4 <= kLptMaxReread;
-  cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
+  if (p.drop_thr24 != 0u) {
+    cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM, true>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
+                             Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, pq);
+    if (e != cudaSuccess) return e;
+    return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM, true>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
+                    Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq64, mdo64, mk, mv, pk);
+  }
+  cudaError_t e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM, false>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
                            Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, pq);
   if (e != cudaSuccess) return e;
-  return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
+  return launch_k(tc_bwd_dkdv_kernel<HD, BF16, NORM, false>, dim3((max_k + kBN - 1) / kBN, p.hkv, p.batch),
                   Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq64, mdo64, mk, mv, pk);
 }
 

@@ -190,5 +190,29 @@ __device__ __forceinline__ uint3 tile_coords(int lpt) {
 // tiles, Q/dO for key tiles) fits in about a third of L2.
 constexpr int64_t kLptMaxReread = 40ll << 20;
 
+// Key-tile support bitmask (sparse normalizers): words per 64-row block.
+// 32 words track 1024 key tiles (131072 keys); longer rows run without it.
+constexpr int kMaskWordsMax = 32;
+
+// Walks the set bits of bits[0 ..] in increasing order (all of 0 .. n - 1
+// when bits is null); next() returns n once they are exhausted.
+struct BitWalk {
+  const uint32_t* bits;
+  int n, word, cur;
+  uint32_t rest;
+  __device__ __forceinline__ BitWalk(const uint32_t* b, int n_) : bits(b), n(n_), word(-1), cur(-1), rest(0u) {}
+  __device__ __forceinline__ int next() {
+    if (bits == nullptr) return cur = min(cur + 1, n);
+    while (rest == 0u) {
+      if (++word * 32 >= n) return n;
+      rest = bits[word];
+    }
+    const int u = word * 32 + __ffs(rest) - 1;
+    rest &= rest - 1u;
+    return u;
+  }
+};
+
+
 }  // namespace tc
 }  // namespace hfan

@@ -66,13 +66,35 @@ def _ptr(t: Optional[Tensor]) -> ctypes.c_void_p:
 # ---------------------------------------------------------------------------
 # dense
 # ---------------------------------------------------------------------------
-def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None) -> N.AttnDesc:
+def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, mask=None,
+                dropout_p=0.0, seed=None) -> N.AttnDesc:
     b, hq, lq, d = q.shape
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=k.shape[1],
         head_dim=d, len_q=lq, len_k=k.shape[2], total_q=b * lq, total_k=k.shape[0] * k.shape[2], cu_seqlens_q=None,
         cu_seqlens_k=None, scale=float(scale), causal=int(bool(causal)),
-        window_left=int(window_left), grad_dtype=dtype_id(q) if grad_dtype is None else grad_dtype)
+        window_left=int(window_left), grad_dtype=dtype_id(q) if grad_dtype is None else grad_dtype,
+        tile_mask=_mask_ptr(mask), dropout_p=float(dropout_p),
+        dropout_seed=None if (seed is None or dropout_p == 0.0) else seed.data_ptr())
+
+
+def mask_words(normalizer: int, heads_q: int, batch: int, len_q: int, len_k: int) -> int:
+    """int32 words of the key-tile support mask (hfan_attn_tile_mask_words):
+    sparse normalizers, rows of at most 131072 keys; 0 otherwise."""
+    if normalizer == N.SOFTMAX1 or len_q <= 0 or len_k <= 0:
+        return 0
+    tiles = -(-len_k // 128)
+    if tiles > 1024:
+        return 0
+    return heads_q * batch * 2 * (-(-len_q // 128)) * ((tiles + 31) // 32)
+
+
+def _new_mask(device, normalizer, heads_q, batch, len_q, len_k) -> Tensor:
+    return torch.empty((mask_words(normalizer, heads_q, batch, len_q, len_k),), dtype=torch.int32, device=device)
+
+
+def _mask_ptr(mask: Optional[Tensor]):
+    return None if mask is None or mask.numel() == 0 else mask.data_ptr()
 
 
 def _new_out(q: Tensor, out_bshd: bool) -> Tensor:
@@ -88,29 +110,37 @@ def _as_bhsd(o: Tensor, out_bshd: bool) -> Tensor:
 
 @torch.library.custom_op("hfan::attn_fwd", mutates_args=())
 def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, causal: bool,
-             window_left: int, out_bshd: bool) -> tuple[Tensor, Tensor]:
+             window_left: int, out_bshd: bool, dropout_p: float = 0.0,
+             seed: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+    """Returns (o, stats, mask): stats float32 [2, Hq, B*S] (see hfan.h) and the
+    int32 key-tile support mask of the sparse normalizers (empty for softmax1),
+    which the backward uses to skip all-zero tiles.  ``dropout_p > 0`` drops
+    probabilities with the keep bits generated from the device int64 ``seed``."""
     _require_cuda(q, k, v)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
     o = _new_out(q, out_bshd)
     b, hq, lq, _ = q.shape
     stats = torch.empty((2, hq, b * lq), dtype=torch.float32, device=q.device)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    mask = _new_mask(q.device, normalizer, hq, b, lq, k.shape[2])
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(_as_bhsd(o, out_bshd)),
                                       _ptr(stats), _stream(q)), "hfan_attn_fwd")
-    return o, stats
+    return o, stats, mask
 
 
 @attn_fwd.register_fake
-def _(q, k, v, normalizer, scale, causal, window_left, out_bshd):
+def _(q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p=0.0, seed=None):
     b, hq, lq, d = q.shape
     o = _new_out(q, out_bshd)
-    return o, q.new_empty((2, hq, b * lq), dtype=torch.float32)
+    return (o, q.new_empty((2, hq, b * lq), dtype=torch.float32),
+            q.new_empty((mask_words(normalizer, hq, b, lq, k.shape[2]),), dtype=torch.int32))
 
 
 @torch.library.custom_op("hfan::attn_bwd", mutates_args=())
-def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, normalizer: int,
-             scale: float, causal: bool, window_left: int) -> tuple[Tensor, Tensor, Tensor]:
+def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, normalizer: int,
+             scale: float, causal: bool, window_left: int, dropout_p: float = 0.0,
+             seed: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
     do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
     dq = torch.empty_like(q, memory_format=torch.contiguous_format)
@@ -118,7 +148,7 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
     dv = torch.empty_like(v, memory_format=torch.contiguous_format)
     b, hq, lq, _ = q.shape
     corr = torch.empty((hq, b * lq), dtype=torch.float32, device=q.device)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
@@ -127,38 +157,39 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
 
 
 @attn_bwd.register_fake
-def _(do, q, k, v, o, stats, normalizer, scale, causal, window_left):
+def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropout_p=0.0, seed=None):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
 
 
 def _attn_setup(ctx, inputs, output):
-    q, k, v, normalizer, scale, causal, window_left, out_bshd = inputs
-    o, stats = output
-    ctx.save_for_backward(q, k, v, o, stats)
-    ctx.args = (normalizer, scale, causal, window_left, out_bshd)
-    ctx.mark_non_differentiable(stats)
+    q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p, seed = inputs
+    o, stats, mask = output
+    ctx.save_for_backward(q, k, v, o, stats, mask, seed)
+    ctx.args = (normalizer, scale, causal, window_left, out_bshd, dropout_p)
+    ctx.mark_non_differentiable(stats, mask)
 
 
-def _attn_backward(ctx, do, dstats):
-    q, k, v, o, stats = ctx.saved_tensors
-    normalizer, scale, causal, window_left, out_bshd = ctx.args
-    dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, normalizer,
-                          scale, causal, window_left)
-    return dq, dk, dv, None, None, None, None, None
+def _attn_backward(ctx, do, dstats, dmask):
+    q, k, v, o, stats, mask, seed = ctx.saved_tensors
+    normalizer, scale, causal, window_left, out_bshd, dropout_p = ctx.args
+    dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, mask, normalizer,
+                          scale, causal, window_left, dropout_p, seed)
+    return dq, dk, dv, None, None, None, None, None, None, None
 
 
 torch.library.register_autograd("hfan::attn_fwd", _attn_backward, setup_context=_attn_setup)
 
 
 def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, normalizer: int, scale: float,
-                  causal: bool, window_left: int = -1) -> None:
+                  causal: bool, window_left: int = -1, mask: Optional[Tensor] = None) -> None:
     """Forward into caller-owned outputs: ``o`` any [B, Hq, S, D] view with unit
     D stride (for example one rank's slice of a head-major gather buffer), ``stats``
-    float32 [2, Hq, B * S].  No autograd; no allocation."""
+    float32 [2, Hq, B * S], optionally the int32 tile mask (``mask_words`` long).
+    No autograd; no allocation."""
     _require_cuda(q, k, v, o, stats)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _ptr(stats),
                                       _stream(q)), "hfan_attn_fwd")
@@ -166,11 +197,12 @@ def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, nor
 
 def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, corr: Tensor,
                   dq: Tensor, dk: Tensor, dv: Tensor, normalizer: int, scale: float, causal: bool,
-                  window_left: int = -1) -> None:
+                  window_left: int = -1, mask: Optional[Tensor] = None) -> None:
     """Backward into caller-owned gradient views (unit D stride) and a float32
-    [Hq, B * S] row-correction buffer.  No autograd; no allocation."""
+    [Hq, B * S] row-correction buffer (``mask``: the forward's tile mask, or
+    None).  No autograd; no allocation."""
     _require_cuda(do, q, k, v, o, dq, dk, dv)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
@@ -180,38 +212,42 @@ def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats:
 # ---------------------------------------------------------------------------
 # varlen
 # ---------------------------------------------------------------------------
-def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal) -> N.AttnDesc:
+def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=None) -> N.AttnDesc:
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=cu_q.numel() - 1, heads_q=q.shape[1],
         heads_kv=k.shape[1], head_dim=q.shape[2], len_q=int(max_q), len_k=int(max_k),
         total_q=q.shape[0], total_k=k.shape[0], cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=cu_k.data_ptr(),
-        scale=float(scale), causal=int(bool(causal)), window_left=0, grad_dtype=dtype_id(q))
+        scale=float(scale), causal=int(bool(causal)), window_left=0, grad_dtype=dtype_id(q),
+        tile_mask=_mask_ptr(mask))
 
 
 @torch.library.custom_op("hfan::varlen_fwd", mutates_args=())
 def varlen_fwd(q: Tensor, k: Tensor, v: Tensor, cu_q: Tensor, cu_k: Tensor, max_q: int, max_k: int,
-               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor]:
+               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(q, k, v, cu_q, cu_k)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
     cu_q = cu_q.to(torch.int32).contiguous()
     cu_k = cu_k.to(torch.int32).contiguous()
     o = torch.empty_like(q, memory_format=torch.contiguous_format)
     stats = torch.empty((2, q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
-    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    mask = _new_mask(q.device, normalizer, q.shape[1], cu_q.numel() - 1, int(max_q), int(max_k))
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _ptr(stats),
                                       _stream(q)), "hfan_attn_fwd(varlen)")
-    return o, stats
+    return o, stats, mask
 
 
 @varlen_fwd.register_fake
 def _(q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
-            q.new_empty((2, q.shape[1], q.shape[0]), dtype=torch.float32))
+            q.new_empty((2, q.shape[1], q.shape[0]), dtype=torch.float32),
+            q.new_empty((mask_words(normalizer, q.shape[1], cu_q.shape[0] - 1, int(max_q), int(max_k)),),
+                        dtype=torch.int32))
 
 
 @torch.library.custom_op("hfan::varlen_bwd", mutates_args=())
-def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, cu_q: Tensor,
+def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, cu_q: Tensor,
                cu_k: Tensor, max_q: int, max_k: int, normalizer: int, scale: float,
                causal: bool) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
@@ -222,7 +258,7 @@ def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Te
     dk = torch.zeros_like(k, memory_format=torch.contiguous_format)
     dv = torch.zeros_like(v, memory_format=torch.contiguous_format)
     corr = torch.empty((q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
-    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _t3(do),
                                       _ptr(stats), _ptr(corr), _t3(dq), _t3(dk), _t3(dv), _stream(q)),
@@ -231,7 +267,7 @@ def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Te
 
 
 @varlen_bwd.register_fake
-def _(do, q, k, v, o, stats, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
+def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
@@ -239,16 +275,16 @@ def _(do, q, k, v, o, stats, cu_q, cu_k, max_q, max_k, normalizer, scale, causal
 
 def _varlen_setup(ctx, inputs, output):
     q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal = inputs
-    o, stats = output
-    ctx.save_for_backward(q, k, v, o, stats, cu_q, cu_k)
+    o, stats, mask = output
+    ctx.save_for_backward(q, k, v, o, stats, mask, cu_q, cu_k)
     ctx.args = (max_q, max_k, normalizer, scale, causal)
-    ctx.mark_non_differentiable(stats)
+    ctx.mark_non_differentiable(stats, mask)
 
 
-def _varlen_backward(ctx, do, dstats):
-    q, k, v, o, stats, cu_q, cu_k = ctx.saved_tensors
+def _varlen_backward(ctx, do, dstats, dmask):
+    q, k, v, o, stats, mask, cu_q, cu_k = ctx.saved_tensors
     max_q, max_k, normalizer, scale, causal = ctx.args
-    dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
     return dq, dk, dv, None, None, None, None, None, None, None
 
 
@@ -413,3 +449,27 @@ def row_normalize(x: Tensor, normalizer: str, dim: int = -1) -> Tensor:
     if dim != -1 and dim != x.dim() - 1:
         return rownorm_fwd(x.movedim(dim, -1).contiguous(), nid).movedim(-1, dim)
     return rownorm_fwd(x, nid)
+
+
+def tile_mask_skipped_fraction(mask: Tensor, heads_q: int, batch: int, len_q: int, len_k: int,
+                               causal: bool = True) -> float:
+    """Fraction of the (64-row block, 128-key tile) pairs that the causal mask
+    leaves visible whose support bit is clear, i.e. the share of tile work the
+    backward skips (dense layout, len_q rows bottom-right aligned to len_k keys)."""
+    if mask.numel() == 0:
+        return 0.0
+    qb = 2 * (-(-len_q // 128))
+    kt = -(-len_k // 128)
+    w = (kt + 31) // 32
+    words = mask.view(heads_q, batch, qb, w).to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(32, device=mask.device, dtype=torch.int64)
+    bits = ((words.unsqueeze(-1) >> shifts) & 1).reshape(heads_q, batch, qb, w * 32)[..., :kt].bool()
+    rb = torch.arange(qb, device=mask.device)
+    last_row = torch.clamp(rb * 64 + 63, max=len_q - 1) + (len_k - len_q)
+    first_key = torch.arange(kt, device=mask.device) * 128
+    vis = (rb * 64 < len_q)[:, None] & (first_key[None, :] < len_k)
+    if causal:
+        vis = vis & (first_key[None, :] <= last_row[:, None])
+    vis = vis.expand(heads_q, batch, qb, kt)
+    total = int(vis.sum())
+    return 0.0 if total == 0 else float((vis & ~bits).sum()) / total

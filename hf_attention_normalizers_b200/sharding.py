@@ -48,6 +48,19 @@ def gather_heads(x: torch.Tensor, head_dim_index: int = 1, group=None) -> torch.
     return out.movedim(0, head_dim_index)
 
 
+def gather_stacked(x: torch.Tensor, group=None, async_op: bool = False):
+    """All-gather a contiguous per-rank block ``x`` into a new [world, *x.shape]
+    tensor (rank r's block at index r) without repacking it.  Returns
+    (gathered, work); work is None unless async_op."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    x = x.contiguous()
+    out = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+    work = dist.all_gather_into_tensor(out, x, group=group, async_op=async_op)
+    return out, work
+
+
 def gather_heads_into(full: torch.Tensor, group=None, async_op: bool = False):
     """In-place all-gather of a head-major buffer ``full`` [world, ...] whose
     slice ``full[rank]`` this rank has already written (for example through a
@@ -112,21 +125,28 @@ def shard_paged_batch(key_cache, value_cache, block_table, seq_lens, page_size: 
                       local.to(block_table.device), lens.to(torch.int32).to(seq_lens.device))
 
 
-def gather_batch(x: torch.Tensor, parts: list[list[int]], group=None) -> torch.Tensor:
+def batch_gather_order(parts: list[list[int]]):
+    """(slots per rank, index of every global row in the padded gather buffer)."""
+    nmax = max(len(p) for p in parts)
+    pos = [r * nmax + j for r in range(len(parts)) for j in range(len(parts[r]))]
+    glob = [i for p in parts for i in p]
+    order = torch.empty(len(glob), dtype=torch.int64)
+    order[torch.tensor(glob, dtype=torch.int64)] = torch.tensor(pos, dtype=torch.int64)
+    return nmax, order
+
+
+def gather_batch(x: torch.Tensor, parts: list[list[int]], group=None, order=None) -> torch.Tensor:
     """All-gather per-rank batch slices (``x`` holds this rank's rows, in the
     order of ``parts[rank]``) back into global batch order.  Slices are padded
-    to the largest part so that one all_gather_into_tensor moves them."""
+    to the largest part so that one all_gather_into_tensor moves them.
+    ``order`` may hold a precomputed ``batch_gather_order(parts)``."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    nmax = max(len(p) for p in parts)
+    nmax, idx = order if order is not None else batch_gather_order(parts)
     send = x.new_zeros((nmax,) + tuple(x.shape[1:]))
     send[: len(parts[rank])] = x
     buf = x.new_empty((world * nmax,) + tuple(x.shape[1:]))
     dist.all_gather_into_tensor(buf, send, group=group)
-    pos = [r * nmax + j for r in range(world) for j in range(len(parts[r]))]
-    glob = [i for r in range(world) for i in parts[r]]
-    order = torch.empty(len(glob), dtype=torch.int64)
-    order[torch.tensor(glob)] = torch.tensor(pos)
-    return buf.index_select(0, order.to(buf.device))
+    return buf.index_select(0, idx.to(buf.device))

@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define HFAN_ABI_VERSION 1
+#define HFAN_ABI_VERSION 2
 
 typedef enum hfan_status {
   HFAN_OK = 0,
@@ -92,6 +92,13 @@ typedef struct hfan_attn_desc {
   int32_t causal;
   int32_t window_left;  /* <= 0: no window                                            */
   int32_t grad_dtype;   /* hfan_dtype of dq/dk/dv written by hfan_attn_bwd            */
+  uint32_t* tile_mask;  /* sparsemax/entmax15: support bitmask of key tiles, or NULL   */
+                        /* (see hfan_attn_tile_mask_words)                             */
+  float dropout_p;      /* [0, 1): attention dropout; 0 = none.  Dense 16-bit inputs   */
+                        /* with head_dim 64/128 only (else HFAN_ERR_UNSUPPORTED).      */
+  const int64_t* dropout_seed; /* device int64 seed (required when dropout_p > 0);     */
+                        /* forward and backward must get the same value.  Replaces the */
+                        /* saved seed of kernels/softmax1_hopper.py:434-441.           */
 } hfan_attn_desc;
 
 /* Row statistics saved by the forward for the backward: float32 [2, heads_q, rows]
@@ -104,6 +111,19 @@ typedef struct hfan_attn_desc {
 
 int hfan_attn_fwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan_tensor v,
                   hfan_tensor o, float* stats, void* stream);
+
+/* Key-tile support mask of the sparse normalizers (no counterpart in the
+ * reference; its kernels sweep every key tile, kernels/sparse_entmax_hopper.py:126-151
+ * and :271-319).  When desc->tile_mask is set, hfan_attn_fwd writes one bit per
+ * (query head, sequence, 64-row query block, 128-key tile): set when any
+ * probability of those rows on those keys is nonzero.  hfan_attn_bwd given the
+ * same buffer skips the tiles whose bit is clear (all-zero probabilities
+ * contribute nothing to any gradient).  Layout: uint32 words
+ * [heads_q][batch][2 * ceil(len_q / 128)][W], W = ceil(ceil(len_k / 128) / 32),
+ * bit t % 32 of word t / 32 = key tile t.  Returns the number of words, or 0
+ * when the request takes no mask (softmax1, or rows longer than 131072 keys);
+ * then desc->tile_mask must be NULL. */
+int64_t hfan_attn_tile_mask_words(const hfan_attn_desc* desc);
 
 int hfan_attn_bwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan_tensor v,
                   hfan_tensor o, hfan_tensor d_o, const float* stats, float* corr,

@@ -29,3 +29,4 @@ from .attention import (  # noqa: F401
     paged_forward,
     paged_backward,
 )
+from . import philox  # noqa: F401

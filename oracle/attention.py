@@ -67,8 +67,13 @@ def attention_forward(q, k, v, normalizer, scale=None, causal=True, window_left=
 
 
 def attention_backward(q, k, v, do, normalizer, scale=None, causal=True, window_left=None,
-                       dtype=np.float64):
-    """Returns (o, dq, dk, dv) for upstream gradient ``do``."""
+                       dtype=np.float64, dropout=None):
+    """Returns (o, dq, dk, dv) for upstream gradient ``do``.
+
+    ``dropout = (keep, p)``: keep a bool [B, Hq, Lq, Lk] mask; the output uses
+    p_ij keep_ij / (1 - p) and the normalizer's backward receives
+    dP keep / (1 - p), as ``kernels/softmax1_hopper.py:105-110, 253-256`` and
+    ``kernels/sparse_entmax_hopper.py:141-145, 262-264`` compute them."""
     q = np.asarray(q, dtype=dtype)
     k0 = np.asarray(k, dtype=dtype)
     v0 = np.asarray(v, dtype=dtype)
@@ -81,13 +86,15 @@ def attention_backward(q, k, v, do, normalizer, scale=None, causal=True, window_
     valid = _mask(q.shape[2], k.shape[2], causal, window_left)
     s = _scores(q, k, scale, valid, dtype)
     p = normalize(normalizer, s)
-    o = np.matmul(p, v)
-    dp = np.matmul(do, np.swapaxes(v, -1, -2))
+    factor = 1.0 if dropout is None else np.asarray(dropout[0], dtype=dtype) / (1.0 - float(np.float32(dropout[1])))
+    pd = p * factor
+    o = np.matmul(pd, v)
+    dp = np.matmul(do, np.swapaxes(v, -1, -2)) * factor
     ds = normalize_backward(normalizer, s, p, dp)
     ds = np.where(valid, ds, 0)
     dq = np.matmul(ds, k) * scale
     dk = np.matmul(np.swapaxes(ds, -1, -2), q) * scale
-    dv = np.matmul(np.swapaxes(p, -1, -2), do)
+    dv = np.matmul(np.swapaxes(pd, -1, -2), do)
     if g != 1:
         b, h, l, d = dk.shape
         dk = dk.reshape(b, h // g, g, l, d).sum(axis=2)

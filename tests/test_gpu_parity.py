@@ -116,7 +116,7 @@ def test_sliding_window_matches_oracle(norm):
 def test_sparse_threshold_matches_oracle_fp32(norm):
     """The saved tau equals the oracle's sort-based tau (zero-pattern check)."""
     q, k, v, _ = _inputs((1, 2, 96, 64), (1, 2, 96, 64), torch.float32, seed=11)
-    o, stats = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], 64 ** -0.5, True, -1, False)
+    o, stats, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], 64 ** -0.5, True, -1, False)
     _, p, s = oracle.attention_forward(_np(q), _np(k), _np(v), norm, causal=True, return_probs=True)
     half = 1.0 if norm == "sparsemax" else 0.5
     with np.errstate(all="ignore"):
@@ -401,3 +401,46 @@ def test_hf_continuous_batching_paged_attention_interface(norm):
     ref = oracle.varlen_forward(_np(q[0].transpose(0, 1)), _np(k_all[0].transpose(0, 1)), _np(v_all[0].transpose(0, 1)),
                                 cu_q.numpy(), cu_k.numpy(), norm)
     assert_close(o, ref, torch.bfloat16, f"hf-paged/{norm}")
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_varlen_torch_compile_fullgraph_bf16(norm):
+    """tests/test_varlen_attention.py:121-143 of the reference."""
+    cu_q = torch.tensor([0, 3, 5], device="cuda", dtype=torch.int32)
+    cu_k = torch.tensor([0, 4, 9], device="cuda", dtype=torch.int32)
+
+    def attention(query, key, value):
+        return varlen.varlen_hopper_attention(query, key, value, cu_q, cu_k, norm, max_seqlen_q=3, max_seqlen_k=5)
+
+    compiled = torch.compile(attention, fullgraph=True)
+    q = torch.randn(5, 4, 32, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(9, 2, 32, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn_like(k, requires_grad=True)
+    out = compiled(q, k, v)
+    out.float().square().mean().backward()
+    assert torch.isfinite(out).all()
+    assert all(torch.isfinite(x.grad).all() for x in (q, k, v))
+    ref = oracle.varlen_forward(_np(q), _np(k), _np(v), cu_q.cpu().numpy(), cu_k.cpu().numpy(), norm)
+    assert_close(out, ref, torch.bfloat16, f"compiled varlen/{norm}")
+
+
+@pytest.mark.parametrize("norm", NORMS)
+def test_paged_torch_compile_fullgraph_bf16(norm):
+    """tests/test_paged_attention.py:88-113 of the reference (unique pages)."""
+    block_table = torch.tensor([[0, 1], [2, 3]], device="cuda")
+    lens = torch.tensor([8, 7], device="cuda")
+
+    def attention(query, key_cache, value_cache):
+        return H.paged_triton_attention(query, key_cache, value_cache, block_table, lens, block_size=4,
+                                        normalizer=norm, max_key_length=8, assume_unique_pages=True)
+
+    compiled = torch.compile(attention, fullgraph=True)
+    q = torch.randn(2, 4, 2, 32, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    kc = torch.randn(16, 2, 32, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    vc = torch.randn_like(kc, requires_grad=True)
+    out = compiled(q, kc, vc)
+    out.float().square().mean().backward()
+    assert torch.isfinite(out).all()
+    assert all(torch.isfinite(x.grad).all() for x in (q, kc, vc))
+    ref = oracle.paged_forward(_np(q), _np(kc), _np(vc), block_table.cpu().numpy(), lens.cpu().numpy(), 4, norm)
+    assert_close(out, ref, torch.bfloat16, f"compiled paged/{norm}")

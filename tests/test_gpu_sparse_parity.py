@@ -68,7 +68,7 @@ def check_threshold(norm, tau_k, support_k, q, k, scale, what, near=NEAR):
 
 
 def _stats(norm, q, k, v, scale):
-    _, st = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], scale, True, -1, False)
+    _, st, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], scale, True, -1, False)
     b, hq, lq, _ = q.shape  # stats [2][Hq][B * Lq]
     return st.reshape(2, hq, b, lq).transpose(1, 2).double().cpu().numpy()
 
@@ -186,3 +186,42 @@ def test_config3_varlen_seed0_lengths(norm):
     i = int(order[-1])
     _tail_check(norm, seq(q, i), seq(k, i), seq(v, i), seq(do, i), tuple(seq(t, i) for t in out), 256,
                 torch.bfloat16, f"config3/{norm}/seq {i}")
+
+
+@pytest.mark.parametrize("norm", SPARSE)
+def test_zero_tiles_skipped_and_results_unchanged(norm):
+    """Local attention (each key close to its own query, far from the others):
+    the support of every row sits near the diagonal, so most key tiles carry
+    no probability at all.  The forward's tile mask must show them, the
+    backward that skips them must give what the backward without the mask
+    gives (dQ bit for bit: a skipped tile adds exact zeros; dK, dV to fp32
+    rounding, their kernel recomputes the scores in another MMA shape), and
+    the tail rows must match the oracle."""
+    b, h, s, d = 1, 2, 2048, 128
+    gen = torch.Generator().manual_seed(7)
+    base = torch.randn(b, h, s, d, generator=gen)
+    # nearby positions get similar vectors (a slowly rotating direction)
+    pos = torch.arange(s, dtype=torch.float32)[:, None]
+    freq = torch.rand(d, generator=gen) * 0.05
+    smooth = torch.cos(pos * freq) * 2.0
+    q = (smooth + 0.3 * base).to(torch.bfloat16).cuda()
+    k = (smooth + 0.3 * torch.randn(b, h, s, d, generator=gen)).to(torch.bfloat16).cuda()
+    v = torch.randn(b, h, s, d, generator=gen).to(torch.bfloat16).cuda()
+    do = torch.randn(b, h, s, d, generator=gen).to(torch.bfloat16).cuda()
+    nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
+    o, st, mk = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    frac = ops.tile_mask_skipped_fraction(mk, h, b, s, s)
+    print(f"{norm}: skipped tile fraction {frac:.3f}")
+    assert frac > 0.5
+    corr = torch.empty((h, b * s), dtype=torch.float32, device="cuda")
+    with_mask = [torch.empty_like(x) for x in (q, k, v)]
+    without = [torch.empty_like(x) for x in (q, k, v)]
+    ops.attn_bwd_into(do, q, k, v, o, st, corr, *with_mask, nid, scale, True, mask=mk)
+    ops.attn_bwd_into(do, q, k, v, o, st, corr, *without, nid, scale, True, mask=None)
+    torch.cuda.synchronize()
+    assert torch.equal(with_mask[0], without[0])
+    for a, e in zip(with_mask[1:], without[1:]):
+        err = float((a.float() - e.float()).abs().max())
+        assert err <= 1e-2 * float(e.float().abs().max()) + 1e-6
+    out = (o, *with_mask)
+    _tail_check(norm, q, k, v, do, out, 256, torch.bfloat16, f"local/{norm}")

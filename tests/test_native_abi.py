@@ -14,7 +14,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def _declared_symbols():
     text = open(os.path.join(ROOT, "include", "hfan.h")).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(hfan_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int64_t|int|const char\*)\s+(hfan_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -65,3 +65,22 @@ def test_rownorm_rejects_bad_shapes():
     lib = N.lib()
     rc = lib.hfan_rownorm_fwd(N.SPARSEMAX, N.FLOAT32, 4, 10, None, 5, None, 10, None)
     assert rc == 1
+
+
+@pytest.mark.parametrize("norm,lq,lk,b,hq", [
+    (N.SPARSEMAX, 8192, 8192, 4, 32), (N.ENTMAX15, 77, 190, 1, 4), (N.ENTMAX15, 1, 513, 2, 8),
+    (N.SOFTMAX1, 512, 512, 1, 4), (N.SPARSEMAX, 16, 131072, 1, 1), (N.SPARSEMAX, 16, 131073, 1, 1),
+])
+def test_tile_mask_size_agrees_with_python(norm, lq, lk, b, hq):
+    from hf_attention_normalizers_b200 import ops
+
+    d = _desc(normalizer=norm, batch=b, heads_q=hq, heads_kv=1, len_q=lq, len_k=lk, total_q=b * lq)
+    assert N.lib().hfan_attn_tile_mask_words(ctypes.byref(d)) == ops.mask_words(norm, hq, b, lq, lk)
+
+
+def test_tile_mask_rejected_where_none_is_taken():
+    lib = N.lib()
+    t = N.HfanTensor(None, 0, 0, 0)
+    rc = lib.hfan_attn_fwd(ctypes.byref(_desc(normalizer=N.SOFTMAX1, tile_mask=1)), t, t, t, t,
+                           ctypes.c_void_p(1), None)
+    assert rc == 1 and "tile_mask" in lib.hfan_last_error().decode()

@@ -75,3 +75,32 @@ def test_config1_fp32_matches_reference(golden, name):
         ref = g[f"config1_{name}_{label}_rows"]
         np.testing.assert_allclose(a[:, :, ::61, :], ref, rtol=0, atol=2e-5)
         assert abs(a.astype(np.float64).sum() - float(g[f"config1_{name}_{label}_sum"])) < 1e-2
+
+
+def test_philox_known_answers():
+    """Philox4x32-10 known-answer vectors (Random123's kat_vectors, as
+    published with the generator): counter/key all zeros and all ones."""
+    from oracle import philox
+
+    assert [int(x) for x in philox.philox4x32_10(0, 0, 0, 0, 0, 0)] == [
+        0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    ones = 0xFFFFFFFF
+    assert [int(x) for x in philox.philox4x32_10(ones, ones, ones, ones, ones, ones)] == [
+        0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]
+
+
+def test_dropout_keep_rate_and_oracle_identity():
+    import numpy as np
+
+    from oracle import philox
+    import oracle
+
+    keep = philox.keep_mask(7, 0.25, 2, 3, 64, 96)
+    assert abs(keep.mean() - 0.75) < 0.02
+    assert not np.array_equal(keep, philox.keep_mask(8, 0.25, 2, 3, 64, 96))
+    rng = np.random.default_rng(0)
+    q, k, v, do = (rng.standard_normal((1, 2, 16, 8)) for _ in range(4))
+    base = oracle.attention_backward(q, k, v, do, "entmax15")
+    all_kept = oracle.attention_backward(q, k, v, do, "entmax15", dropout=(np.ones((1, 2, 16, 16), bool), 0.0))
+    for a, b in zip(base, all_kept):
+        assert np.allclose(a, b, rtol=0, atol=1e-12)
