@@ -726,7 +726,31 @@ def cpu_baseline(budget_s: float = 20.0):
         sec, flops = cpu_sample(threads, rows)
     return {"value": round(flops / sec / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"last {rows} query rows x 4 heads of one (batch, KV group) slice, all {S} keys, "
-                      f"fwd+bwd sparsemax+entmax15, float32 numpy oracle; {sec:.1f} s"}
+                      f"fwd+bwd sparsemax+entmax15, float32 numpy oracle; {sec:.1f} s",
+            "config1": cpu_config1(threads)}
+
+
+def cpu_config1(threads: int):
+    """BASELINE configs[0] as a whole problem on the host cores: fp32 q,k,v
+    [2, 8, 512, 128], causal, fwd + bwd of every normalizer through the numpy
+    oracle (median of 3)."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(0)
+    q, k, v, g = (rng.standard_normal((2, 8, 512, 128)).astype(np.float32) for _ in range(4))
+    flops = 3.5 * causal_flops(2, 8, 512, 128)
+    out = {"workload": "BASELINE configs[0] (B=2 H=8 S=512 D=128 fp32, causal, fwd+bwd)", "cores": threads}
+    for name in ("softmax1", "sparsemax", "entmax15"):
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            oracle.attention_backward(q, k, v, g, name, scale=128 ** -0.5, causal=True, dtype=np.float32)
+            times.append(time.perf_counter() - t0)
+        sec = statistics.median(times)
+        out[name] = {"ms": round(sec * 1e3, 1), "GFLOP/s": round(flops / sec / 1e9, 2)}
+    return out
 
 
 def run_reference(args, rank):

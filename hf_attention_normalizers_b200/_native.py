@@ -51,6 +51,7 @@ class AttnDesc(ctypes.Structure):
         ("tile_mask", ctypes.c_void_p),
         ("dropout_p", ctypes.c_float),
         ("dropout_seed", ctypes.c_void_p),
+        ("key_lengths", ctypes.c_void_p),
     ]
 
 

@@ -15,6 +15,7 @@ semantics as the reference's eager fallback.
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 from typing import Callable, Optional, Union
 
@@ -57,7 +58,7 @@ def _fused_name(softmax_fn) -> Optional[str]:
 
 
 def _fused_bshd(query, key, value, normalizer, scale, is_causal, window_left=None,
-                dropout_p: float = 0.0) -> torch.Tensor:
+                dropout_p: float = 0.0, key_lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Fused attention: q [B,Hq,S,D], k/v [B,Hkv,L,D] -> [B,S,Hq,D] contiguous."""
     from . import ops
     from .kernels._fused import dropout_seed
@@ -67,8 +68,77 @@ def _fused_bshd(query, key, value, normalizer, scale, is_causal, window_left=Non
     actual_scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
     window = -1 if window_left is None else int(window_left)
     o, _, _ = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
-                           window, True, float(dropout_p), dropout_seed(query, dropout_p))
+                           window, True, float(dropout_p), dropout_seed(query, dropout_p), key_lengths)
     return o
+
+
+_MASK_CACHE: dict = {"ref": None, "key": None, "value": None}
+
+
+def _mask_pattern(mask: Optional[torch.Tensor], lq: int, lk: int, source=None):
+    """Recognise the masks the fused kernels express without materialising
+    anything (every layer of a model gets the same mask, so the answer is
+    cached for the last mask seen):
+
+      ("causal", None)         j <= i for every row
+      ("padded", lengths)      j <= i and j < lengths[b]: HF's causal mask of a
+                               right-padded batch (int32 lengths [B])
+      ("window", w)            i - w < j <= i (sliding window of w keys)
+
+    ``mask`` is HF's [B, 1, Lq, Lk] boolean (True = attend) or additive float
+    (0 = attend) mask with Lq == Lk.  Anything else returns None: the caller
+    then takes the materialised path.  The check itself is one O(B Lq Lk)
+    boolean comparison on the device (the reference introspects the mask
+    closures instead, backends.py:208-326).  ``source`` is the object the
+    caller got (a BlockMask the boolean mask was evaluated from); the cache
+    holds a weak reference to it, never an address."""
+    if mask is None or lq != lk or torch.compiler.is_compiling():
+        return None
+    owner = mask if source is None else source
+    key = (getattr(owner, "_version", 0), lq, lk)
+    ref = _MASK_CACHE["ref"]
+    if ref is not None and ref() is owner and _MASK_CACHE["key"] == key:
+        return _MASK_CACHE["value"]
+    if callable(mask) and not isinstance(mask, torch.Tensor):
+        mask = mask()  # evaluated only on a cache miss
+    if (not isinstance(mask, torch.Tensor) or mask.ndim != 4 or mask.shape[1] != 1 or mask.shape[-2] != lq
+            or mask.shape[-1] < lk):
+        return None
+    m = mask[:, 0, :, :lk]
+    allowed = m if m.dtype == torch.bool else (m == 0)
+    i = torch.arange(lq, device=m.device)[:, None]
+    j = torch.arange(lk, device=m.device)[None, :]
+    causal = j <= i
+    lengths = allowed[:, -1, :].sum(-1)
+    result = None
+    if torch.equal(allowed, (causal[None] & (j[None] < lengths[:, None, None]))):
+        full = bool((lengths == lk).all())
+        result = ("causal", None) if full else ("padded", lengths.to(torch.int32))
+    else:
+        w = int(lengths[0])
+        if 0 < w < lk and torch.equal(allowed, (causal & (j > i - w))[None].expand_as(allowed)):
+            result = ("window", w)
+    try:
+        _MASK_CACHE["ref"] = weakref.ref(owner)
+        _MASK_CACHE["key"], _MASK_CACHE["value"] = key, result
+    except TypeError:  # not weak-referenceable: no caching
+        _MASK_CACHE["ref"] = None
+    return result
+
+
+def _fused_masked(query, key, value, normalizer, scaling, mask, dropout_p, sliding_window=None, source=None):
+    """Fused attention for a recognised mask (see _mask_pattern), else None."""
+    pat = _mask_pattern(mask, query.shape[-2], key.shape[-2], source)
+    if pat is None or not query.is_cuda or not _fused_dropout_ok(query, dropout_p):
+        return None
+    kind, arg = pat
+    if kind == "causal":
+        return _fused_bshd(query, key, value, normalizer, scaling, True, sliding_window, dropout_p)
+    if kind == "window" and sliding_window is None:
+        return _fused_bshd(query, key, value, normalizer, scaling, True, arg, dropout_p)
+    if kind == "padded" and sliding_window is None:
+        return _fused_bshd(query, key, value, normalizer, scaling, True, None, dropout_p, key_lengths=arg)
+    return None
 
 
 def _fused_dropout_ok(query: torch.Tensor, dropout_p: float) -> bool:
@@ -140,6 +210,10 @@ def sdpa_attention_forward(module: nn.Module, query: torch.Tensor, key: torch.Te
     training = getattr(module, "training", False)
     square = query.shape[2] == key.shape[2]
     drop = dropout if training else 0.0
+    if name is not None and attention_mask is not None:
+        out = _fused_masked(query, key, value, name, scaling, attention_mask, drop, kwargs.get("sliding_window"))
+        if out is not None:
+            return out, None
     if (name is not None and attention_mask is None and _fused_dropout_ok(query, drop) and query.is_cuda
             and (not is_causal or square)):
         # (the fused causal mask is bottom-right aligned; it equals this path's
@@ -189,6 +263,10 @@ def _fused_adapter(normalizer: str, label: str):
             kwargs.pop(unused, None)
         drop = dropout if getattr(module, "training", False) else 0.0
         check_dropout(drop)
+        if attention_mask is not None:
+            out = _fused_masked(query, key, value, normalizer, scaling, attention_mask, drop, sliding_window)
+            if out is not None:
+                return out, None
         if attention_mask is not None or not query.is_cuda or not _fused_dropout_ok(query, drop):
             # (dropout on 32-bit inputs or other head sizes: materialised path)
             return sdpa_attention_forward(module, query, key, value, attention_mask, softmax_fn=fn,
@@ -253,14 +331,30 @@ def flex_attention_normalizer_forward(module: nn.Module, query: torch.Tensor, ke
                                       value: torch.Tensor, attention_mask, softmax_fn: Callable[..., torch.Tensor],
                                       dropout: float = 0.0, scaling: Optional[float] = None,
                                       **kwargs) -> tuple[torch.Tensor, None]:
-    """``*_flex_attention``: a BlockMask is expanded to a dense mask (exact,
-    materialised); without a mask the fused kernel runs."""
+    """``*_flex_attention`` (reference backends.py:475-568): a causal,
+    sliding-window or right-padded BlockMask runs the fused kernel (the
+    boolean mask is evaluated once per distinct mask to recognise it); other
+    BlockMasks are expanded to a dense mask and materialised; without a mask
+    the fused kernel runs."""
     try:
         from torch.nn.attention.flex_attention import BlockMask
     except ImportError:  # pragma: no cover
         BlockMask = ()  # type: ignore[assignment]
     kwargs.pop("softmax_n_param", None)
     if isinstance(attention_mask, BlockMask):
+        name = _fused_name(softmax_fn)
+        training = getattr(module, "training", False)
+        if name is not None:
+            block_mask = attention_mask
+
+            def one_head():
+                return _dense_mask_from_flex_block_mask(block_mask, query.shape[-2], key.shape[-2],
+                                                        query.shape[0], 1)
+
+            out = _fused_masked(query, key, value, name, scaling, one_head, dropout if training else 0.0,
+                                kwargs.get("sliding_window"), source=attention_mask)
+            if out is not None:
+                return out, None
         attention_mask = _dense_mask_from_flex_block_mask(attention_mask, query.shape[-2], key.shape[-2],
                                                           query.shape[0], query.shape[1])
         kwargs.pop("is_causal", None)

@@ -151,6 +151,13 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   p.norm = desc->normalizer;
   p.grad_f32 = desc->grad_dtype == HFAN_FLOAT32;
   if (desc->cu_seqlens_q && desc->total_q < 0) return fail(HFAN_ERR_INVALID, "total_q must be >= 0");
+  if (desc->key_lengths != nullptr) {
+    if (desc->cu_seqlens_q != nullptr)
+      return fail(HFAN_ERR_INVALID, "key_lengths applies to the dense layout only");
+    p.lens_only = 1;
+    p.seq_lens = desc->key_lengths;
+    p.causal_top_left = 1;
+  }
   if (!(desc->dropout_p >= 0.f && desc->dropout_p < 1.f)) return fail(HFAN_ERR_INVALID, "dropout_p must be in [0, 1).");
   if (desc->dropout_p > 0.f) {
     if (desc->dropout_seed == nullptr) return fail(HFAN_ERR_INVALID, "dropout_seed is required when dropout_p > 0");

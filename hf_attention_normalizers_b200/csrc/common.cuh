@@ -146,12 +146,14 @@ __device__ __forceinline__ float sparse_g(int norm, float z, float tau) {
 struct Geometry {
   int q_start, q_len;   // first packed row / number of query rows of this sequence
   int k_start, k_len;   // first packed key / number of keys
+  int shift;            // causal alignment: row i sees keys j <= i + shift (k_len - q_len,
+                        // bottom-right; 0 with causal_top_left)
 };
 
 __device__ __forceinline__ bool key_visible(int i, int j, const Geometry& g, int causal,
                                             int window_left) {
   if (j >= g.k_len) return false;
-  int limit = i + g.k_len - g.q_len;
+  int limit = i + g.shift;
   if (causal && j > limit) return false;
   if (window_left > 0 && j <= limit - window_left) return false;
   return true;

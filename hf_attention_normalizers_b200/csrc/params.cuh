@@ -40,6 +40,7 @@ struct AttnParams {
   int paged;
   int lens_only;           // dense K/V whose per-sequence key lengths come from seq_lens
   int tile_lpt;            // tensor-core kernels: hand tiles out longest-first across the whole grid
+  int causal_top_left;     // causal mask aligned at the first key (row i sees j <= i) instead of the last
   // Sparse normalizers: key tiles with support, one bit per (query head,
   // sequence, 64-row block, 128-key tile), written by the tensor-core forward
   // and read by the backward to skip tiles whose probabilities are all zero.
@@ -84,6 +85,7 @@ __device__ __forceinline__ Geometry geometry(const AttnParams& p, int b) {
     g.k_start = 0;
     g.k_len = (p.paged || p.lens_only) ? seq_len_k(p, b) : p.len_k;
   }
+  g.shift = p.causal_top_left ? 0 : g.k_len - g.q_len;
   return g;
 }
 

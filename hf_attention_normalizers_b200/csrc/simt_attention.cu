@@ -78,9 +78,9 @@ __global__ void __launch_bounds__(kRows * 32) simt_fwd_kernel(AttnParams p) {
 
   const int last_row = min(q0 + kRows - 1, g.q_len - 1);
   int k_hi = g.k_len;
-  if (p.causal) k_hi = min(k_hi, last_row + g.k_len - g.q_len + 1);
+  if (p.causal) k_hi = min(k_hi, last_row + g.shift + 1);
   int k_lo = 0;
-  if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
+  if (p.window_left > 0) k_lo = max(0, q0 + g.shift - p.window_left + 1);
   k_lo = (k_lo / kTile) * kTile;
   const float zs = zscale_of<NORM>(p.scale);
 
@@ -237,9 +237,9 @@ __global__ void __launch_bounds__(kRows * 32) simt_bwd_dq_kernel(AttnParams p) {
 
   const int last_row = min(q0 + kRows - 1, g.q_len - 1);
   int k_hi = g.k_len;
-  if (p.causal) k_hi = min(k_hi, last_row + g.k_len - g.q_len + 1);
+  if (p.causal) k_hi = min(k_hi, last_row + g.shift + 1);
   int k_lo = 0;
-  if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
+  if (p.window_left > 0) k_lo = max(0, q0 + g.shift - p.window_left + 1);
   k_lo = (k_lo / kTile) * kTile;
   const float zs = zscale_of<NORM>(p.scale);
   const float inv_l = 1.f / st1;
@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(kRows * 32) simt_bwd_dkdv_kernel(AttnParams p)
     }
   }
   // Query rows that can see any key of this CTA.
-  const int off = g.k_len - g.q_len;  // key j visible to row i iff j <= i + off (causal)
+  const int off = g.shift;  // key j visible to row i iff j <= i + off (causal)
   int i_lo = 0;
   if (p.causal) i_lo = max(0, k0 - off);
   int i_hi = g.q_len;

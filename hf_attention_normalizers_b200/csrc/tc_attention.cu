@@ -1,14 +1,20 @@
 // Tensor-core fused attention forward for 16-bit inputs on sm_100a.
 //
 // One CTA computes 128 query rows of one (batch, query head) against all
-// visible keys of its KV head, in key tiles of 128:
+// visible keys of its KV head, in key tiles of 128.  Warp roles (HD = head
+// dim, NWG = HD / 32 row warpgroups: 4 at HD = 128, 2 at HD = 64):
 //
-//   warp 4      TMA producer: Q once, then K (and V) tiles into 2-stage rings
-//   warp 5      MMA issuer:   S = Q K^T into a double-buffered TMEM tile,
-//                             O += P V into a TMEM accumulator
-//   warps 0-3   normalizer:   thread i owns query row i (TMEM lane i); reads
-//                             S with tcgen05.ld, writes P (16-bit, 128-byte
-//                             swizzled, K-major) to shared memory, finalises O
+//   warps 0 .. 4 NWG - 1   row warps: warpgroup wg owns key columns
+//                          [128/NWG wg, 128/NWG (wg + 1)) of every S tile and
+//                          head-dim columns [32 wg, 32 wg + 32) of O; thread =
+//                          TMEM lane = query row.  They read S with tcgen05.ld,
+//                          write P as packed 16-bit pairs into TMEM (the A
+//                          operand of the P V MMA) and finalise O.
+//   warp 4 NWG             TMA producer: Q once, then K and V tiles through one
+//                          ring of 32 KB stages (5 at HD = 128, 8 at HD = 64)
+//                          in the order the MMA warps consume them.
+//   warp 4 NWG + 1         MMA issuer 1: S = Q K^T into a double-buffered TMEM tile.
+//   warp 4 NWG + 2         MMA issuer 2: O += P V (TMEM accumulator).
 //
 // softmax1 runs one pass with an online max / denominator seeded with the
 // implicit zero logit (m = 0, l = 1; reference kernels/softmax1_hopper.py:80-83);
@@ -22,7 +28,10 @@
 // the exact tau of vutils/entmax.py:35-133 without sorting.  Rows whose
 // candidates outgrow the buffer continue with exact bracket sweeps over the
 // whole row (common.cuh, tau_step).  The final pass then forms
-// p = (z - tau)_+^a and P V; the output needs no normalisation.
+// p = (z - tau)_+^a and P V; the output needs no normalisation.  It also
+// records, per 64-row half and key tile, whether any p > 0 (p.tile_mask):
+// the backward skips the tiles without support.  Optional dropout multiplies
+// the P fed to P V by keep / (1 - p_drop) (Philox keep bits, common.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -295,9 +304,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 
   const int last_row = min(q0 + kBM - 1, g.q_len - 1);
   int k_hi = g.k_len;
-  if (p.causal) k_hi = min(k_hi, last_row + g.k_len - g.q_len + 1);
+  if (p.causal) k_hi = min(k_hi, last_row + g.shift + 1);
   int k_lo = 0;
-  if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
+  if (p.window_left > 0) k_lo = max(0, q0 + g.shift - p.window_left + 1);
   k_lo = (k_lo / kBN) * kBN;
   const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kBN - 1) / kBN : 0;
   const int kt0 = k_lo / kBN;  // absolute index of the first key tile
@@ -462,7 +471,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     const int i = q0 + row;             // query row within the sequence
     const bool row_ok = i < g.q_len;
     const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
-    const int limit = i + g.k_len - g.q_len;
+    const int limit = i + g.shift;
     // visible keys of this row: [vis_lo, vis_hi)
     int vis_hi = row_ok ? g.k_len : 0;
     if (p.causal) vis_hi = min(vis_hi, limit + 1);

@@ -1,27 +1,34 @@
 // Tensor-core fused attention backward for 16-bit inputs on sm_100a.
 //
-// Two kernels, both with the forward's warp roles (warp 4: TMA producer,
-// warp 5: MMA issuer, warps 0-3: one tile row per thread, TMEM lane == row):
+// Two kernels with the forward's warp roles: HD / 32 row warpgroups (thread
+// = TMEM lane = tile row), one TMA producer warp and two MMA issuer warps.
 //
 // dq kernel  (one CTA per 128 query rows of one (batch, query head))
-//     per key tile:  S = Q K^T, dP = dO V^T          (TMEM, f32)
-//                    dS = w (dP - c)                  (registers -> smem, 16-bit)
-//                    dQ += dS K                       (TMEM, K reused as an MN-major operand)
-//     w = p for softmax1 (p = exp2(s log2e scale - m) / l from the saved row
-//     statistics) and w = 1[p>0] (sparsemax) or sqrt(p) (entmax15): the
-//     closed-form backwards of vutils/entmax.py:148-157 and :175-183 and the
-//     softmax Jacobian.  The row correction c is sum_j w dP / sum_j w for the
-//     sparse normalizers (a first pass over the key tiles) and O . dO for
+//     per key tile:  S = Q K^T, dP = dO V^T          (TMEM, f32; issuer 1)
+//                    dS = w (dP - c)                  (row warps -> TMEM, packed 16-bit)
+//                    dQ += dS K                       (TMEM; issuer 2, K reused as an MN-major operand)
+//     K streams through a 3-stage ring (it stays until its dQ MMA), V through
+//     2 stages.  w = p for softmax1 (p = exp2(s log2e scale - m) / l from the
+//     saved row statistics) and w = 1[p>0] (sparsemax) or sqrt(p) (entmax15):
+//     the closed-form backwards of vutils/entmax.py:148-157 and :175-183 and
+//     the softmax Jacobian.  The row correction c is sum_j w dP / sum_j w for
+//     the sparse normalizers (a first pass over the key tiles) and O . dO for
 //     softmax1 (the implicit sink has value 0).  c is saved for the dk/dv
 //     kernel.
 //
 // dk/dv kernel  (one CTA per 128 keys of one (batch, KV head); it walks every
 //                query head of the KV group, so GQA needs no atomics)
-//     per query tile:  S^T = K Q^T, dP^T = V dO^T      (TMEM)
-//                      P^T, dS^T                        (registers -> smem)
-//                      dV += P^T dO,  dK += dS^T Q      (TMEM accumulators)
+//     per unit (query head, 64 query rows):
+//                      S^T = K Q^T, dP^T = V dO^T      (TMEM, double-buffered; issuer 1)
+//                      P^T, dS^T                        (row warps -> shared memory, double-buffered)
+//                      dV += P^T dO,  dK += dS^T Q      (TMEM accumulators; issuer 2)
+//     Q / dO stream through a 3-stage ring of 64-row tiles.
 //
-// Gradients are written in the input dtype; dK carries the softmax scale.
+// Sparse normalizers skip the key tiles (dq kernel) and units (dk/dv kernel)
+// whose probabilities are all zero, from the forward's tile mask.  Optional
+// dropout scales dP by the forward's keep / (1 - p_drop) and feeds dV the
+// dropped probabilities.  Gradients are written in the input dtype; dK
+// carries the softmax scale.
 #include "common.cuh"
 #include "params.cuh"
 #include "tc_common.cuh"
@@ -120,9 +127,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 
   const int last_row = min(q0 + kBM - 1, g.q_len - 1);
   int k_hi = g.k_len;
-  if (p.causal) k_hi = min(k_hi, last_row + g.k_len - g.q_len + 1);
+  if (p.causal) k_hi = min(k_hi, last_row + g.shift + 1);
   int k_lo = 0;
-  if (p.window_left > 0) k_lo = max(0, q0 + g.k_len - g.q_len - p.window_left + 1);
+  if (p.window_left > 0) k_lo = max(0, q0 + g.shift - p.window_left + 1);
   k_lo = (k_lo / kBN) * kBN;
   const int n_tiles = k_hi > k_lo ? (k_hi - k_lo + kBN - 1) / kBN : 0;
   // Sparse normalizers skip the key tiles where every probability of the 128
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     const int i = q0 + row;
     const bool row_ok = i < g.q_len;
     const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
-    const int limit = i + g.k_len - g.q_len;
+    const int limit = i + g.shift;
     int vis_hi = row_ok ? g.k_len : 0;
     if (p.causal) vis_hi = min(vis_hi, limit + 1);
     int vis_lo = 0;
@@ -612,7 +619,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   const int bcoord = varlen ? 0 : b;
 
   // query rows that see any key of this tile
-  const int off = g.k_len - g.q_len;
+  const int off = g.shift;
   int i_lo = 0;
   if (p.causal) i_lo = max(0, k0 - off);
   int i_hi = g.q_len;

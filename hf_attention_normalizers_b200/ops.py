@@ -67,7 +67,7 @@ def _ptr(t: Optional[Tensor]) -> ctypes.c_void_p:
 # dense
 # ---------------------------------------------------------------------------
 def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, mask=None,
-                dropout_p=0.0, seed=None) -> N.AttnDesc:
+                dropout_p=0.0, seed=None, key_lengths=None) -> N.AttnDesc:
     b, hq, lq, d = q.shape
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=k.shape[1],
@@ -75,7 +75,8 @@ def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, m
         cu_seqlens_k=None, scale=float(scale), causal=int(bool(causal)),
         window_left=int(window_left), grad_dtype=dtype_id(q) if grad_dtype is None else grad_dtype,
         tile_mask=_mask_ptr(mask), dropout_p=float(dropout_p),
-        dropout_seed=None if (seed is None or dropout_p == 0.0) else seed.data_ptr())
+        dropout_seed=None if (seed is None or dropout_p == 0.0) else seed.data_ptr(),
+        key_lengths=None if key_lengths is None else key_lengths.data_ptr())
 
 
 def mask_words(normalizer: int, heads_q: int, batch: int, len_q: int, len_k: int) -> int:
@@ -111,18 +112,23 @@ def _as_bhsd(o: Tensor, out_bshd: bool) -> Tensor:
 @torch.library.custom_op("hfan::attn_fwd", mutates_args=())
 def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, causal: bool,
              window_left: int, out_bshd: bool, dropout_p: float = 0.0,
-             seed: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+             seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     """Returns (o, stats, mask): stats float32 [2, Hq, B*S] (see hfan.h) and the
     int32 key-tile support mask of the sparse normalizers (empty for softmax1),
     which the backward uses to skip all-zero tiles.  ``dropout_p > 0`` drops
-    probabilities with the keep bits generated from the device int64 ``seed``."""
+    probabilities with the keep bits generated from the device int64 ``seed``.
+    ``key_lengths`` (int32 [B]) gives every sequence its own key count with the
+    causal mask aligned at the first key: HF's right-padded batch."""
     _require_cuda(q, k, v)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
+    if key_lengths is not None:
+        key_lengths = key_lengths.to(device=q.device, dtype=torch.int32).contiguous()
     o = _new_out(q, out_bshd)
     b, hq, lq, _ = q.shape
     stats = torch.empty((2, hq, b * lq), dtype=torch.float32, device=q.device)
     mask = _new_mask(q.device, normalizer, hq, b, lq, k.shape[2])
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed,
+                       key_lengths=key_lengths)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(_as_bhsd(o, out_bshd)),
                                       _ptr(stats), _stream(q)), "hfan_attn_fwd")
@@ -130,7 +136,7 @@ def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, cau
 
 
 @attn_fwd.register_fake
-def _(q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p=0.0, seed=None):
+def _(q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p=0.0, seed=None, key_lengths=None):
     b, hq, lq, d = q.shape
     o = _new_out(q, out_bshd)
     return (o, q.new_empty((2, hq, b * lq), dtype=torch.float32),
@@ -140,15 +146,20 @@ def _(q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p=0.0, 
 @torch.library.custom_op("hfan::attn_bwd", mutates_args=())
 def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, normalizer: int,
              scale: float, causal: bool, window_left: int, dropout_p: float = 0.0,
-             seed: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+             seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
     do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
     dq = torch.empty_like(q, memory_format=torch.contiguous_format)
-    dk = torch.empty_like(k, memory_format=torch.contiguous_format)
-    dv = torch.empty_like(v, memory_format=torch.contiguous_format)
+    # keys past a sequence's length get no gradient from the kernels: zeros
+    new_kv = torch.zeros_like if key_lengths is not None else torch.empty_like
+    dk = new_kv(k, memory_format=torch.contiguous_format)
+    dv = new_kv(v, memory_format=torch.contiguous_format)
+    if key_lengths is not None:
+        key_lengths = key_lengths.to(device=q.device, dtype=torch.int32).contiguous()
     b, hq, lq, _ = q.shape
     corr = torch.empty((hq, b * lq), dtype=torch.float32, device=q.device)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed,
+                       key_lengths=key_lengths)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
@@ -157,26 +168,27 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
 
 
 @attn_bwd.register_fake
-def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropout_p=0.0, seed=None):
+def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropout_p=0.0, seed=None,
+      key_lengths=None):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
 
 
 def _attn_setup(ctx, inputs, output):
-    q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p, seed = inputs
+    q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p, seed, key_lengths = inputs
     o, stats, mask = output
-    ctx.save_for_backward(q, k, v, o, stats, mask, seed)
+    ctx.save_for_backward(q, k, v, o, stats, mask, seed, key_lengths)
     ctx.args = (normalizer, scale, causal, window_left, out_bshd, dropout_p)
     ctx.mark_non_differentiable(stats, mask)
 
 
 def _attn_backward(ctx, do, dstats, dmask):
-    q, k, v, o, stats, mask, seed = ctx.saved_tensors
+    q, k, v, o, stats, mask, seed, key_lengths = ctx.saved_tensors
     normalizer, scale, causal, window_left, out_bshd, dropout_p = ctx.args
     dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, mask, normalizer,
-                          scale, causal, window_left, dropout_p, seed)
-    return dq, dk, dv, None, None, None, None, None, None, None
+                          scale, causal, window_left, dropout_p, seed, key_lengths)
+    return dq, dk, dv, None, None, None, None, None, None, None, None
 
 
 torch.library.register_autograd("hfan::attn_fwd", _attn_backward, setup_context=_attn_setup)

@@ -99,6 +99,13 @@ typedef struct hfan_attn_desc {
   const int64_t* dropout_seed; /* device int64 seed (required when dropout_p > 0);     */
                         /* forward and backward must get the same value.  Replaces the */
                         /* saved seed of kernels/softmax1_hopper.py:434-441.           */
+  const int32_t* key_lengths; /* dense layout: [batch] device key counts (keys j <   */
+                        /* key_lengths[b] exist), or NULL = len_k for every sequence.  */
+                        /* With it the causal mask is aligned at the first key (row i  */
+                        /* sees j <= i): HF's causal mask of a right-padded batch.     */
+                        /* Replaces _hopper_right_padded_attention (backends.py:409-472) */
+                        /* with one launch.  Gradients of keys past a length are not   */
+                        /* written.                                                    */
 } hfan_attn_desc;
 
 /* Row statistics saved by the forward for the backward: float32 [2, heads_q, rows]
