@@ -594,11 +594,13 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         // chunk maxima (8 keys each) gate the candidate appends
         float cm[COLS / kCW];
         float tm = kNegInf;
+        bool grew = false;  // a chunk maximum entered the KT largest
 #pragma unroll
         for (int c = 0; c < COLS / kCW; ++c) {
           const float m8 = max_n<kCW>(sreg + c * kCW);
           cm[c] = m8;
           tm = fmaxf(tm, m8);
+          grew |= m8 > tk[KT - 1];
           float x = m8;
 #pragma unroll
           for (int k = 0; k < KT - 1; ++k) {  // branch-free insertion
@@ -609,7 +611,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           tk[KT - 1] = fmaxf(tk[KT - 1], x);
         }
         zmax = fmaxf(zmax, tm * zs);
-        {
+        // The bound only moves when the KT largest chunk maxima do (or when
+        // another warpgroup published a higher one: read every fourth tile);
+        // a stale bound only admits more candidates, never a wrong tau.
+        if (__any_sync(0xffffffffu, grew) || (t & 3) == 0) {
           float zk[KT];
 #pragma unroll
           for (int k = 0; k < KT; ++k) zk[k] = tk[k] * zs;

@@ -578,8 +578,7 @@ struct KLayout {
   static constexpr uint32_t DO = Q + kQStages * NH * kQHalf;     // kQStages stages
   static constexpr uint32_t PP = DO + kQStages * NH * kQHalf;    // 2 x P^T  [128 keys][64 queries]
   static constexpr uint32_t PD = PP + 2 * kHalf;                 // 2 x dS^T [128 keys][64 queries]
-  static constexpr uint32_t STATS = PD + 2 * kHalf;              // 2 buffers x 3 x 64 floats
-  static constexpr uint32_t BARS = STATS + 2 * 3 * kQB * 4;
+  static constexpr uint32_t BARS = PD + 2 * kHalf;
   static constexpr uint32_t CTL = BARS + sizeof(KBars);
   static constexpr uint32_t MASK = CTL + 16;                   // [kUnitWords] units with support
   static constexpr uint32_t TOTAL = MASK + kUnitWords * 4 + 1024;
@@ -604,7 +603,6 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::CTL);
   int* abort_ptr = reinterpret_cast<int*>(smem + L::CTL + 4);
   volatile int* abort_flag = abort_ptr;
-  float* stats_smem = reinterpret_cast<float*>(smem + L::STATS);  // [2][3][kQB]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint3 tile = tile_coords(p.tile_lpt);  // key tile 0 carries the most causal rows
@@ -654,12 +652,15 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       mbar_init(&bars->qd_full[s], 1);
       mbar_init(&bars->qd_empty[s], 1);
     }
+    // the S^T / dP^T buffer and the P^T / dS^T tiles of a list position are
+    // consumed and produced by one row group (NGRP groups take turns)
+    constexpr int GROUP_WARPS = Roles<HD>::ROW_THREADS / 32 / (Roles<HD>::NWG >= 4 ? 2 : 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->sdp_full[s], 1);
-      mbar_init(&bars->sdp_empty[s], Roles<HD>::ROW_THREADS / 32);
+      mbar_init(&bars->sdp_empty[s], GROUP_WARPS);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->p_full[s], Roles<HD>::ROW_THREADS / 32);
+      mbar_init(&bars->p_full[s], GROUP_WARPS);
       mbar_init(&bars->p_empty[s], 1);
     }
     mbar_init(&bars->done, 1);
@@ -783,9 +784,23 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       }
     }
   } else {
+    // Row warps.  Thread = TMEM lane = key of the tile.  The row warpgroups
+    // form NGRP independent groups that take the active units in turn (group
+    // g: list positions a with a % NGRP == g), so one group's TMEM loads,
+    // shared-memory stores and barrier waits overlap the other's arithmetic;
+    // with two groups, group g always uses S^T / dP^T buffer g and P^T / dS^T
+    // tile pair g.  A thread covers COLS = 32 query columns of its unit, in two
+    // steps of 16.  The row statistics of those 32 queries sit one per lane and
+    // are broadcast with shuffles (no shared-memory staging, no barrier
+    // between the warps).
     constexpr int NWG = Roles<HD>::NWG;
-    constexpr int COLS = kQB / NWG;  // query columns per warpgroup (16 for HD = 128)
-    const int wg = warp >> 2;         // warpgroup wg owns query columns [COLS wg, COLS (wg + 1))
+    constexpr int NGRP = NWG >= 4 ? 2 : 1;  // independent row groups
+    constexpr int GWG = NWG / NGRP;         // warpgroups per group
+    constexpr int COLS = kQB / GWG;         // query columns per thread
+    static_assert(COLS == 32, "one statistic per lane");
+    const int wg = warp >> 2;
+    const int grp = wg / GWG, sg = wg % GWG;
+    const int cb = sg * COLS;           // this thread's first query column of a unit
     const int row = threadIdx.x & 127;  // key within the tile
     const int j = k0 + row;
     const bool key_ok = j < g.k_len;
@@ -799,100 +814,87 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       seed_hi = (uint32_t)(sd >> 32);
     }
     bool ok = true;
-    // The named barriers run on every iteration, even after a timeout, so that
-    // no warp waits for one that has left the loop.
-    // Row statistics of a unit's 64 query rows, double-buffered in shared
-    // memory: after the barrier that starts unit u (every warp is done with
-    // unit u - 1 and its buffer), warpgroup 0 stages unit u + 1's (loaded into
-    // registers during unit u - 1) in the other buffer; the barrier that starts
-    // unit u + 1 publishes them.
-    float na = kPosInf, nb = 1.f, nc = 0.f;
-    auto fetch = [&](int u_) {
-      na = kPosInf;
-      nb = 1.f;
+    // Statistics of query column cb + lane of unit uu, negated where the
+    // arithmetic subtracts them: -st0 (log2 max or tau), 1/l (softmax1) and -c.
+    // Rows past the sequence read as st0 = +inf: x = -inf, p = 0.
+    auto load_stats = [&](int uu, float& nst, float& il, float& nc) {
+      nst = kNegInf;
+      il = 1.f;
       nc = 0.f;
-      if (wg != 0 || row >= kQB || u_ >= n_units) return;
-      const int iq = (m_lo + u_ % n_m) * kQB + row;
+      if (uu >= n_units) return;
+      const int iq = (m_lo + uu % n_m) * kQB + cb + lane;
       if (iq < g.q_len) {
-        const int64_t si = stat_index(p, g, kvh * groups + u_ / n_m, iq);
-        na = p.stats[si];
-        nb = p.stats[(int64_t)p.hq * p.rows_total + si];
-        nc = p.corr[si];
+        const int64_t si = stat_index(p, g, kvh * groups + uu / n_m, iq);
+        nst = -p.stats[si];
+        if (NORM == HFAN_SOFTMAX1) il = 1.f / p.stats[(int64_t)p.hq * p.rows_total + si];
+        nc = -p.corr[si];
       }
     };
-    auto stage = [&](int buf) {  // softmax1 stages them negated: x = s zs - st0 and dP - c are single packed ops
-      if (wg == 0 && row < kQB) {
-        float* sb_ = stats_smem + buf * 3 * kQB;
-        const float sg = -1.f;
-        sb_[row] = sg * na;
-        sb_[kQB + row] = NORM == HFAN_SOFTMAX1 ? 1.f / nb : 1.f;
-        sb_[2 * kQB + row] = sg * nc;
-      }
-    };
-    // u: the unit of list position a; u1, u2: the next two active units
+    // This group's units in list order, with their list positions.
     BitWalk walk(ubits_or_all, n_units);
-    int u = walk.next(), u1 = walk.next(), u2 = walk.next();
-    fetch(u);
-    stage(0);
-    fetch(u1);
-    for (int a = 0; u < n_units; ++a, u = u1, u1 = u2, u2 = walk.next()) {
+    int a_walk = -1;
+    auto next_mine = [&](int* pos) -> int {
+      int uu;
+      do {
+        uu = walk.next();
+        ++a_walk;
+      } while (uu < n_units && a_walk % NGRP != grp);
+      *pos = a_walk;
+      return uu;
+    };
+    int a, a_n;
+    int u = next_mine(&a), u_n = next_mine(&a_n);
+    float nst_c, il_c, nc_c, nst_n, il_n, nc_n;
+    load_stats(u, nst_c, il_c, nc_c);
+    load_stats(u_n, nst_n, il_n, nc_n);
+    while (u < n_units) {
       const int m = m_lo + u % n_m;
       const int qbase = m * kQB;
       const int bf = a & 1;
-      named_bar_sync(1, Roles<HD>::ROW_THREADS);
-      stage(bf ^ 1);  // unit u1
-      fetch(u2);
-      const float* st0s = stats_smem + bf * 3 * kQB;
-      const float* st1s = st0s + kQB;
-      const float* crs = st1s + kQB;
-      if (!ok) continue;
-      if (!(ok = wait_warp(&bars->sdp_full[bf], (a >> 1) & 1, abort_flag))) continue;
+      if (!(ok = wait_warp(&bars->sdp_full[bf], (a >> 1) & 1, abort_flag))) break;
       tc_fence_after();
       // visible queries of this key: [c_lo, c_hi) relative to qbase
       const int jl = j - off;  // causal: query i sees key j iff i >= j - off
       int c_lo = p.causal ? jl - qbase : -1 << 30;
       int c_hi = key_ok ? g.q_len - qbase : -(1 << 30);
       if (p.window_left > 0) c_hi = min(c_hi, jl + p.window_left - qbase);
-      uint32_t rs[COLS], rd[COLS];
-      if constexpr (COLS == 16) {
-        tmem_ld16(tmem_s + bf * kQB + lane_addr + wg * COLS, rs);
-        tmem_ld16(tmem_dp + bf * kQB + lane_addr + wg * COLS, rd);
-      } else {
-        tmem_ld32(tmem_s + bf * kQB + lane_addr + wg * COLS, *reinterpret_cast<uint32_t(*)[32]>(rs));
-        tmem_ld32(tmem_dp + bf * kQB + lane_addr + wg * COLS, *reinterpret_cast<uint32_t(*)[32]>(rd));
-      }
-      tmem_wait_ld();
-      tc_fence_before();
-      warp_arrive(&bars->sdp_empty[bf]);  // the unit after next may reuse this buffer
-      uint32_t ppk[COLS / 2], dpk[COLS / 2];
-      const int cb = wg * COLS;
       const int lo = c_lo - cb, hi = c_hi - cb;
-      {
-        const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= COLS);
-        const uint64_t zs2 = f2_pack(zs, zs);
+      const bool full = __all_sync(0xffffffffu, lo <= 0 && hi >= COLS);
+      const uint64_t zs2 = f2_pack(zs, zs);
+      const int hqu = kvh * groups + u / n_m;
+      uint32_t ppk[COLS / 2], dpk[COLS / 2];
 #pragma unroll
-        for (int e = 0; e < COLS; e += 2) {
-          // statistics of query columns e, e+1 (broadcast 8-byte loads; staged negated)
-          const int col = cb + e;
-          const uint64_t nst = *reinterpret_cast<const uint64_t*>(st0s + col);
-          const uint64_t nc2 = *reinterpret_cast<const uint64_t*>(crs + col);
-          uint64_t x = ffma2(f2_pack(__uint_as_float(rs[e]), __uint_as_float(rs[e + 1])), zs2, nst);
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t rs[16], rd[16];
+        tmem_ld16(tmem_s + bf * kQB + lane_addr + cb + 16 * hf, rs);
+        tmem_ld16(tmem_dp + bf * kQB + lane_addr + cb + 16 * hf, rd);
+        tmem_wait_ld();
+        if (hf == 1) {
+          tc_fence_before();
+          warp_arrive(&bars->sdp_empty[bf]);  // the group's next unit may reuse this buffer
+        }
+#pragma unroll
+        for (int e2 = 0; e2 < 16; e2 += 2) {
+          const int e = 16 * hf + e2;  // column within the thread's 32
+          const uint64_t nst = f2_pack(__shfl_sync(0xffffffffu, nst_c, e), __shfl_sync(0xffffffffu, nst_c, e + 1));
+          const uint64_t nc2 = f2_pack(__shfl_sync(0xffffffffu, nc_c, e), __shfl_sync(0xffffffffu, nc_c, e + 1));
+          uint64_t x = ffma2(f2_pack(__uint_as_float(rs[e2]), __uint_as_float(rs[e2 + 1])), zs2, nst);
           if (!full)
             x = f2_pack(e >= lo && e < hi ? f2_lo(x) : kNegInf, e + 1 >= lo && e + 1 < hi ? f2_hi(x) : kNegInf);
           uint64_t g2, ks2 = 0;
           if (drop) {  // keep / (1 - p_drop) of (query row, this key), as in the forward
-            const uint64_t r0 = ((uint64_t)b * p.hq + (kvh * groups + u / n_m)) * p.len_q + (qbase + col);
+            const uint64_t r0 = ((uint64_t)b * p.hq + hqu) * p.len_q + (qbase + cb + e);
             const uint32_t jg = (uint32_t)(j >> 2), js = (uint32_t)(j & 3);
             const uint32_t w0 = (dropout_keep4(r0, jg, seed_lo, seed_hi, p.drop_thr24) >> js) & 1u;
             const uint32_t w1 = (dropout_keep4(r0 + 1, jg, seed_lo, seed_hi, p.drop_thr24) >> js) & 1u;
             ks2 = f2_pack(w0 ? p.drop_scale : 0.f, w1 ? p.drop_scale : 0.f);
-            g2 = ffma2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), ks2, nc2);
+            g2 = ffma2(f2_pack(__uint_as_float(rd[e2]), __uint_as_float(rd[e2 + 1])), ks2, nc2);
           } else {
-            g2 = fadd2(f2_pack(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1])), nc2);
+            g2 = fadd2(f2_pack(__uint_as_float(rd[e2]), __uint_as_float(rd[e2 + 1])), nc2);
           }
           uint64_t pr, ds;
           if (NORM == HFAN_SOFTMAX1) {
-            const uint64_t il = *reinterpret_cast<const uint64_t*>(st1s + col);
+            const uint64_t il = f2_pack(__shfl_sync(0xffffffffu, il_c, e), __shfl_sync(0xffffffffu, il_c, e + 1));
             pr = fmul2(f2_pack(ex2_ftz(f2_lo(x)), ex2_ftz(f2_hi(x))), il);
             ds = fmul2(pr, g2);
           } else if (NORM == HFAN_SPARSEMAX) {
@@ -911,13 +913,21 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       // P^T / dS^T tile pair a & 1 is free once the dV / dK of list position a - 2 completed
       const int pb = a & 1;
       if (a >= 2) {
-        if (!(ok = wait_warp(&bars->p_empty[pb], ((a >> 1) & 1) ^ 1, abort_flag))) continue;
+        if (!(ok = wait_warp(&bars->p_empty[pb], ((a >> 1) & 1) ^ 1, abort_flag))) break;
       }
-      store_chunks_sw128<COLS / 8>(smem + L::PP + pb * kHalf, row, wg * (COLS / 8), ppk);
-      store_chunks_sw128<COLS / 8>(smem + L::PD + pb * kHalf, row, wg * (COLS / 8), dpk);
+      store_chunks_sw128<COLS / 8>(smem + L::PP + pb * kHalf, row, cb / 8, ppk);
+      store_chunks_sw128<COLS / 8>(smem + L::PD + pb * kHalf, row, cb / 8, dpk);
       fence_proxy_async_smem();
       tc_fence_before();
       warp_arrive(&bars->p_full[pb]);
+      // the group's next unit (its statistics were loaded during this one)
+      u = u_n;
+      a = a_n;
+      nst_c = nst_n;
+      il_c = il_n;
+      nc_c = nc_n;
+      u_n = next_mine(&a_n);
+      load_stats(u_n, nst_n, il_n, nc_n);
     }
     if (ok && has_units) {
       ok = wait_warp(&bars->done, 0, abort_flag);
