@@ -270,6 +270,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #ifndef HFAN_KT_ENT
 #define HFAN_KT_ENT 4
 #endif
+#ifndef HFAN_KT_SPM
+#define HFAN_KT_SPM 4
+#endif
 #ifndef HFAN_VOTE_ITERS
 #define HFAN_VOTE_ITERS 3
 #endif
@@ -401,12 +404,13 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     if (lane == 0 && n_tiles > 0) {
       const uint32_t q_base = smem_u32(smem + L::Q);
       const uint32_t ring_base = smem_u32(smem + L::RING);
-      uint32_t base0 = 0, base1 = 0, ctrl_phase = 0;  // uses of stages 0 / 1 by finished K-only passes
+      // parity of the uses of each scan stage by the finished K-only passes
+      uint32_t base_par = 0, ctrl_phase = 0;
       auto wait_item = [&](int idx, int nst, int* st) -> bool {
         const int s_ = idx % nst;
-        const uint32_t uses = (uint32_t)(idx / nst) + (s_ == 0 ? base0 : s_ == 1 ? base1 : 0u);
+        const uint32_t par = ((uint32_t)(idx / nst) & 1u) ^ (s_ < kScanStages ? (base_par >> s_) & 1u : 0u);
         *st = s_;
-        return mbar_wait(&bars->full[s_], uses & 1, abort_flag);
+        return mbar_wait(&bars->full[s_], par, abort_flag);
       };
       int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = qk_issuer ? mbar_wait(&bars->q_full, 0, abort_flag) : true;
@@ -449,8 +453,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           }
         }
         if (!ok || fin) break;
-        base0 += (uint32_t)(n_tiles + 1) / 2;
-        base1 += (uint32_t)n_tiles / 2;
+#pragma unroll
+        for (int s_ = 0; s_ < kScanStages; ++s_) {
+          const int uses = n_tiles > s_ ? (n_tiles - s_ + kScanStages - 1) / kScanStages : 0;
+          base_par ^= (uint32_t)(uses & 1) << s_;
+        }
         if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
         ctrl_phase ^= 1;
         pass = ctl->next_pass;
@@ -490,14 +497,27 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     uint32_t sc = 0, pc = 0;
     bool ok = true;
     float sreg[COLS];  // raw scores s = q.k of this warpgroup's columns (masked: -inf)
+#ifdef HFAN_DIAG
+    long long dls_w = 0, dls_l = 0;
+#endif
     auto load_s = [&](int t) -> bool {
       const int sb = sc & 1;
+#ifdef HFAN_DIAG
+      long long c0_ = clock64();
+#endif
       if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
+#ifdef HFAN_DIAG
+      long long c1_ = clock64();
+      dls_w += c1_ - c0_;
+#endif
       uint32_t r[COLS / 32][32];
 #pragma unroll
       for (int c = 0; c < COLS / 32; ++c) tmem_ld32(tmem + lane_addr + sb * 128 + wg * COLS + c * 32, r[c]);
       tmem_wait_ld();
+#ifdef HFAN_DIAG
+      dls_l += clock64() - c1_;
+#endif
       tc_fence_before();
       warp_arrive(&bars->s_empty[sb]);
       ++sc;
@@ -569,7 +589,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     if (SCAN) {
       Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
-      constexpr int KT = NORM == HFAN_SPARSEMAX ? 4 : HFAN_KT_ENT;  // tracked chunk maxima (entmax15 supports are wider)
+      constexpr int KT = NORM == HFAN_SPARSEMAX ? HFAN_KT_SPM : HFAN_KT_ENT;  // tracked chunk maxima (entmax15 supports are wider)
       float tk[KT];  // the KT largest chunk maxima so far (raw scores, descending)
 #pragma unroll
       for (int k = 0; k < KT; ++k) tk[k] = kNegInf;
@@ -594,27 +614,32 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         // chunk maxima (8 keys each) gate the candidate appends
         float cm[COLS / kCW];
         float tm = kNegInf;
-        bool grew = false;  // a chunk maximum entered the KT largest
 #pragma unroll
         for (int c = 0; c < COLS / kCW; ++c) {
-          const float m8 = max_n<kCW>(sreg + c * kCW);
-          cm[c] = m8;
-          tm = fmaxf(tm, m8);
-          grew |= m8 > tk[KT - 1];
-          float x = m8;
-#pragma unroll
-          for (int k = 0; k < KT - 1; ++k) {  // branch-free insertion
-            const float hi_ = fmaxf(tk[k], x);
-            x = fminf(tk[k], x);
-            tk[k] = hi_;
-          }
-          tk[KT - 1] = fmaxf(tk[KT - 1], x);
+          cm[c] = max_n<kCW>(sreg + c * kCW);
+          tm = fmaxf(tm, cm[c]);
         }
         zmax = fmaxf(zmax, tm * zs);
-        // The bound only moves when the KT largest chunk maxima do (or when
-        // another warpgroup published a higher one: read every fourth tile);
-        // a stale bound only admits more candidates, never a wrong tau.
-        if (__any_sync(0xffffffffu, grew) || (t & 3) == 0) {
+        // A tile whose scores all lie at or below the admission bound changes
+        // nothing: it has no candidate, and its chunk maxima cannot raise the
+        // bound (the threshold of any set of values is at most its k-th
+        // largest member, so values <= thr never yield a bound above thr).
+        // Only tiles with a score above the bound somewhere in the warp (and
+        // every fourth tile, to adopt the other warpgroups' bounds) update the
+        // KT largest chunk maxima, the bound, and the buffers.
+        const bool heavy = __any_sync(0xffffffffu, tm > cd.thr_s) || (t & 3) == 0;
+        if (heavy) {
+#pragma unroll
+          for (int c = 0; c < COLS / kCW; ++c) {
+            float x = cm[c];
+#pragma unroll
+            for (int k = 0; k < KT - 1; ++k) {  // branch-free insertion
+              const float hi_ = fmaxf(tk[k], x);
+              x = fminf(tk[k], x);
+              tk[k] = hi_;
+            }
+            tk[KT - 1] = fmaxf(tk[KT - 1], x);
+          }
           float zk[KT];
 #pragma unroll
           for (int k = 0; k < KT; ++k) zk[k] = tk[k] * zs;
@@ -627,7 +652,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           }
         }
         DIAG_LAP(dt);
-        if (!cd.overflow && tm > cd.thr_s) {
+        if (heavy && !cd.overflow && tm > cd.thr_s) {
 #pragma unroll
           for (int c = 0; c < COLS / kCW; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
@@ -927,6 +952,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       DIAG_ADD(7, clock64() - diag_t0);
       DIAG_ADD(12, dg_s);
       DIAG_ADD(13, dg_pv);
+      DIAG_ADD(8, dls_w);
+      DIAG_ADD(9, dls_l);
     }
 #endif
     if (!ok) record_error(p, ctl, kDevWaitTimeout);
