@@ -160,6 +160,7 @@ def run_ours(args, rank, world, local_rank):
     stats = {n: torch.empty((2, hq, B * S), dtype=torch.float32, device=dev) for n in NORMS}
     masks = {n: torch.empty((ops.mask_words(N.NORMALIZER_IDS[n], hq, B, S, S),), dtype=torch.int32, device=dev)
              for n in NORMS}
+    wmeans = {n: ops.new_wmean(t["q"], N.NORMALIZER_IDS[n]) for n in NORMS}
     if world > 1:
         from hf_attention_normalizers_b200.sharding import gather_heads_into
 
@@ -175,8 +176,8 @@ def run_ours(args, rank, world, local_rank):
         if world == 1:
             for name in NORMS:
                 nid = N.NORMALIZER_IDS[name]
-                o, st, mk = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
-                ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1)
+                o, st, mk, wm = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
+                ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1, wmean=wm)
             return
         par = state["i"] % 2
         state["i"] += 1
@@ -187,10 +188,12 @@ def run_ours(args, rank, world, local_rank):
             nid = N.NORMALIZER_IDS[name]
             bf = sets[par][name]
             o = bf["o"][rank]
-            ops.attn_fwd_into(t["q"], t["k"], t["v"], o, stats[name], nid, scale, True, mask=masks[name])
+            ops.attn_fwd_into(t["q"], t["k"], t["v"], o, stats[name], nid, scale, True, mask=masks[name],
+                              wmean=wmeans[name])
             pending[par].append(gather_heads_into(bf["o"], async_op=True))
             ops.attn_bwd_into(t["do"], t["q"], t["k"], t["v"], o, stats[name], corr, bf["dq"][rank],
-                              bf["dk"][rank], bf["dv"][rank], nid, scale, True, mask=masks[name])
+                              bf["dk"][rank], bf["dv"][rank], nid, scale, True, mask=masks[name],
+                              wmean=wmeans[name])
             for x in ("dq", "dk", "dv"):
                 pending[par].append(gather_heads_into(bf[x], async_op=True))
 
@@ -244,7 +247,7 @@ def run_ours(args, rank, world, local_rank):
     phases = {}
     for name in NORMS:
         nid = N.NORMALIZER_IDS[name]
-        o, st, mk = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
+        o, st, mk, wm = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         reps = 3
         torch.cuda.synchronize()
@@ -253,7 +256,7 @@ def run_ours(args, rank, world, local_rank):
             ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
         ev[1].record()
         for _ in range(reps):
-            ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1)
+            ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1, wmean=wm)
         ev[2].record()
         torch.cuda.synchronize()
         fwd = ev[0].elapsed_time(ev[1]) / reps
@@ -570,13 +573,13 @@ def bench_prescaled(t, flops, norms=NORMS):
     out = {}
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
-        o, st, mk = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
+        o, st, mk, wm = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record()
         ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
         ev[1].record()
-        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, mk, nid, D ** -0.5, True, -1)
+        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, mk, nid, D ** -0.5, True, -1, wmean=wm)
         ev[2].record()
         torch.cuda.synchronize()
         f_ms, b_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
@@ -670,14 +673,14 @@ def bench_model(dev, steps=3, warmup=2, world=1, rank=0):
                 q = torch.randn(1, 16, seq, 128, device=dev, dtype=torch.bfloat16)
                 k = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
                 v = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
-                o, st, mk = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
-                ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1)
+                o, st, mk, wm = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1, wmean=wm)
                 torch.cuda.synchronize()
                 a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a0.record()
                 for _ in range(28):
-                    o, st, mk = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
-                    ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1)
+                    o, st, mk, wm = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                    ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1, wmean=wm)
                 a1.record()
                 torch.cuda.synchronize()
                 res["attention_ms"] = round(a0.elapsed_time(a1), 2)

@@ -52,6 +52,7 @@ class AttnDesc(ctypes.Structure):
         ("dropout_p", ctypes.c_float),
         ("dropout_seed", ctypes.c_void_p),
         ("key_lengths", ctypes.c_void_p),
+        ("wmean", HfanTensor),
     ]
 
 

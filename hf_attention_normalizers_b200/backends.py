@@ -67,8 +67,8 @@ def _fused_bshd(query, key, value, normalizer, scale, is_causal, window_left=Non
         raise ValueError("Query heads must be divisible by key/value heads.")
     actual_scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
     window = -1 if window_left is None else int(window_left)
-    o, _, _ = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
-                           window, True, float(dropout_p), dropout_seed(query, dropout_p), key_lengths)
+    o = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
+                           window, True, float(dropout_p), dropout_seed(query, dropout_p), key_lengths)[0]
     return o
 
 

@@ -151,6 +151,16 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   p.norm = desc->normalizer;
   p.grad_f32 = desc->grad_dtype == HFAN_FLOAT32;
   if (desc->cu_seqlens_q && desc->total_q < 0) return fail(HFAN_ERR_INVALID, "total_q must be >= 0");
+  if (desc->wmean.data != nullptr && desc->normalizer != HFAN_SOFTMAX1) {
+    const hfan_tensor& w = desc->wmean;
+    if ((reinterpret_cast<uintptr_t>(w.data) & 15u) != 0 || w.stride_token % 8 != 0 || w.stride_head % 8 != 0 ||
+        w.stride_batch % 8 != 0)
+      return fail(HFAN_ERR_INVALID, "wmean must be 16-byte aligned with strides that are multiples of 8 elements");
+    p.wm = desc->wmean.data;
+    p.wm_sb = desc->wmean.stride_batch;
+    p.wm_sh = desc->wmean.stride_head;
+    p.wm_st = desc->wmean.stride_token;
+  }
   if (desc->key_lengths != nullptr) {
     if (desc->cu_seqlens_q != nullptr)
       return fail(HFAN_ERR_INVALID, "key_lengths applies to the dense layout only");

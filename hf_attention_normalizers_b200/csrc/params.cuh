@@ -54,6 +54,10 @@ struct AttnParams {
   uint32_t drop_thr24;
   float drop_scale;
   const int64_t* drop_seed;
+  // Sparse normalizers: w-weighted mean of V per row (input dtype), written by
+  // the tensor-core forward and read by its backward (null: not used).
+  void* wm;
+  int64_t wm_sb, wm_sh, wm_st;
 
   float scale;
   int causal, window_left, norm;

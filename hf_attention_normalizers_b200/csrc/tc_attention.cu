@@ -343,7 +343,14 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   const uint32_t tmem_o = tmem + 256;  // O: HD columns
-  const uint32_t tmem_p = tmem + 384;  // P double buffer: 2 x 64 columns of packed 16-bit pairs
+  // P double buffer: 2 x 64 columns of packed 16-bit pairs.  Sparse with wmean
+  // requested: [384, 384 + HD) accumulates U = sum_j w_j v_j instead, and P
+  // and W (packed) overwrite each warpgroup's own columns of the S buffer they
+  // came from (so S(t + 2) waits for P V(t) and W V(t)).
+  const uint32_t tmem_p = tmem + 384;
+  const uint32_t tmem_u = tmem + 384;
+  const bool want_u = SPARSE && p.wm != nullptr;
+  constexpr int PCOLS = kBN / Roles<HD>::NWG;  // keys per warpgroup and S tile
   volatile int* abort_flag = &ctl->abort;
 
   if (warp == Roles<HD>::TMA_WARP) {
@@ -414,7 +421,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       };
       int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = qk_issuer ? mbar_wait(&bars->q_full, 0, abort_flag) : true;
-      uint32_t sc = 0;
+      uint32_t sc = 0, npre = 0;  // S tiles issued; K-only passes finished
       while (ok) {
         const bool fin = pass == kPassFinal;
         if (qk_issuer) {
@@ -422,7 +429,12 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             int ks;
             const int sb = sc & 1;
             if (!(ok = wait_item(fin ? (t ? 2 * t - 1 : 0) : t, fin ? L::NS : kScanStages, &ks))) break;
-            if (!(ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag))) break;
+            if (want_u && fin && t >= 2) {
+              // the buffer holds P and W of final-pass tile t - 2 until its P V is done
+              if (!(ok = mbar_wait(&bars->pv_done[sb], ((t >> 1) & 1) ^ 1, abort_flag))) break;
+            } else {
+              if (!(ok = mbar_wait(&bars->s_empty[sb], ((sc >> 1) & 1) ^ 1, abort_flag))) break;
+            }
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < HD / 16; ++kk) {
@@ -435,24 +447,52 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             ++sc;
           }
         } else if (fin) {
+          // S buffer of final-pass tile j (the K-only passes issued sc0 tiles before)
+          const uint32_t sc0 = (uint32_t)n_tiles * npre;
           for (int j = 0; j < n_tiles && ok; ++j) {
             int vs;
             const int pb = j & 1;
             if (!(ok = wait_item(min(2 * j + 2, 2 * n_tiles - 1), L::NS, &vs))) break;
             if (!(ok = mbar_wait(&bars->p_full[pb], (j >> 1) & 1, abort_flag))) break;
             tc_fence_after();
+            if (want_u) {
+              // A = P (and W) in the S buffer: keys [16 kk, 16 kk + 16) belong to
+              // warpgroup 16 kk / PCOLS, whose P occupies the first PCOLS / 2
+              // columns of its slice and W the next PCOLS / 2.
+              const int sbj = (int)((sc0 + (uint32_t)j) & 1u);
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk) {
-              // A = P [128 x 128 keys] in TMEM buffer pb (8 columns per 16 keys);
-              // B = V tile, MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
-              const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
-              mma_f16_ts(tmem_o, tmem_p + pb * 64 + kk * 8, bd, IDESC_PV, j > 0 || kk > 0);
+              for (int kk = 0; kk < kBN / 16; ++kk) {
+                const int wk = (16 * kk) / PCOLS, ko = 16 * kk - wk * PCOLS;
+                const uint32_t pcol = (uint32_t)(sbj * 128 + wk * PCOLS + ko / 2);
+                const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
+                mma_f16_ts(tmem_o, tmem + pcol, bd, IDESC_PV, j > 0 || kk > 0);
+              }
+              {
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk) {
+                  const int wk = (16 * kk) / PCOLS, ko = 16 * kk - wk * PCOLS;
+                  const uint32_t wcol = (uint32_t)(sbj * 128 + wk * PCOLS + PCOLS / 2 + ko / 2);
+                  const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
+                  mma_f16_ts(tmem_u, tmem + wcol, bd, IDESC_PV, j > 0 || kk > 0);
+                }
+              }
+              mma_commit(&bars->empty[vs]);
+              mma_commit(&bars->pv_done[sbj]);
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < kBN / 16; ++kk) {
+                // A = P [128 x 128 keys] in TMEM buffer pb (8 columns per 16 keys);
+                // B = V tile, MN-major (rows = keys, 64-wide head-dim blocks kHalf apart).
+                const uint64_t bd = sw128_desc(ring_base + vs * KV_BYTES + kk * 16 * 128, kHalf, 1024);
+                mma_f16_ts(tmem_o, tmem_p + pb * 64 + kk * 8, bd, IDESC_PV, j > 0 || kk > 0);
+              }
+              mma_commit(&bars->empty[vs]);
+              mma_commit(&bars->pv_done[pb]);
             }
-            mma_commit(&bars->empty[vs]);
-            mma_commit(&bars->pv_done[pb]);
           }
         }
         if (!ok || fin) break;
+        ++npre;
 #pragma unroll
         for (int s_ = 0; s_ < kScanStages; ++s_) {
           const int uses = n_tiles > s_ ? (n_tiles - s_ + kScanStages - 1) / kScanStages : 0;
@@ -852,8 +892,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #ifdef HFAN_DIAG
     long long dg_s = 0, dg_pv = 0;
 #endif
+    float wsum = 0.f;  // sparse: sum_j w_j of this warpgroup's keys (U's normaliser)
     for (int t = 0; t < n_tiles && (ok || !SPARSE); ++t) {
       if (ok) DIAG_T(dg_s, ok = load_s(t));
+      uint32_t wpk[COLS / 2];  // sparse with U: packed W of this warpgroup's keys
       float alpha = 1.f;
       bool rescale = false;
       if (!SPARSE) {
@@ -883,22 +925,51 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         l += f2_lo(l2) + f2_hi(l2);
       } else {
         const uint64_t zs2 = f2_pack(zs, zs), nt2 = f2_pack(ntau, ntau);
+        // keep bits of this warpgroup's COLS keys (bit j = key kb + j)
+        uint64_t kbits = ~0ull;
+        if (drop) {
+          const int kb = k_lo + t * kBN + wg * COLS;  // a multiple of 4: groups of four keys
+          kbits = 0ull;
+#pragma unroll
+          for (int g4 = 0; g4 < COLS / 4; ++g4)
+            kbits |= (uint64_t)dropout_keep4(drow, (uint32_t)((kb >> 2) + g4), seed_lo, seed_hi, p.drop_thr24)
+                     << (4 * g4);
+        }
+        uint64_t ws2 = 0;  // sum of w over the pairs (undropped)
+        bool nzl = false;  // dropout: some undropped p > 0 (the mask is about p, not the kept values)
 #pragma unroll
         for (int j = 0; j < COLS; j += 2) {
           uint64_t d = ffma2(f2_pack(sreg[j], sreg[j + 1]), zs2, nt2);
           d = f2_pack(fmaxf(f2_lo(d), 0.f), fmaxf(f2_hi(d), 0.f));
+          // w = dp/dz up to the constant the backward folds in: 1[p > 0] or (z - tau)_+
+          uint64_t w = NORM == HFAN_SPARSEMAX ? f2_pack(f2_lo(d) > 0.f ? 1.f : 0.f, f2_hi(d) > 0.f ? 1.f : 0.f) : d;
+          if (drop && track) nzl |= (f2_lo(d) > 0.f) | (f2_hi(d) > 0.f);
           if (NORM != HFAN_SPARSEMAX) d = fmul2(d, d);
+          if (want_u) {
+            ws2 = fadd2(ws2, w);
+            if (drop) {
+              const uint64_t ks = f2_pack(((kbits >> j) & 1ull) ? p.drop_scale : 0.f,
+                                          ((kbits >> (j + 1)) & 1ull) ? p.drop_scale : 0.f);
+              w = fmul2(w, ks);
+            }
+            wpk[j / 2] = pack2<BF16>(f2_lo(w), f2_hi(w));
+          }
+          if (drop) {
+            d = fmul2(d, f2_pack(((kbits >> j) & 1ull) ? p.drop_scale : 0.f,
+                                 ((kbits >> (j + 1)) & 1ull) ? p.drop_scale : 0.f));
+          }
           sreg[j] = f2_lo(d);
           sreg[j + 1] = f2_hi(d);
         }
+        wsum += f2_lo(ws2) + f2_hi(ws2);
         if (track) {  // this warp's 32 rows x COLS keys: any p > 0 sets the tile's bit for its 64-row half
-          const unsigned bal = __ballot_sync(0xffffffffu, max_n<COLS>(sreg) > 0.f);
+          const unsigned bal = __ballot_sync(0xffffffffu, drop ? nzl : max_n<COLS>(sreg) > 0.f);
           const int kt = kt0 + t;
           if (lane == 0 && bal != 0u)
             atomicOr(&sbits[((warp & 3) >> 1) * kMaskWordsMax + (kt >> 5)], 1u << (kt & 31));
         }
       }
-      if (drop) {
+      if (drop && !SPARSE) {
         const int kb = k_lo + t * kBN + wg * COLS;  // a multiple of 4: groups of four keys
 #pragma unroll
         for (int g4 = 0; g4 < COLS / 4; ++g4) {
@@ -924,19 +995,34 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         tmem_st32(tmem_o + lane_addr + wg * 32, r);
         tmem_wait_st();
       }
-      if (pc >= 2) {
-        DIAG_T(dg_pv, ok = wait_warp(&bars->pv_done[pb], ((pc >> 1) & 1) ^ 1, abort_flag));
-        if (!ok) continue;
-        tc_fence_after();
-      }
-      // this warpgroup's COLS keys of the P row -> TMEM columns
-      // [COLS/2 wg, COLS/2 (wg + 1)) of buffer pb, packed in key order
+      if (want_u) {
+        // P, then W, over this warpgroup's own COLS columns of the S buffer
+        // the tile came from (read into registers above; nobody else reads
+        // them, and the buffer is reissued only after this tile's P V)
+        const uint32_t sl = tmem + lane_addr + ((sc - 1) & 1) * 128 + wg * COLS;
 #pragma unroll
-      for (int c = 0; c < COLS / 32; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < COLS / 32; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
-        tmem_st16(tmem_p + lane_addr + pb * 64 + wg * (COLS / 2) + c * 16, pk);
+          for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
+          tmem_st16(sl + c * 16, pk);
+          tmem_st16(sl + COLS / 2 + c * 16, *reinterpret_cast<uint32_t(*)[16]>(wpk + c * 16));
+        }
+      } else {
+        if (pc >= 2) {
+          DIAG_T(dg_pv, ok = wait_warp(&bars->pv_done[pb], ((pc >> 1) & 1) ^ 1, abort_flag));
+          if (!ok) continue;
+          tc_fence_after();
+        }
+        // this warpgroup's COLS keys of the P row -> TMEM columns
+        // [COLS/2 wg, COLS/2 (wg + 1)) of buffer pb, packed in key order
+#pragma unroll
+        for (int c = 0; c < COLS / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
+          tmem_st16(tmem_p + lane_addr + pb * 64 + wg * (COLS / 2) + c * 16, pk);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
@@ -944,7 +1030,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       ++pc;
     }
     if (ok && n_tiles > 0) {
-      ok = wait_warp(&bars->pv_done[(pc - 1) & 1], ((pc - 1) >> 1) & 1, abort_flag);
+      // with U: the last tile's P V was committed to the barrier of its S buffer
+      const int lb = want_u ? (int)((sc - 1) & 1u) : (int)((pc - 1) & 1u);
+      ok = wait_warp(&bars->pv_done[lb], ((pc - 1) >> 1) & 1, abort_flag);
       tc_fence_after();
     }
 #ifdef HFAN_DIAG
@@ -965,14 +1053,16 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             sbits[half * kMaskWordsMax + w];
       }
     }
-    if (!SPARSE) {
-      // total denominator of the row
+    if (!SPARSE || want_u) {
+      // total denominator of the row (softmax1) or sum_j w_j (sparse, U)
       float* xl = xch + 2 * NWG * 128;
-      xl[wg * 128 + row] = l;
+      xl[wg * 128 + row] = SPARSE ? wsum : l;
       named_bar_sync(1, NT);
-      l = 0.f;
+      float tot = 0.f;
 #pragma unroll
-      for (int w = 0; w < NWG; ++w) l += xl[w * 128 + row];
+      for (int w = 0; w < NWG; ++w) tot += xl[w * 128 + row];
+      if (SPARSE) wsum = tot;
+      else l = tot;
     }
 
     // ---- epilogue: this warpgroup's 32 columns of the O row -> global, row
@@ -1000,6 +1090,32 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
           v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
           *reinterpret_cast<uint4*>(orow + col + j) = v;
+        }
+      }
+    }
+    if (want_u) {
+      // this warpgroup's 32 columns of wmean = U / sum_j w_j
+      const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+      T* wrow = static_cast<T*>(p.wm) + qrow_off(p, g, b, h, row_ok ? i : 0, p.wm_sb, p.wm_sh, p.wm_st);
+      uint32_t r[32];
+      const int col = wg * 32;
+      if (n_tiles > 0) {
+        tmem_ld32(tmem_u + lane_addr + col, r);
+        tmem_wait_ld();
+      }
+      if (n_tiles == 0 || !ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 v;
+          v.x = pack2<BF16>(__uint_as_float(r[j + 0]) * inv, __uint_as_float(r[j + 1]) * inv);
+          v.y = pack2<BF16>(__uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
+          v.z = pack2<BF16>(__uint_as_float(r[j + 4]) * inv, __uint_as_float(r[j + 5]) * inv);
+          v.w = pack2<BF16>(__uint_as_float(r[j + 6]) * inv, __uint_as_float(r[j + 7]) * inv);
+          *reinterpret_cast<uint4*>(wrow + col + j) = v;
         }
       }
     }

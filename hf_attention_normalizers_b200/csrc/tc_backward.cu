@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   constexpr int NH = L::NH;
   constexpr uint32_t TILE = NH * kHalf;
   constexpr bool SPARSE = NORM != HFAN_SOFTMAX1;
-  constexpr int NPASS = SPARSE ? 2 : 1;
+  // Sparse normalizers sweep the key tiles twice (the row correction c, then
+  // dQ) unless the forward saved wmean, which gives c = dO . wmean directly.
+  const int NPASS = SPARSE && p.wm == nullptr ? 2 : 1;
   constexpr uint32_t IDESC_S = idesc_f16(BF16, kBM, kBN, false, false);
   constexpr uint32_t IDESC_DQ = idesc_f16(BF16, kBM, HD, false, true);
 
@@ -355,13 +357,18 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       *sa = ra;
       *sb = rb;
     };
-    if (NORM == HFAN_SOFTMAX1) {
-      // c = O . dO (the implicit sink carries no value); warpgroup wg sums the
-      // head-dim slice [HD/NWG wg, HD/NWG (wg + 1)), then the slices are combined.
+    if (NORM == HFAN_SOFTMAX1 || NPASS == 1) {
+      // c = O . dO for softmax1 (the implicit sink carries no value) and
+      // dO . wmean for the sparse normalizers (sum_j w_j dP_j / sum_j w_j with
+      // dP_j = dO . v_j); warpgroup wg sums the head-dim slice
+      // [HD/NWG wg, HD/NWG (wg + 1)), then the slices are combined.
       constexpr int DW = HD / NWG;
       float acc = 0.f;
       if (row_ok) {
-        const T* orow = static_cast<const T*>(p.o) + qrow_off(p, g, b, h, i, p.o_sb, p.o_sh, p.o_st) + wg * DW;
+        const T* orow = NORM == HFAN_SOFTMAX1
+                            ? static_cast<const T*>(p.o) + qrow_off(p, g, b, h, i, p.o_sb, p.o_sh, p.o_st) + wg * DW
+                            : static_cast<const T*>(p.wm) + qrow_off(p, g, b, h, i, p.wm_sb, p.wm_sh, p.wm_st) +
+                                  wg * DW;
         const T* drow = static_cast<const T*>(p.dout) + qrow_off(p, g, b, h, i, p.do_sb, p.do_sh, p.do_st) + wg * DW;
 #pragma unroll
         for (int d = 0; d < DW; d += 8) {
@@ -433,7 +440,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       return f2_pack(fmaxf(f2_lo(x), 0.f), fmaxf(f2_hi(x), 0.f));
     };
 
-    if (SPARSE) {
+    if (SPARSE && NPASS == 2) {
       float num = 0.f, den = 0.f;
       for (int a = 0; a < n_act && ok; ++a) {
         const int t = tile_at(a);

@@ -55,6 +55,6 @@ def fused_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
     check_dropout(dropout_p, query)
     actual_scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
     window = -1 if window_left is None else int(window_left)
-    o, _, _ = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
-                           window, bool(out_bshd), float(dropout_p), dropout_seed(query, dropout_p))
+    o = ops.attn_fwd(query, key, value, N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal),
+                           window, bool(out_bshd), float(dropout_p), dropout_seed(query, dropout_p))[0]
     return o

@@ -67,7 +67,7 @@ def _ptr(t: Optional[Tensor]) -> ctypes.c_void_p:
 # dense
 # ---------------------------------------------------------------------------
 def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, mask=None,
-                dropout_p=0.0, seed=None, key_lengths=None) -> N.AttnDesc:
+                dropout_p=0.0, seed=None, key_lengths=None, wmean=None) -> N.AttnDesc:
     b, hq, lq, d = q.shape
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=k.shape[1],
@@ -76,7 +76,21 @@ def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, m
         window_left=int(window_left), grad_dtype=dtype_id(q) if grad_dtype is None else grad_dtype,
         tile_mask=_mask_ptr(mask), dropout_p=float(dropout_p),
         dropout_seed=None if (seed is None or dropout_p == 0.0) else seed.data_ptr(),
-        key_lengths=None if key_lengths is None else key_lengths.data_ptr())
+        key_lengths=None if key_lengths is None else key_lengths.data_ptr(),
+        wmean=_t4(_wm_or_none(wmean)))
+
+
+def _wm_or_none(wmean: Optional[Tensor]) -> Optional[Tensor]:
+    return None if wmean is None or wmean.numel() == 0 else wmean
+
+
+def new_wmean(q: Tensor, normalizer: int) -> Tensor:
+    """The sparse forward's saved w-weighted mean of V, [B, Hq, S, D] in q's
+    dtype (empty for softmax1, fp32 inputs and head dims the tensor-core
+    kernels do not take: those backwards sweep the keys for the correction)."""
+    if normalizer == N.SOFTMAX1 or q.dtype not in (torch.bfloat16, torch.float16) or q.shape[-1] not in (64, 128):
+        return q.new_empty((0,))
+    return torch.empty(q.shape, dtype=q.dtype, device=q.device)
 
 
 def mask_words(normalizer: int, heads_q: int, batch: int, len_q: int, len_k: int) -> int:
@@ -112,10 +126,13 @@ def _as_bhsd(o: Tensor, out_bshd: bool) -> Tensor:
 @torch.library.custom_op("hfan::attn_fwd", mutates_args=())
 def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, causal: bool,
              window_left: int, out_bshd: bool, dropout_p: float = 0.0,
-             seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
-    """Returns (o, stats, mask): stats float32 [2, Hq, B*S] (see hfan.h) and the
-    int32 key-tile support mask of the sparse normalizers (empty for softmax1),
-    which the backward uses to skip all-zero tiles.  ``dropout_p > 0`` drops
+             seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None
+             ) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Returns (o, stats, mask, wmean): stats float32 [2, Hq, B*S] (see hfan.h),
+    the int32 key-tile support mask of the sparse normalizers (empty for
+    softmax1), which the backward uses to skip all-zero tiles, and the sparse
+    normalizers' w-weighted mean of V (``new_wmean``), which gives the backward
+    its row correction without a sweep over the keys.  ``dropout_p > 0`` drops
     probabilities with the keep bits generated from the device int64 ``seed``.
     ``key_lengths`` (int32 [B]) gives every sequence its own key count with the
     causal mask aligned at the first key: HF's right-padded batch."""
@@ -127,12 +144,13 @@ def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, cau
     b, hq, lq, _ = q.shape
     stats = torch.empty((2, hq, b * lq), dtype=torch.float32, device=q.device)
     mask = _new_mask(q.device, normalizer, hq, b, lq, k.shape[2])
+    wmean = new_wmean(q, normalizer)
     desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed,
-                       key_lengths=key_lengths)
+                       key_lengths=key_lengths, wmean=wmean)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(_as_bhsd(o, out_bshd)),
                                       _ptr(stats), _stream(q)), "hfan_attn_fwd")
-    return o, stats, mask
+    return o, stats, mask, wmean
 
 
 @attn_fwd.register_fake
@@ -140,13 +158,15 @@ def _(q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p=0.0, 
     b, hq, lq, d = q.shape
     o = _new_out(q, out_bshd)
     return (o, q.new_empty((2, hq, b * lq), dtype=torch.float32),
-            q.new_empty((mask_words(normalizer, hq, b, lq, k.shape[2]),), dtype=torch.int32))
+            q.new_empty((mask_words(normalizer, hq, b, lq, k.shape[2]),), dtype=torch.int32),
+            new_wmean(q, normalizer))
 
 
 @torch.library.custom_op("hfan::attn_bwd", mutates_args=())
 def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, normalizer: int,
              scale: float, causal: bool, window_left: int, dropout_p: float = 0.0,
-             seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+             seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None,
+             wmean: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
     do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
     dq = torch.empty_like(q, memory_format=torch.contiguous_format)
@@ -159,7 +179,7 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
     b, hq, lq, _ = q.shape
     corr = torch.empty((hq, b * lq), dtype=torch.float32, device=q.device)
     desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed,
-                       key_lengths=key_lengths)
+                       key_lengths=key_lengths, wmean=wmean)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
@@ -169,7 +189,7 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
 
 @attn_bwd.register_fake
 def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropout_p=0.0, seed=None,
-      key_lengths=None):
+      key_lengths=None, wmean=None):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
@@ -177,17 +197,17 @@ def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropo
 
 def _attn_setup(ctx, inputs, output):
     q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p, seed, key_lengths = inputs
-    o, stats, mask = output
-    ctx.save_for_backward(q, k, v, o, stats, mask, seed, key_lengths)
+    o, stats, mask, wmean = output
+    ctx.save_for_backward(q, k, v, o, stats, mask, seed, key_lengths, wmean)
     ctx.args = (normalizer, scale, causal, window_left, out_bshd, dropout_p)
-    ctx.mark_non_differentiable(stats, mask)
+    ctx.mark_non_differentiable(stats, mask, wmean)
 
 
-def _attn_backward(ctx, do, dstats, dmask):
-    q, k, v, o, stats, mask, seed, key_lengths = ctx.saved_tensors
+def _attn_backward(ctx, do, dstats, dmask, dwmean):
+    q, k, v, o, stats, mask, seed, key_lengths, wmean = ctx.saved_tensors
     normalizer, scale, causal, window_left, out_bshd, dropout_p = ctx.args
     dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, mask, normalizer,
-                          scale, causal, window_left, dropout_p, seed, key_lengths)
+                          scale, causal, window_left, dropout_p, seed, key_lengths, wmean)
     return dq, dk, dv, None, None, None, None, None, None, None, None
 
 
@@ -195,13 +215,15 @@ torch.library.register_autograd("hfan::attn_fwd", _attn_backward, setup_context=
 
 
 def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, normalizer: int, scale: float,
-                  causal: bool, window_left: int = -1, mask: Optional[Tensor] = None) -> None:
+                  causal: bool, window_left: int = -1, mask: Optional[Tensor] = None,
+                  wmean: Optional[Tensor] = None) -> None:
     """Forward into caller-owned outputs: ``o`` any [B, Hq, S, D] view with unit
     D stride (for example one rank's slice of a head-major gather buffer), ``stats``
-    float32 [2, Hq, B * S], optionally the int32 tile mask (``mask_words`` long).
+    float32 [2, Hq, B * S], optionally the int32 tile mask (``mask_words`` long)
+    and the sparse normalizers' ``wmean`` (``new_wmean``).
     No autograd; no allocation."""
     _require_cuda(q, k, v, o, stats)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, wmean=wmean)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _ptr(stats),
                                       _stream(q)), "hfan_attn_fwd")
@@ -209,12 +231,13 @@ def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, nor
 
 def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, corr: Tensor,
                   dq: Tensor, dk: Tensor, dv: Tensor, normalizer: int, scale: float, causal: bool,
-                  window_left: int = -1, mask: Optional[Tensor] = None) -> None:
+                  window_left: int = -1, mask: Optional[Tensor] = None, wmean: Optional[Tensor] = None) -> None:
     """Backward into caller-owned gradient views (unit D stride) and a float32
     [Hq, B * S] row-correction buffer (``mask``: the forward's tile mask, or
-    None).  No autograd; no allocation."""
+    None; ``wmean``: what the forward wrote, or None).  No autograd; no
+    allocation."""
     _require_cuda(do, q, k, v, o, dq, dk, dv)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, wmean=wmean)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),

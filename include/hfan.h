@@ -106,6 +106,14 @@ typedef struct hfan_attn_desc {
                         /* Replaces _hopper_right_padded_attention (backends.py:409-472) */
                         /* with one launch.  Gradients of keys past a length are not   */
                         /* written.                                                    */
+  hfan_tensor wmean;    /* sparsemax/entmax15, tensor-core path: [B, Hq, S, D] (dtype  */
+                        /* of q) written by the forward: per row the w-weighted mean   */
+                        /* of V, sum_j w_j v_j / sum_j w_j with w = 1[p > 0]            */
+                        /* (sparsemax) or sqrt(p) (entmax15).  The backward then gets  */
+                        /* the row correction c = dO . wmean without a second sweep    */
+                        /* over the keys.  data = NULL: not produced / not used.  No   */
+                        /* counterpart in the reference (its backward sweeps twice,    */
+                        /* kernels/sparse_entmax_hopper.py:230-300).                   */
 } hfan_attn_desc;
 
 /* Row statistics saved by the forward for the backward: float32 [2, heads_q, rows]

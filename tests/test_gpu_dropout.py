@@ -39,7 +39,7 @@ def test_dropout_matches_oracle_with_the_same_mask(norm, case, dtype):
     q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=7 + d)
     seed = torch.tensor(seed_value, dtype=torch.int64, device="cuda")
     qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
-    o, _, _ = ops.attn_fwd(qr, kr, vr, N.NORMALIZER_IDS[norm], d ** -0.5, True, -1, False, p_drop, seed)
+    o = ops.attn_fwd(qr, kr, vr, N.NORMALIZER_IDS[norm], d ** -0.5, True, -1, False, p_drop, seed)[0]
     o.backward(do)
     torch.cuda.synchronize()
     keep = oracle.philox.keep_mask(seed_value, p_drop, b, hq, s, s)

@@ -68,7 +68,7 @@ def check_threshold(norm, tau_k, support_k, q, k, scale, what, near=NEAR):
 
 
 def _stats(norm, q, k, v, scale):
-    _, st, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], scale, True, -1, False)
+    _, st, _, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], scale, True, -1, False)
     b, hq, lq, _ = q.shape  # stats [2][Hq][B * Lq]
     return st.reshape(2, hq, b, lq).transpose(1, 2).double().cpu().numpy()
 
@@ -209,7 +209,7 @@ def test_zero_tiles_skipped_and_results_unchanged(norm):
     v = torch.randn(b, h, s, d, generator=gen).to(torch.bfloat16).cuda()
     do = torch.randn(b, h, s, d, generator=gen).to(torch.bfloat16).cuda()
     nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
-    o, st, mk = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    o, st, mk, wm = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
     frac = ops.tile_mask_skipped_fraction(mk, h, b, s, s)
     print(f"{norm}: skipped tile fraction {frac:.3f}")
     assert frac > 0.5
@@ -225,3 +225,36 @@ def test_zero_tiles_skipped_and_results_unchanged(norm):
         assert err <= 1e-2 * float(e.float().abs().max()) + 1e-6
     out = (o, *with_mask)
     _tail_check(norm, q, k, v, do, out, 256, torch.bfloat16, f"local/{norm}")
+
+
+@pytest.mark.parametrize("norm", SPARSE)
+@pytest.mark.parametrize("d,dtype", [(128, torch.bfloat16), (64, torch.float16)])
+def test_saved_wmean_matches_oracle_and_two_pass_backward(norm, d, dtype):
+    """The forward's wmean (per row sum_j w_j v_j / sum_j w_j, w = 1[p > 0] for
+    sparsemax and sqrt(p) for entmax15) against the oracle's probabilities, and
+    the backward that takes its row correction from it (c = dO . wmean, one
+    sweep over the keys) against the backward that sweeps twice (c = sum_j w_j
+    dP_j / sum_j w_j from the recomputed scores).  The two corrections differ
+    by the 16-bit rounding of wmean, so the gradients agree to a stated bound,
+    not bit for bit."""
+    b, hq, hkv, s = 1, 8, 2, 1024
+    q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=11)
+    nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
+    o, st, mk, wm = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    assert wm.shape == q.shape
+    _, p, _ = oracle.attention_forward(_np(q), _np(k), _np(v), norm, scale=scale, causal=True, return_probs=True)
+    w = (p > 0).astype(np.float64) if norm == "sparsemax" else np.sqrt(p)
+    vv = np.repeat(_np(v), hq // hkv, axis=1)
+    ref = np.einsum("bhqk,bhkd->bhqd", w, vv) / w.sum(-1, keepdims=True)
+    err = np.abs(wm.double().cpu().numpy() - ref).max()
+    assert err <= 1e-2 * np.abs(ref).max() + 1e-3, f"wmean max err {err:.3e}"
+    grads = {}
+    for label, wmean in (("one sweep", wm), ("two sweeps", None)):
+        corr = torch.empty((hq, b * s), dtype=torch.float32, device="cuda")
+        g = [torch.empty_like(x) for x in (q, k, v)]
+        ops.attn_bwd_into(do, q, k, v, o, st, corr, *g, nid, scale, True, mask=mk, wmean=wmean)
+        grads[label] = (corr, *g)
+    torch.cuda.synchronize()
+    for name, a, e in zip(("corr", "dq", "dk", "dv"), grads["one sweep"], grads["two sweeps"]):
+        err = float((a.float() - e.float()).abs().max())
+        assert err <= 1e-2 * float(e.float().abs().max()) + 1e-5, f"{name}: max err {err:.3e}"
