@@ -526,8 +526,8 @@ def bench_varlen(dev, norms=("softmax1", "entmax15"), world=1, rank=0):
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
         fwd = lambda: ops.varlen_fwd(q, k, v, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
-        o, st, mk = fwd()
-        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, mk, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
+        o, st, mk, wm = fwd()
+        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, mk, cu_d, cu_d, mx, mx, nid, d ** -0.5, True, wm)
         bwd()
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]

@@ -87,7 +87,9 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
 constexpr float kRescaleLog2 = 8.f;
 
-enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2 };
+// kPassGather: the sparse rows' supports are all in the candidate buffers, so
+// the row warps gather P V from them and no final tensor-core pass runs.
+enum Pass : int { kPassFinal = 0, kPassTopC = 1, kPassSweep = 2, kPassGather = 3 };
 
 struct Bars {
   uint64_t q_full;
@@ -231,8 +233,8 @@ __device__ float buffer_solve_multi(const float* buf0, int capw, int row, const 
 
 // Raise thr to the buffer's own threshold and drop dead entries.  State is
 // passed by value so that callers keep it in registers.
-template <int NORM>
-__device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap, float zs) {
+template <int NORM, bool IDX>
+__device__ __noinline__ Cand buffer_compact(float* buf, uint16_t* ibuf, int row, Cand c, int cap, float zs) {
   DIAG_ADD(0, 1);
   bool exact;
   float sup;
@@ -244,7 +246,10 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
   int live = 0;
   for (int e = 0; e < c.n; ++e) {
     float z = buf[e * 128 + row];
-    if (z > c.thr) buf[live++ * 128 + row] = z;
+    if (z > c.thr) {
+      if (IDX) ibuf[live * 128 + row] = ibuf[e * 128 + row];
+      buf[live++ * 128 + row] = z;
+    }
   }
   c.n = live;
   // Stop buffering once compaction no longer frees room for a chunk of
@@ -253,6 +258,14 @@ __device__ __noinline__ Cand buffer_compact(float* buf, int row, Cand c, int cap
   // every chunk would cost more than the sweeps that settle such rows.
   if (live > (NORM == HFAN_SPARSEMAX ? cap / 2 : cap - kCompactRoom)) c.overflow = true;
   return c;
+}
+
+// Two 16-bit values (low half first in memory) -> packed f32x2.
+template <bool BF16>
+__device__ __forceinline__ uint64_t unpack2(uint32_t x) {
+  if (BF16) return f2_pack(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x));
+  return f2_pack(f.x, f.y);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -391,6 +404,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
         ctrl_phase ^= 1;
         pass = ctl->next_pass;
+        if (pass == kPassGather) break;
       }
       if (!ok) record_error(p, ctl, kDevWaitTimeout);
     }
@@ -501,6 +515,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         if (!(ok = mbar_wait(&bars->ctrl, ctrl_phase, abort_flag))) break;
         ctrl_phase ^= 1;
         pass = ctl->next_pass;
+        if (pass == kPassGather) break;
       }
       if (!ok) record_error(p, ctl, kDevWaitTimeout);
     }
@@ -529,9 +544,18 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // During the scan passes the V ring and the P buffer are idle; they hold
     // the candidate buffers (the producer loads V only in the final pass),
     // one slice per warpgroup.
-    constexpr int CAPW = (int)(L::CAND_BYTES / (128 * 4)) / NWG;
+    // Each entry: the score (z units, float) and, for sparsemax, its key
+    // (uint16: the tile relative to k_lo above JB bits, the column in the
+    // warpgroup's slice below), which the gather pass reads.  entmax15 keeps
+    // the larger score-only buffers: its wider supports overflow the smaller
+    // ones into whole-row sweeps.
+    constexpr bool IDX = NORM == HFAN_SPARSEMAX;
+    constexpr int CAPW = (int)(L::CAND_BYTES / (128 * (IDX ? 6 : 4))) / NWG;
+    constexpr int JB = COLS == 32 ? 5 : 6;
     float* cbuf0 = reinterpret_cast<float*>(smem + L::CAND);
     float* cbuf = cbuf0 + wg * CAPW * 128;
+    uint16_t* ibuf0 = reinterpret_cast<uint16_t*>(smem + L::CAND + NWG * CAPW * 128 * 4);
+    uint16_t* ibuf = ibuf0 + wg * CAPW * 128;
     float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [4096] floats
 
     uint32_t sc = 0, pc = 0;
@@ -626,8 +650,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #ifdef HFAN_DIAG
     long long diag_t0 = clock64();
 #endif
+    bool gather = false;  // the sparse final pass is a gather from the buffers
+    Cand cd{0, false, kNegInf, kNegInf};
     if (SCAN) {
-      Cand cd{0, false, kNegInf, kNegInf};
       float zmax = kNegInf;
       constexpr int KT = NORM == HFAN_SPARSEMAX ? HFAN_KT_SPM : HFAN_KT_ENT;  // tracked chunk maxima (entmax15 supports are wider)
       float tk[KT];  // the KT largest chunk maxima so far (raw scores, descending)
@@ -696,7 +721,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #pragma unroll
           for (int c = 0; c < COLS / kCW; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
-              if (cd.n > CAPW - kCW) cd = buffer_compact<NORM>(cbuf, row, cd, CAPW, zs);
+              if (cd.n > CAPW - kCW) cd = buffer_compact<NORM, IDX>(cbuf, ibuf, row, cd, CAPW, zs);
               if (!cd.overflow) {
                 // predicated appends: every value is written at slot n, and n
                 // only advances past the candidates
@@ -704,6 +729,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
                 for (int e = 0; e < kCW; ++e) {
                   const float x = sreg[c * kCW + e];
                   cbuf[cd.n * 128 + row] = x * zs;
+                  if (IDX) ibuf[cd.n * 128 + row] = (uint16_t)((t << JB) | (c * kCW + e));
                   cd.n += x > cd.thr_s ? 1 : 0;
                 }
               }
@@ -738,7 +764,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             int live = 0;
             for (int e = 0; e < cd.n; ++e) {
               const float z = cbuf[e * 128 + row];
-              if (z > cd.thr) cbuf[live++ * 128 + row] = z;
+              if (z > cd.thr) {
+                if (IDX) ibuf[live * 128 + row] = ibuf[e * 128 + row];
+                cbuf[live++ * 128 + row] = z;
+              }
             }
             cd.n = live;
             if (live > CAPW - kCompactRoom) cd.overflow = true;
@@ -803,10 +832,18 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         named_bar_sync(1, NT);
         if (threadIdx.x == 0) {
           const bool more_ = ctl->any_pending != 0 && sweep < kMaxSweeps && ctl->abort == 0;
-          ctl->next_pass = more_ ? kPassSweep : kPassFinal;
+          // Without sweeps every row's support is in its candidate buffers
+          // (every score above the final bound was buffered), so P V is
+          // gathered from them; rows settled by sweeps need the full pass.
+          const bool gather_ok = IDX && !DROP && sweep == 0 && ctl->any_pending == 0 && ctl->abort == 0 &&
+                                 n_tiles <= (65536 >> JB);
+          ctl->next_pass = more_ ? kPassSweep : (gather_ok ? kPassGather : kPassFinal);
+          DIAG_ADD(10, gather_ok && !more_ ? 1 : 0);
+          DIAG_ADD(11, more_ ? 1 : 0);
           mbar_arrive(&bars->ctrl);
         }
         named_bar_sync(1, NT);
+        gather = ctl->next_pass == kPassGather;
         if (ctl->next_pass != kPassSweep) break;
         // Besides the sums above the bound, a pending row buffers every
         // score above it again: once they fit (the bound is close to tau),
@@ -873,6 +910,92 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     if (threadIdx.x == 0) DIAG_ADD(6, clock64() - diag_t0);
     diag_t0 = clock64();
 #endif
+    // ---- sparse gather (kPassGather): O = sum_j p_j v_j and U = sum_j w_j v_j
+    // over the support entries of the candidate buffers, instead of a second
+    // Q K^T and a P V over every key tile.  Each thread first keeps the
+    // support of its own buffer in place (d = z - tau > 0 and the key) and
+    // sets the tile bits; then every warpgroup walks the NWG lists of its row
+    // for its 32 head-dim columns, reading V rows from global memory (L2).
+    // The order of the sums is fixed: buffer order (key order within a
+    // warpgroup), then warpgroup order.
+    auto gather_pv = [&](float tau_) {
+      int* xn = reinterpret_cast<int*>(xch + 6144);  // [NWG][128] list lengths
+      const T* vb = static_cast<const T*>(p.v) + key_off(p, b, kvh, 0, p.v_sb, p.v_sh, p.v_st);
+      auto vrow = [&](int w, int id) -> const T* {
+        const int key = k_lo + (id >> JB) * kBN + w * COLS + (id & (COLS - 1));
+        const int64_t tok = varlen ? (int64_t)(g.k_start + key) : (int64_t)key;
+        return vb + tok * p.v_st;
+      };
+      int m = 0;
+      for (int e = 0; e < cd.n; ++e) {
+        const float z = cbuf[e * 128 + row];
+        if (z > tau_) {
+          const uint16_t id = ibuf[e * 128 + row];
+          cbuf[m * 128 + row] = z - tau_;
+          ibuf[m * 128 + row] = id;
+          ++m;
+          // the four warpgroups read this V row next: bring it into L2 now
+          const T* vr = vrow(wg, id);
+#pragma unroll
+          for (int c = 0; c < HD * (int)sizeof(T); c += 128) prefetch_l2(reinterpret_cast<const char*>(vr) + c);
+          if (track) {
+            const int kt = kt0 + (id >> JB);
+            atomicOr(&sbits[(row >> 6) * kMaskWordsMax + (kt >> 5)], 1u << (kt & 31));
+          }
+        }
+      }
+      xn[wg * 128 + row] = m;
+      named_bar_sync(1, NT);
+      uint64_t acc[16], accu[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] = accu[j] = 0ull;
+      float wsum_ = 0.f;
+      for (int w = 0; w < NWG; ++w) {
+        const int mw = xn[w * 128 + row];
+        const float* db = cbuf0 + w * CAPW * 128;
+        const uint16_t* ib = ibuf0 + w * CAPW * 128;
+        for (int e = 0; e < mw; ++e) {
+          const float d = db[e * 128 + row];
+          const uint4* vp = reinterpret_cast<const uint4*>(vrow(w, ib[e * 128 + row]) + wg * 32);
+          // p = d (sparsemax) or d^2 (entmax15); w = 1[p > 0] or d
+          const float pr = NORM == HFAN_SPARSEMAX ? d : d * d;
+          const float wt = NORM == HFAN_SPARSEMAX ? 1.f : d;
+          wsum_ += wt;
+          const uint64_t p2 = f2_pack(pr, pr), w2 = f2_pack(wt, wt);
+          uint4 x[4];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) x[q4] = __ldg(vp + q4);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint32_t xs[4] = {x[q4].x, x[q4].y, x[q4].z, x[q4].w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const uint64_t v2 = unpack2<BF16>(xs[r]);
+              acc[q4 * 4 + r] = ffma2(p2, v2, acc[q4 * 4 + r]);
+              if (want_u) accu[q4 * 4 + r] = ffma2(w2, v2, accu[q4 * 4 + r]);
+            }
+          }
+        }
+      }
+      if (row_ok) {
+        auto put = [&](T* dst, const uint64_t (&a)[16], float inv) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 v;
+            v.x = pack2<BF16>(f2_lo(a[q4 * 4 + 0]) * inv, f2_hi(a[q4 * 4 + 0]) * inv);
+            v.y = pack2<BF16>(f2_lo(a[q4 * 4 + 1]) * inv, f2_hi(a[q4 * 4 + 1]) * inv);
+            v.z = pack2<BF16>(f2_lo(a[q4 * 4 + 2]) * inv, f2_hi(a[q4 * 4 + 2]) * inv);
+            v.w = pack2<BF16>(f2_lo(a[q4 * 4 + 3]) * inv, f2_hi(a[q4 * 4 + 3]) * inv);
+            reinterpret_cast<uint4*>(dst)[q4] = v;
+          }
+        };
+        put(static_cast<T*>(p.o) + qrow_off(p, g, b, h, i, p.o_sb, p.o_sh, p.o_st) + wg * 32, acc, 1.f);
+        if (want_u)
+          put(static_cast<T*>(p.wm) + qrow_off(p, g, b, h, i, p.wm_sb, p.wm_sh, p.wm_st) + wg * 32, accu,
+              wsum_ > 0.f ? 1.f / wsum_ : 0.f);
+      }
+    };
+
     // ---- final pass: P and O
     float m_ref = 0.f, l = wg == 0 ? 1.f : 0.f;  // the implicit zero logit counts once
     const float ntau = -tau;
@@ -893,7 +1016,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     long long dg_s = 0, dg_pv = 0;
 #endif
     float wsum = 0.f;  // sparse: sum_j w_j of this warpgroup's keys (U's normaliser)
-    for (int t = 0; t < n_tiles && (ok || !SPARSE); ++t) {
+    for (int t = 0; t < (gather ? 0 : n_tiles) && (ok || !SPARSE); ++t) {
       if (ok) DIAG_T(dg_s, ok = load_s(t));
       uint32_t wpk[COLS / 2];  // sparse with U: packed W of this warpgroup's keys
       float alpha = 1.f;
@@ -1029,7 +1152,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       warp_arrive(&bars->p_full[pb]);
       ++pc;
     }
-    if (ok && n_tiles > 0) {
+    if (ok && n_tiles > 0 && !gather) {
       // with U: the last tile's P V was committed to the barrier of its S buffer
       const int lb = want_u ? (int)((sc - 1) & 1u) : (int)((pc - 1) & 1u);
       ok = wait_warp(&bars->pv_done[lb], ((pc - 1) >> 1) & 1, abort_flag);
@@ -1045,6 +1168,15 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     }
 #endif
     if (!ok) record_error(p, ctl, kDevWaitTimeout);
+    if (SPARSE && IDX && !DROP && gather) {
+#ifdef HFAN_DIAG
+      const long long g0_ = clock64();
+#endif
+      gather_pv(tau);
+#ifdef HFAN_DIAG
+      if (threadIdx.x == 0) DIAG_ADD(14, clock64() - g0_);
+#endif
+    }
     if (SPARSE && track && p.tile_mask != nullptr) {
       named_bar_sync(1, NT);  // every row warp's support bits are in
       if (threadIdx.x < 2 * p.mask_words) {
@@ -1053,7 +1185,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
             sbits[half * kMaskWordsMax + w];
       }
     }
-    if (!SPARSE || want_u) {
+    if (!gather && (!SPARSE || want_u)) {
       // total denominator of the row (softmax1) or sum_j w_j (sparse, U)
       float* xl = xch + 2 * NWG * 128;
       xl[wg * 128 + row] = SPARSE ? wsum : l;
@@ -1068,7 +1200,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // ---- epilogue: this warpgroup's 32 columns of the O row -> global, row
     // statistics.  The TMEM load is warp-collective, so every lane loads; only
     // valid rows store.
-    {
+    if (!gather) {
       const float inv = SPARSE ? 1.f : 1.f / l;
       T* orow = static_cast<T*>(p.o) + qrow_off(p, g, b, h, row_ok ? i : 0, p.o_sb, p.o_sh, p.o_st);
       uint32_t r[32];
@@ -1093,7 +1225,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         }
       }
     }
-    if (want_u) {
+    if (want_u && !gather) {
       // this warpgroup's 32 columns of wmean = U / sum_j w_j
       const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
       T* wrow = static_cast<T*>(p.wm) + qrow_off(p, g, b, h, row_ok ? i : 0, p.wm_sb, p.wm_sh, p.wm_st);

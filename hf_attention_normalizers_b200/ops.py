@@ -247,18 +247,19 @@ def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats:
 # ---------------------------------------------------------------------------
 # varlen
 # ---------------------------------------------------------------------------
-def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=None) -> N.AttnDesc:
+def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=None, wmean=None) -> N.AttnDesc:
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=cu_q.numel() - 1, heads_q=q.shape[1],
         heads_kv=k.shape[1], head_dim=q.shape[2], len_q=int(max_q), len_k=int(max_k),
         total_q=q.shape[0], total_k=k.shape[0], cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=cu_k.data_ptr(),
         scale=float(scale), causal=int(bool(causal)), window_left=0, grad_dtype=dtype_id(q),
-        tile_mask=_mask_ptr(mask))
+        tile_mask=_mask_ptr(mask), wmean=_t3(_wm_or_none(wmean)))
 
 
 @torch.library.custom_op("hfan::varlen_fwd", mutates_args=())
 def varlen_fwd(q: Tensor, k: Tensor, v: Tensor, cu_q: Tensor, cu_k: Tensor, max_q: int, max_k: int,
-               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor, Tensor]:
+               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Returns (o, stats, mask, wmean) as ``attn_fwd`` does, over packed rows."""
     _require_cuda(q, k, v, cu_q, cu_k)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
     cu_q = cu_q.to(torch.int32).contiguous()
@@ -266,11 +267,12 @@ def varlen_fwd(q: Tensor, k: Tensor, v: Tensor, cu_q: Tensor, cu_k: Tensor, max_
     o = torch.empty_like(q, memory_format=torch.contiguous_format)
     stats = torch.empty((2, q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
     mask = _new_mask(q.device, normalizer, q.shape[1], cu_q.numel() - 1, int(max_q), int(max_k))
-    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask)
+    wmean = new_wmean(q, normalizer)
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask, wmean=wmean)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _ptr(stats),
                                       _stream(q)), "hfan_attn_fwd(varlen)")
-    return o, stats, mask
+    return o, stats, mask, wmean
 
 
 @varlen_fwd.register_fake
@@ -278,13 +280,14 @@ def _(q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             q.new_empty((2, q.shape[1], q.shape[0]), dtype=torch.float32),
             q.new_empty((mask_words(normalizer, q.shape[1], cu_q.shape[0] - 1, int(max_q), int(max_k)),),
-                        dtype=torch.int32))
+                        dtype=torch.int32),
+            new_wmean(q, normalizer))
 
 
 @torch.library.custom_op("hfan::varlen_bwd", mutates_args=())
 def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, cu_q: Tensor,
                cu_k: Tensor, max_q: int, max_k: int, normalizer: int, scale: float,
-               causal: bool) -> tuple[Tensor, Tensor, Tensor]:
+               causal: bool, wmean: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
     do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
     cu_q = cu_q.to(torch.int32).contiguous()
@@ -293,7 +296,7 @@ def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Te
     dk = torch.zeros_like(k, memory_format=torch.contiguous_format)
     dv = torch.zeros_like(v, memory_format=torch.contiguous_format)
     corr = torch.empty((q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
-    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask)
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask, wmean=wmean)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _t3(do),
                                       _ptr(stats), _ptr(corr), _t3(dq), _t3(dk), _t3(dv), _stream(q)),
@@ -302,7 +305,7 @@ def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Te
 
 
 @varlen_bwd.register_fake
-def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
+def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, wmean=None):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
@@ -310,16 +313,17 @@ def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, 
 
 def _varlen_setup(ctx, inputs, output):
     q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal = inputs
-    o, stats, mask = output
-    ctx.save_for_backward(q, k, v, o, stats, mask, cu_q, cu_k)
+    o, stats, mask, wmean = output
+    ctx.save_for_backward(q, k, v, o, stats, mask, cu_q, cu_k, wmean)
     ctx.args = (max_q, max_k, normalizer, scale, causal)
-    ctx.mark_non_differentiable(stats, mask)
+    ctx.mark_non_differentiable(stats, mask, wmean)
 
 
-def _varlen_backward(ctx, do, dstats, dmask):
-    q, k, v, o, stats, mask, cu_q, cu_k = ctx.saved_tensors
+def _varlen_backward(ctx, do, dstats, dmask, dwmean):
+    q, k, v, o, stats, mask, cu_q, cu_k, wmean = ctx.saved_tensors
     max_q, max_k, normalizer, scale, causal = ctx.args
-    dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal)
+    dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal,
+                            wmean)
     return dq, dk, dv, None, None, None, None, None, None, None
 
 
