@@ -161,6 +161,7 @@ def run_ours(args, rank, world, local_rank):
     masks = {n: torch.empty((ops.mask_words(N.NORMALIZER_IDS[n], hq, B, S, S),), dtype=torch.int32, device=dev)
              for n in NORMS}
     wmeans = {n: ops.new_wmean(t["q"], N.NORMALIZER_IDS[n]) for n in NORMS}
+    supports = {n: ops.new_dense_support(t["q"], t["k"], N.NORMALIZER_IDS[n]) for n in NORMS}
     if world > 1:
         from hf_attention_normalizers_b200.sharding import gather_heads_into
 
@@ -176,8 +177,9 @@ def run_ours(args, rank, world, local_rank):
         if world == 1:
             for name in NORMS:
                 nid = N.NORMALIZER_IDS[name]
-                o, st, mk, wm = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
-                ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1, wmean=wm)
+                o, st, mk, wm, sup = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
+                ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1, wmean=wm,
+                             support=sup)
             return
         par = state["i"] % 2
         state["i"] += 1
@@ -189,11 +191,11 @@ def run_ours(args, rank, world, local_rank):
             bf = sets[par][name]
             o = bf["o"][rank]
             ops.attn_fwd_into(t["q"], t["k"], t["v"], o, stats[name], nid, scale, True, mask=masks[name],
-                              wmean=wmeans[name])
+                              wmean=wmeans[name], support=supports[name])
             pending[par].append(gather_heads_into(bf["o"], async_op=True))
             ops.attn_bwd_into(t["do"], t["q"], t["k"], t["v"], o, stats[name], corr, bf["dq"][rank],
                               bf["dk"][rank], bf["dv"][rank], nid, scale, True, mask=masks[name],
-                              wmean=wmeans[name])
+                              wmean=wmeans[name], support=supports[name])
             for x in ("dq", "dk", "dv"):
                 pending[par].append(gather_heads_into(bf[x], async_op=True))
 
@@ -247,7 +249,7 @@ def run_ours(args, rank, world, local_rank):
     phases = {}
     for name in NORMS:
         nid = N.NORMALIZER_IDS[name]
-        o, st, mk, wm = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
+        o, st, mk, wm, sup = ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         reps = 3
         torch.cuda.synchronize()
@@ -256,7 +258,8 @@ def run_ours(args, rank, world, local_rank):
             ops.attn_fwd(t["q"], t["k"], t["v"], nid, scale, True, -1, False)
         ev[1].record()
         for _ in range(reps):
-            ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1, wmean=wm)
+            ops.attn_bwd(t["do"], t["q"], t["k"], t["v"], o, st, mk, nid, scale, True, -1, wmean=wm,
+                         support=sup)
         ev[2].record()
         torch.cuda.synchronize()
         fwd = ev[0].elapsed_time(ev[1]) / reps
@@ -526,8 +529,8 @@ def bench_varlen(dev, norms=("softmax1", "entmax15"), world=1, rank=0):
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
         fwd = lambda: ops.varlen_fwd(q, k, v, cu_d, cu_d, mx, mx, nid, d ** -0.5, True)
-        o, st, mk, wm = fwd()
-        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, mk, cu_d, cu_d, mx, mx, nid, d ** -0.5, True, wm)
+        o, st, mk, wm, sup = fwd()
+        bwd = lambda: ops.varlen_bwd(do, q, k, v, o, st, mk, cu_d, cu_d, mx, mx, nid, d ** -0.5, True, wm, sup)
         bwd()
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -573,13 +576,13 @@ def bench_prescaled(t, flops, norms=NORMS):
     out = {}
     for name in norms:
         nid = N.NORMALIZER_IDS[name]
-        o, st, mk, wm = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
+        o, st, mk, wm, sup = ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
         torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record()
         ops.attn_fwd(qs, ks, t["v"], nid, D ** -0.5, True, -1, False)
         ev[1].record()
-        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, mk, nid, D ** -0.5, True, -1, wmean=wm)
+        ops.attn_bwd(t["do"], qs, ks, t["v"], o, st, mk, nid, D ** -0.5, True, -1, wmean=wm, support=sup)
         ev[2].record()
         torch.cuda.synchronize()
         f_ms, b_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
@@ -673,14 +676,14 @@ def bench_model(dev, steps=3, warmup=2, world=1, rank=0):
                 q = torch.randn(1, 16, seq, 128, device=dev, dtype=torch.bfloat16)
                 k = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
                 v = torch.randn(1, 8, seq, 128, device=dev, dtype=torch.bfloat16)
-                o, st, mk, wm = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
-                ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1, wmean=wm)
+                o, st, mk, wm, sup = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1, wmean=wm, support=sup)
                 torch.cuda.synchronize()
                 a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a0.record()
                 for _ in range(28):
-                    o, st, mk, wm = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
-                    ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1, wmean=wm)
+                    o, st, mk, wm, sup = real_fwd(q, k, v, nid, 128 ** -0.5, True, -1, False)
+                    ops.attn_bwd(q, q, k, v, o, st, mk, nid, 128 ** -0.5, True, -1, wmean=wm, support=sup)
                 a1.record()
                 torch.cuda.synchronize()
                 res["attention_ms"] = round(a0.elapsed_time(a1), 2)

@@ -53,6 +53,7 @@ class AttnDesc(ctypes.Structure):
         ("dropout_seed", ctypes.c_void_p),
         ("key_lengths", ctypes.c_void_p),
         ("wmean", HfanTensor),
+        ("support", ctypes.c_void_p),
     ]
 
 
@@ -83,6 +84,7 @@ _P = ctypes.c_void_p
 SIGNATURES = {
     "hfan_attn_fwd": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _T, _T, _T, _T, _P, _P]),
     "hfan_attn_tile_mask_words": (ctypes.c_int64, [ctypes.POINTER(AttnDesc)]),
+    "hfan_attn_support_bytes": (ctypes.c_int64, [ctypes.POINTER(AttnDesc)]),
     "hfan_attn_bwd": (ctypes.c_int, [ctypes.POINTER(AttnDesc), _T, _T, _T, _T, _T, _P, _P, _T, _T, _T, _P]),
     "hfan_paged_fwd": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _P, _P]),
     "hfan_paged_bwd": (ctypes.c_int, [ctypes.POINTER(PagedDesc), _T, _T, _T, _T, _T, _P, _P, _T, _T, _T, _P]),

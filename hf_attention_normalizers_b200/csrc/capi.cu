@@ -127,6 +127,29 @@ int64_t mask_words(const hfan_attn_desc& d) {
   return (int64_t)d.heads_q * d.batch * 2 * ceil_div(d.len_q, 128) * ((tiles + 31) / 32);
 }
 
+// Byte offsets of the support-list arrays inside the caller's workspace
+// (see AttnParams::sl_key); false when the request takes no lists.
+struct SupportLayout {
+  int64_t flag, cnt, ent, g, total;
+};
+
+bool support_layout(const hfan_attn_desc& d, SupportLayout* l) {
+  if (d.normalizer == HFAN_SOFTMAX1 || d.dropout_p != 0.f) return false;
+  if (d.dtype != HFAN_BFLOAT16 && d.dtype != HFAN_FLOAT16) return false;
+  if (d.head_dim != 64 && d.head_dim != 128) return false;
+  const int64_t rows = d.cu_seqlens_q ? (int64_t)d.total_q : (int64_t)d.batch * d.len_q;
+  if (rows <= 0 || d.heads_q <= 0) return false;
+  const int64_t slots = (int64_t)d.heads_q * kSupSlots * rows;
+  const int64_t cnt = (int64_t)d.heads_q * (d.head_dim / 32) * rows;
+  auto up = [](int64_t x) { return (x + 255) & ~int64_t(255); };
+  l->flag = 0;
+  l->cnt = 256;
+  l->ent = l->cnt + up(cnt * 4);
+  l->g = l->ent + up(slots * 8);
+  l->total = l->g + up(slots * 4);
+  return true;
+}
+
 int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   if (desc == nullptr) return fail(HFAN_ERR_INVALID, "null descriptor");
   int rc = check_common(desc->dtype, desc->normalizer, desc->batch, desc->heads_q, desc->heads_kv,
@@ -151,6 +174,18 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
   p.norm = desc->normalizer;
   p.grad_f32 = desc->grad_dtype == HFAN_FLOAT32;
   if (desc->cu_seqlens_q && desc->total_q < 0) return fail(HFAN_ERR_INVALID, "total_q must be >= 0");
+  if (desc->support != nullptr) {
+    SupportLayout l;
+    if (!support_layout(*desc, &l))
+      return fail(HFAN_ERR_INVALID, "support workspace given for a request that takes none (see hfan_attn_support_bytes)");
+    if ((reinterpret_cast<uintptr_t>(desc->support) & 255u) != 0)
+      return fail(HFAN_ERR_INVALID, "support workspace must be 256-byte aligned");
+    uint8_t* w = static_cast<uint8_t*>(desc->support);
+    p.sl_flag = reinterpret_cast<int*>(w + l.flag);
+    p.sl_cnt = reinterpret_cast<int*>(w + l.cnt);
+    p.sl_ent = reinterpret_cast<int2*>(w + l.ent);
+    p.sl_g = reinterpret_cast<float*>(w + l.g);
+  }
   if (desc->wmean.data != nullptr && desc->normalizer != HFAN_SOFTMAX1) {
     const hfan_tensor& w = desc->wmean;
     if ((reinterpret_cast<uintptr_t>(w.data) & 15u) != 0 || w.stride_token % 8 != 0 || w.stride_head % 8 != 0 ||
@@ -255,7 +290,13 @@ int hfan_attn_fwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan
   if (desc->len_q == 0 || desc->len_k == 0 || p.rows_total == 0) return HFAN_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (tc_supported(desc->dtype, p)) {
+  const bool tc = tc_supported(desc->dtype, p);
+  if (p.sl_flag != nullptr) {
+    // lists complete until a sub-list overflows; the general kernels write none
+    e = cudaMemsetAsync(p.sl_flag, tc ? 0 : 1, sizeof(int), s);
+    if (e != cudaSuccess) return cuda_fail(e, "hfan_attn_fwd");
+  }
+  if (tc) {
     e = tc_attention_fwd(desc->dtype, p, desc->len_q, s);
   } else if (p.drop_thr24 != 0u) {
     return fail(HFAN_ERR_UNSUPPORTED, "fused dropout needs 16-bit inputs with head_dim 64 or 128");
@@ -268,6 +309,11 @@ int hfan_attn_fwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan
 }
 
 int64_t hfan_attn_tile_mask_words(const hfan_attn_desc* desc) { return desc ? mask_words(*desc) : 0; }
+
+int64_t hfan_attn_support_bytes(const hfan_attn_desc* desc) {
+  SupportLayout l;
+  return desc && support_layout(*desc, &l) ? l.total : 0;
+}
 
 int hfan_attn_bwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan_tensor v,
                   hfan_tensor o, hfan_tensor d_o, const float* stats, float* corr,

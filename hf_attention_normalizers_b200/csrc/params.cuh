@@ -6,6 +6,8 @@
 
 namespace hfan {
 
+constexpr int kSupSlots = 128;  // support-list slots per query row
+
 struct AttnParams {
   const void* q;
   const void* k;
@@ -58,6 +60,18 @@ struct AttnParams {
   // the tensor-core forward and read by its backward (null: not used).
   void* wm;
   int64_t wm_sb, wm_sh, wm_st;
+  // Sparse normalizers, tensor-core path without dropout: per-row support
+  // lists written by the forward (null: none).  Row r of query head h owns
+  // kSupSlots consecutive slots at [(h * rows_total + r) * kSupSlots]: NWG =
+  // head_dim / 32 sub-lists (one per row warpgroup, keys in increasing order)
+  // of kSupSlots / NWG slots.  sl_ent: {key token (the K/V token index),
+  // float bits of p > 0}; sl_g: the backward's dP, then dS; sl_cnt:
+  // [(h * rows_total + r) * NWG + w] entries of sub-list w; sl_flag: nonzero
+  // when some sub-list overflowed (the backward then runs the tile kernels).
+  int2* sl_ent;
+  float* sl_g;
+  int* sl_cnt;
+  int* sl_flag;
 
   float scale;
   int causal, window_left, norm;

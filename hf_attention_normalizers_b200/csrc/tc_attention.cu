@@ -363,6 +363,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
   const uint32_t tmem_p = tmem + 384;
   const uint32_t tmem_u = tmem + 384;
   const bool want_u = SPARSE && p.wm != nullptr;
+  // per-row support lists for the sparse backward (no dropout)
+  const bool lists = SPARSE && !DROP && p.sl_ent != nullptr;
   constexpr int PCOLS = kBN / Roles<HD>::NWG;  // keys per warpgroup and S tile
   volatile int* abort_flag = &ctl->abort;
 
@@ -927,12 +929,19 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         return vb + tok * p.v_st;
       };
       int m = 0;
+      const int64_t srow = (int64_t)g.q_start + i;  // stats row
       for (int e = 0; e < cd.n; ++e) {
         const float z = cbuf[e * 128 + row];
         if (z > tau_) {
           const uint16_t id = ibuf[e * 128 + row];
           cbuf[m * 128 + row] = z - tau_;
           ibuf[m * 128 + row] = id;
+          if (lists && row_ok && m < kSupSlots / NWG) {
+            const int key = k_lo + (id >> JB) * kBN + wg * COLS + (id & (COLS - 1));
+            const float d = z - tau_, pr = NORM == HFAN_SPARSEMAX ? d : d * d;
+            p.sl_ent[((int64_t)h * p.rows_total + srow) * kSupSlots + wg * (kSupSlots / NWG) + m] =
+                make_int2(varlen ? g.k_start + key : key, __float_as_int(pr));
+          }
           ++m;
           // the four warpgroups read this V row next: bring it into L2 now
           const T* vr = vrow(wg, id);
@@ -945,6 +954,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         }
       }
       xn[wg * 128 + row] = m;
+      if (lists && row_ok) {
+        p.sl_cnt[((int64_t)h * p.rows_total + srow) * NWG + wg] = min(m, kSupSlots / NWG);
+        if (m > kSupSlots / NWG) atomicExch(p.sl_flag, 1);  // the backward runs the tile kernels
+      }
       named_bar_sync(1, NT);
       uint64_t acc[16], accu[16];
 #pragma unroll
@@ -1016,6 +1029,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     long long dg_s = 0, dg_pv = 0;
 #endif
     float wsum = 0.f;  // sparse: sum_j w_j of this warpgroup's keys (U's normaliser)
+    int sl_n = 0;      // entries of this warpgroup's support sub-list
+    const int64_t sl_row = (int64_t)g.q_start + i;
     for (int t = 0; t < (gather ? 0 : n_tiles) && (ok || !SPARSE); ++t) {
       if (ok) DIAG_T(dg_s, ok = load_s(t));
       uint32_t wpk[COLS / 2];  // sparse with U: packed W of this warpgroup's keys
@@ -1085,6 +1100,24 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           sreg[j + 1] = f2_hi(d);
         }
         wsum += f2_lo(ws2) + f2_hi(ws2);
+        if (lists && row_ok) {
+          // this warpgroup's keys with p > 0, in key order, into the row's
+          // sub-list (8-key chunks gate the predicated appends)
+          const int kb = (varlen ? g.k_start : 0) + k_lo + t * kBN + wg * COLS;
+          int2* base = p.sl_ent + ((int64_t)h * p.rows_total + sl_row) * kSupSlots + wg * (kSupSlots / NWG);
+#pragma unroll
+          for (int c = 0; c < COLS / 8; ++c) {
+            if (max_n<8>(sreg + c * 8) > 0.f) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (sreg[c * 8 + e] > 0.f) {
+                  if (sl_n < kSupSlots / NWG) base[sl_n] = make_int2(kb + c * 8 + e, __float_as_int(sreg[c * 8 + e]));
+                  ++sl_n;
+                }
+              }
+            }
+          }
+        }
         if (track) {  // this warp's 32 rows x COLS keys: any p > 0 sets the tile's bit for its 64-row half
           const unsigned bal = __ballot_sync(0xffffffffu, drop ? nzl : max_n<COLS>(sreg) > 0.f);
           const int kt = kt0 + t;
@@ -1151,6 +1184,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       tc_fence_before();
       warp_arrive(&bars->p_full[pb]);
       ++pc;
+    }
+    if (lists && row_ok && !gather) {
+      p.sl_cnt[((int64_t)h * p.rows_total + sl_row) * NWG + wg] = min(sl_n, kSupSlots / NWG);
+      if (sl_n > kSupSlots / NWG) atomicExch(p.sl_flag, 1);
     }
     if (ok && n_tiles > 0 && !gather) {
       // with U: the last tile's P V was committed to the barrier of its S buffer

@@ -15,6 +15,6 @@ def varlen_hopper_softmax1_attention(query: torch.Tensor, key: torch.Tensor, val
     if query.shape[-1] > 256:
         raise ValueError("head_dim larger than 256 is not supported.")
     actual_scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
-    o, _, _, _ = ops.varlen_fwd(query, key, value, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q),
-                          int(max_seqlen_k), N.SOFTMAX1, actual_scale, bool(is_causal))
+    o = ops.varlen_fwd(query, key, value, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q),
+                       int(max_seqlen_k), N.SOFTMAX1, actual_scale, bool(is_causal))[0]
     return o

@@ -18,6 +18,6 @@ def varlen_hopper_sparse_attention(query: torch.Tensor, key: torch.Tensor, value
     if normalizer not in {"sparsemax", "entmax15"}:
         raise ValueError("normalizer must be sparsemax or entmax15.")
     actual_scale = query.shape[-1] ** -0.5 if scale is None else float(scale)
-    o, _, _, _ = ops.varlen_fwd(query, key, value, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q),
-                          int(max_seqlen_k), N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal))
+    o = ops.varlen_fwd(query, key, value, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q),
+                       int(max_seqlen_k), N.NORMALIZER_IDS[normalizer], actual_scale, bool(is_causal))[0]
     return o

@@ -67,7 +67,7 @@ def _ptr(t: Optional[Tensor]) -> ctypes.c_void_p:
 # dense
 # ---------------------------------------------------------------------------
 def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, mask=None,
-                dropout_p=0.0, seed=None, key_lengths=None, wmean=None) -> N.AttnDesc:
+                dropout_p=0.0, seed=None, key_lengths=None, wmean=None, support=None) -> N.AttnDesc:
     b, hq, lq, d = q.shape
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=b, heads_q=hq, heads_kv=k.shape[1],
@@ -77,7 +77,30 @@ def _dense_desc(q, k, normalizer, scale, causal, window_left, grad_dtype=None, m
         tile_mask=_mask_ptr(mask), dropout_p=float(dropout_p),
         dropout_seed=None if (seed is None or dropout_p == 0.0) else seed.data_ptr(),
         key_lengths=None if key_lengths is None else key_lengths.data_ptr(),
-        wmean=_t4(_wm_or_none(wmean)))
+        wmean=_t4(_wm_or_none(wmean)), support=_support_ptr(support))
+
+
+def _support_ptr(support: Optional[Tensor]):
+    return None if support is None or support.numel() == 0 else support.data_ptr()
+
+
+def new_support(q: Tensor, desc: N.AttnDesc) -> Tensor:
+    """Workspace for the forward's per-row support lists (hfan_attn_support_bytes;
+    empty when the request takes none), which let the backward compute dQ
+    from the few keys with p > 0 instead of every key tile."""
+    nbytes = int(N.lib().hfan_attn_support_bytes(ctypes.byref(desc)))
+    return torch.empty((nbytes,), dtype=torch.uint8, device=q.device)
+
+
+def new_dense_support(q: Tensor, k: Tensor, normalizer: int) -> Tensor:
+    """``new_support`` for a dense [B, H, S, D] request without dropout."""
+    return new_support(q, _dense_desc(q, k, normalizer, 1.0, True, -1))
+
+
+def support_overflowed(support: Tensor) -> bool:
+    """True when some row's support list overflowed in the last forward that
+    wrote ``support`` (its backward then ran the tile kernels).  Synchronises."""
+    return support.numel() > 0 and int(support[:4].view(torch.int32).item()) != 0
 
 
 def _wm_or_none(wmean: Optional[Tensor]) -> Optional[Tensor]:
@@ -127,12 +150,13 @@ def _as_bhsd(o: Tensor, out_bshd: bool) -> Tensor:
 def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, causal: bool,
              window_left: int, out_bshd: bool, dropout_p: float = 0.0,
              seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None
-             ) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-    """Returns (o, stats, mask, wmean): stats float32 [2, Hq, B*S] (see hfan.h),
-    the int32 key-tile support mask of the sparse normalizers (empty for
-    softmax1), which the backward uses to skip all-zero tiles, and the sparse
+             ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (o, stats, mask, wmean, support): stats float32 [2, Hq, B*S] (see
+    hfan.h), the int32 key-tile support mask of the sparse normalizers (empty
+    for softmax1), which the backward uses to skip all-zero tiles, the sparse
     normalizers' w-weighted mean of V (``new_wmean``), which gives the backward
-    its row correction without a sweep over the keys.  ``dropout_p > 0`` drops
+    its row correction without a sweep over the keys, and the support-list
+    workspace (``new_support``).  ``dropout_p > 0`` drops
     probabilities with the keep bits generated from the device int64 ``seed``.
     ``key_lengths`` (int32 [B]) gives every sequence its own key count with the
     causal mask aligned at the first key: HF's right-padded batch."""
@@ -147,10 +171,12 @@ def attn_fwd(q: Tensor, k: Tensor, v: Tensor, normalizer: int, scale: float, cau
     wmean = new_wmean(q, normalizer)
     desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed,
                        key_lengths=key_lengths, wmean=wmean)
+    support = new_support(q, desc)
+    desc.support = _support_ptr(support)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(_as_bhsd(o, out_bshd)),
                                       _ptr(stats), _stream(q)), "hfan_attn_fwd")
-    return o, stats, mask, wmean
+    return o, stats, mask, wmean, support
 
 
 @attn_fwd.register_fake
@@ -159,14 +185,15 @@ def _(q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p=0.0, 
     o = _new_out(q, out_bshd)
     return (o, q.new_empty((2, hq, b * lq), dtype=torch.float32),
             q.new_empty((mask_words(normalizer, hq, b, lq, k.shape[2]),), dtype=torch.int32),
-            new_wmean(q, normalizer))
+            new_wmean(q, normalizer),
+            new_support(q, _dense_desc(q, k, normalizer, scale, causal, window_left, dropout_p=dropout_p)))
 
 
 @torch.library.custom_op("hfan::attn_bwd", mutates_args=())
 def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, normalizer: int,
              scale: float, causal: bool, window_left: int, dropout_p: float = 0.0,
              seed: Optional[Tensor] = None, key_lengths: Optional[Tensor] = None,
-             wmean: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+             wmean: Optional[Tensor] = None, support: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
     do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
     dq = torch.empty_like(q, memory_format=torch.contiguous_format)
@@ -179,7 +206,7 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
     b, hq, lq, _ = q.shape
     corr = torch.empty((hq, b * lq), dtype=torch.float32, device=q.device)
     desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, dropout_p=dropout_p, seed=seed,
-                       key_lengths=key_lengths, wmean=wmean)
+                       key_lengths=key_lengths, wmean=wmean, support=support)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
@@ -189,7 +216,7 @@ def attn_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tens
 
 @attn_bwd.register_fake
 def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropout_p=0.0, seed=None,
-      key_lengths=None, wmean=None):
+      key_lengths=None, wmean=None, support=None):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
@@ -197,17 +224,17 @@ def _(do, q, k, v, o, stats, mask, normalizer, scale, causal, window_left, dropo
 
 def _attn_setup(ctx, inputs, output):
     q, k, v, normalizer, scale, causal, window_left, out_bshd, dropout_p, seed, key_lengths = inputs
-    o, stats, mask, wmean = output
-    ctx.save_for_backward(q, k, v, o, stats, mask, seed, key_lengths, wmean)
+    o, stats, mask, wmean, support = output
+    ctx.save_for_backward(q, k, v, o, stats, mask, seed, key_lengths, wmean, support)
     ctx.args = (normalizer, scale, causal, window_left, out_bshd, dropout_p)
-    ctx.mark_non_differentiable(stats, mask, wmean)
+    ctx.mark_non_differentiable(stats, mask, wmean, support)
 
 
-def _attn_backward(ctx, do, dstats, dmask, dwmean):
-    q, k, v, o, stats, mask, seed, key_lengths, wmean = ctx.saved_tensors
+def _attn_backward(ctx, do, dstats, dmask, dwmean, dsupport):
+    q, k, v, o, stats, mask, seed, key_lengths, wmean, support = ctx.saved_tensors
     normalizer, scale, causal, window_left, out_bshd, dropout_p = ctx.args
     dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, mask, normalizer,
-                          scale, causal, window_left, dropout_p, seed, key_lengths, wmean)
+                          scale, causal, window_left, dropout_p, seed, key_lengths, wmean, support)
     return dq, dk, dv, None, None, None, None, None, None, None, None
 
 
@@ -216,14 +243,14 @@ torch.library.register_autograd("hfan::attn_fwd", _attn_backward, setup_context=
 
 def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, normalizer: int, scale: float,
                   causal: bool, window_left: int = -1, mask: Optional[Tensor] = None,
-                  wmean: Optional[Tensor] = None) -> None:
+                  wmean: Optional[Tensor] = None, support: Optional[Tensor] = None) -> None:
     """Forward into caller-owned outputs: ``o`` any [B, Hq, S, D] view with unit
     D stride (for example one rank's slice of a head-major gather buffer), ``stats``
     float32 [2, Hq, B * S], optionally the int32 tile mask (``mask_words`` long)
-    and the sparse normalizers' ``wmean`` (``new_wmean``).
-    No autograd; no allocation."""
+    and the sparse normalizers' ``wmean`` (``new_wmean``) and support-list
+    workspace (``new_support``).  No autograd; no allocation."""
     _require_cuda(q, k, v, o, stats)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, wmean=wmean)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, wmean=wmean, support=support)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _ptr(stats),
                                       _stream(q)), "hfan_attn_fwd")
@@ -231,13 +258,14 @@ def attn_fwd_into(q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, nor
 
 def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, corr: Tensor,
                   dq: Tensor, dk: Tensor, dv: Tensor, normalizer: int, scale: float, causal: bool,
-                  window_left: int = -1, mask: Optional[Tensor] = None, wmean: Optional[Tensor] = None) -> None:
+                  window_left: int = -1, mask: Optional[Tensor] = None, wmean: Optional[Tensor] = None,
+                  support: Optional[Tensor] = None) -> None:
     """Backward into caller-owned gradient views (unit D stride) and a float32
     [Hq, B * S] row-correction buffer (``mask``: the forward's tile mask, or
-    None; ``wmean``: what the forward wrote, or None).  No autograd; no
-    allocation."""
+    None; ``wmean`` and ``support``: what the forward wrote, or None).  No
+    autograd; no allocation."""
     _require_cuda(do, q, k, v, o, dq, dk, dv)
-    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, wmean=wmean)
+    desc = _dense_desc(q, k, normalizer, scale, causal, window_left, mask=mask, wmean=wmean, support=support)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t4(q), _t4(k), _t4(v), _t4(o), _t4(do),
                                       _ptr(stats), _ptr(corr), _t4(dq), _t4(dk), _t4(dv), _stream(q)),
@@ -247,19 +275,26 @@ def attn_bwd_into(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats:
 # ---------------------------------------------------------------------------
 # varlen
 # ---------------------------------------------------------------------------
-def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=None, wmean=None) -> N.AttnDesc:
+def _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=None, wmean=None,
+                 support=None, sizes_only=False) -> N.AttnDesc:
+    """``sizes_only``: a descriptor for the size queries only (fake tensors have
+    no data pointers; the queries test the offsets for null and read nothing)."""
+    if sizes_only:
+        cq = ck = 1
+    else:
+        cq, ck = cu_q.data_ptr(), cu_k.data_ptr()
     return N.AttnDesc(
         dtype=dtype_id(q), normalizer=normalizer, batch=cu_q.numel() - 1, heads_q=q.shape[1],
         heads_kv=k.shape[1], head_dim=q.shape[2], len_q=int(max_q), len_k=int(max_k),
-        total_q=q.shape[0], total_k=k.shape[0], cu_seqlens_q=cu_q.data_ptr(), cu_seqlens_k=cu_k.data_ptr(),
+        total_q=q.shape[0], total_k=k.shape[0], cu_seqlens_q=cq, cu_seqlens_k=ck,
         scale=float(scale), causal=int(bool(causal)), window_left=0, grad_dtype=dtype_id(q),
-        tile_mask=_mask_ptr(mask), wmean=_t3(_wm_or_none(wmean)))
+        tile_mask=_mask_ptr(mask), wmean=_t3(_wm_or_none(wmean)), support=_support_ptr(support))
 
 
 @torch.library.custom_op("hfan::varlen_fwd", mutates_args=())
 def varlen_fwd(q: Tensor, k: Tensor, v: Tensor, cu_q: Tensor, cu_k: Tensor, max_q: int, max_k: int,
-               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-    """Returns (o, stats, mask, wmean) as ``attn_fwd`` does, over packed rows."""
+               normalizer: int, scale: float, causal: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (o, stats, mask, wmean, support) as ``attn_fwd`` does, over packed rows."""
     _require_cuda(q, k, v, cu_q, cu_k)
     q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
     cu_q = cu_q.to(torch.int32).contiguous()
@@ -269,10 +304,12 @@ def varlen_fwd(q: Tensor, k: Tensor, v: Tensor, cu_q: Tensor, cu_k: Tensor, max_
     mask = _new_mask(q.device, normalizer, q.shape[1], cu_q.numel() - 1, int(max_q), int(max_k))
     wmean = new_wmean(q, normalizer)
     desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask, wmean=wmean)
+    support = new_support(q, desc)
+    desc.support = _support_ptr(support)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_fwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _ptr(stats),
                                       _stream(q)), "hfan_attn_fwd(varlen)")
-    return o, stats, mask, wmean
+    return o, stats, mask, wmean, support
 
 
 @varlen_fwd.register_fake
@@ -281,13 +318,15 @@ def _(q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal):
             q.new_empty((2, q.shape[1], q.shape[0]), dtype=torch.float32),
             q.new_empty((mask_words(normalizer, q.shape[1], cu_q.shape[0] - 1, int(max_q), int(max_k)),),
                         dtype=torch.int32),
-            new_wmean(q, normalizer))
+            new_wmean(q, normalizer),
+            new_support(q, _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, sizes_only=True)))
 
 
 @torch.library.custom_op("hfan::varlen_bwd", mutates_args=())
 def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Tensor, mask: Tensor, cu_q: Tensor,
                cu_k: Tensor, max_q: int, max_k: int, normalizer: int, scale: float,
-               causal: bool, wmean: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
+               causal: bool, wmean: Optional[Tensor] = None,
+               support: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     _require_cuda(do, q, k, v, o)
     do, q, k, v, o = (_inner_contig(t) for t in (do, q, k, v, o))
     cu_q = cu_q.to(torch.int32).contiguous()
@@ -296,7 +335,8 @@ def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Te
     dk = torch.zeros_like(k, memory_format=torch.contiguous_format)
     dv = torch.zeros_like(v, memory_format=torch.contiguous_format)
     corr = torch.empty((q.shape[1], q.shape[0]), dtype=torch.float32, device=q.device)
-    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask, wmean=wmean)
+    desc = _varlen_desc(q, k, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, mask=mask, wmean=wmean,
+                        support=support)
     with torch.cuda.device(q.device):
         N.check(N.lib().hfan_attn_bwd(ctypes.byref(desc), _t3(q), _t3(k), _t3(v), _t3(o), _t3(do),
                                       _ptr(stats), _ptr(corr), _t3(dq), _t3(dk), _t3(dv), _stream(q)),
@@ -305,7 +345,7 @@ def varlen_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, stats: Te
 
 
 @varlen_bwd.register_fake
-def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, wmean=None):
+def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal, wmean=None, support=None):
     return (torch.empty_like(q, memory_format=torch.contiguous_format),
             torch.empty_like(k, memory_format=torch.contiguous_format),
             torch.empty_like(v, memory_format=torch.contiguous_format))
@@ -313,17 +353,17 @@ def _(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, 
 
 def _varlen_setup(ctx, inputs, output):
     q, k, v, cu_q, cu_k, max_q, max_k, normalizer, scale, causal = inputs
-    o, stats, mask, wmean = output
-    ctx.save_for_backward(q, k, v, o, stats, mask, cu_q, cu_k, wmean)
+    o, stats, mask, wmean, support = output
+    ctx.save_for_backward(q, k, v, o, stats, mask, cu_q, cu_k, wmean, support)
     ctx.args = (max_q, max_k, normalizer, scale, causal)
-    ctx.mark_non_differentiable(stats, mask, wmean)
+    ctx.mark_non_differentiable(stats, mask, wmean, support)
 
 
-def _varlen_backward(ctx, do, dstats, dmask, dwmean):
-    q, k, v, o, stats, mask, cu_q, cu_k, wmean = ctx.saved_tensors
+def _varlen_backward(ctx, do, dstats, dmask, dwmean, dsupport):
+    q, k, v, o, stats, mask, cu_q, cu_k, wmean, support = ctx.saved_tensors
     max_q, max_k, normalizer, scale, causal = ctx.args
     dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal,
-                            wmean)
+                            wmean, support)
     return dq, dk, dv, None, None, None, None, None, None, None
 
 

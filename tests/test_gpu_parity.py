@@ -116,7 +116,7 @@ def test_sliding_window_matches_oracle(norm):
 def test_sparse_threshold_matches_oracle_fp32(norm):
     """The saved tau equals the oracle's sort-based tau (zero-pattern check)."""
     q, k, v, _ = _inputs((1, 2, 96, 64), (1, 2, 96, 64), torch.float32, seed=11)
-    o, stats, _, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], 64 ** -0.5, True, -1, False)
+    o, stats, _, _, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], 64 ** -0.5, True, -1, False)
     _, p, s = oracle.attention_forward(_np(q), _np(k), _np(v), norm, causal=True, return_probs=True)
     half = 1.0 if norm == "sparsemax" else 0.5
     with np.errstate(all="ignore"):

@@ -68,7 +68,7 @@ def check_threshold(norm, tau_k, support_k, q, k, scale, what, near=NEAR):
 
 
 def _stats(norm, q, k, v, scale):
-    _, st, _, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], scale, True, -1, False)
+    _, st, _, _, _ = ops.attn_fwd(q, k, v, N.NORMALIZER_IDS[norm], scale, True, -1, False)
     b, hq, lq, _ = q.shape  # stats [2][Hq][B * Lq]
     return st.reshape(2, hq, b, lq).transpose(1, 2).double().cpu().numpy()
 
@@ -209,7 +209,7 @@ def test_zero_tiles_skipped_and_results_unchanged(norm):
     v = torch.randn(b, h, s, d, generator=gen).to(torch.bfloat16).cuda()
     do = torch.randn(b, h, s, d, generator=gen).to(torch.bfloat16).cuda()
     nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
-    o, st, mk, wm = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    o, st, mk, wm, sup = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
     frac = ops.tile_mask_skipped_fraction(mk, h, b, s, s)
     print(f"{norm}: skipped tile fraction {frac:.3f}")
     assert frac > 0.5
@@ -240,7 +240,7 @@ def test_saved_wmean_matches_oracle_and_two_pass_backward(norm, d, dtype):
     b, hq, hkv, s = 1, 8, 2, 1024
     q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=11)
     nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
-    o, st, mk, wm = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    o, st, mk, wm, sup = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
     assert wm.shape == q.shape
     _, p, _ = oracle.attention_forward(_np(q), _np(k), _np(v), norm, scale=scale, causal=True, return_probs=True)
     w = (p > 0).astype(np.float64) if norm == "sparsemax" else np.sqrt(p)
@@ -258,3 +258,35 @@ def test_saved_wmean_matches_oracle_and_two_pass_backward(norm, d, dtype):
     for name, a, e in zip(("corr", "dq", "dk", "dv"), grads["one sweep"], grads["two sweeps"]):
         err = float((a.float() - e.float()).abs().max())
         assert err <= 1e-2 * float(e.float().abs().max()) + 1e-5, f"{name}: max err {err:.3e}"
+
+
+@pytest.mark.parametrize("norm", SPARSE)
+@pytest.mark.parametrize("d,dtype", [(128, torch.bfloat16), (64, torch.float16)])
+def test_support_list_backward_matches_tile_backward(norm, d, dtype):
+    """The forward's support lists (every row's keys with p > 0) drive a dQ
+    kernel that touches only those keys; it must agree with the tile kernels
+    that recompute every tile, and its gradients with the oracle.  On N(0, 1)
+    scores no list overflows; on the pre-scaled wide-support case the lists
+    overflow and the backward falls back to the tile kernels (checked against
+    the oracle by the wide-support tests)."""
+    b, hq, hkv, s = 1, 8, 2, 1024
+    q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=13)
+    nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
+    o, st, mk, wm, sup = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    assert sup.numel() > 0 and not ops.support_overflowed(sup)
+    grads = {}
+    for label, support in (("lists", sup), ("tiles", None)):
+        corr = torch.empty((hq, b * s), dtype=torch.float32, device="cuda")
+        g = [torch.empty_like(x) for x in (q, k, v)]
+        ops.attn_bwd_into(do, q, k, v, o, st, corr, *g, nid, scale, True, mask=mk, wmean=wm, support=support)
+        grads[label] = (corr, *g)
+    torch.cuda.synchronize()
+    for name, a, e in zip(("corr", "dq", "dk", "dv"), grads["lists"], grads["tiles"]):
+        err = float((a.float() - e.float()).abs().max())
+        assert err <= 1e-2 * float(e.float().abs().max()) + 1e-5, f"{name}: max err {err:.3e}"
+    ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), norm, scale=scale, causal=True)
+    for name, a, e in zip(("dq", "dk", "dv"), grads["lists"][1:], ref[1:]):
+        assert_close(a, e, dtype, f"lists/{name}")
+    qs, ks = q * d ** -0.25, k * d ** -0.25
+    _, _, _, _, wide = ops.attn_fwd(qs, ks, v, nid, scale, True, -1, False)
+    assert ops.support_overflowed(wide)
