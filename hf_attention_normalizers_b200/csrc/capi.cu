@@ -128,25 +128,36 @@ int64_t mask_words(const hfan_attn_desc& d) {
 }
 
 // Byte offsets of the support-list arrays inside the caller's workspace
-// (see AttnParams::sl_key); false when the request takes no lists.
+// (see AttnParams::sl_ent); false when the request takes no lists.
 struct SupportLayout {
-  int64_t flag, cnt, ent, g, total;
+  int64_t flag, cnt, ent, g, kcnt, koff, bsum, tr, nk, total;
 };
 
 bool support_layout(const hfan_attn_desc& d, SupportLayout* l) {
-  if (d.normalizer == HFAN_SOFTMAX1 || d.dropout_p != 0.f) return false;
+  // sparsemax only: entmax15's supports (about 22 keys per row on N(0, 1)
+  // scores at 8192 keys, against sparsemax's 4.4) make the per-entry gathers
+  // cost as much as the tile kernels, and recording them in its forward (which
+  // has no key indices in its candidate buffers) costs more than they save.
+  if (d.normalizer != HFAN_SPARSEMAX || d.dropout_p != 0.f) return false;
   if (d.dtype != HFAN_BFLOAT16 && d.dtype != HFAN_FLOAT16) return false;
   if (d.head_dim != 64 && d.head_dim != 128) return false;
   const int64_t rows = d.cu_seqlens_q ? (int64_t)d.total_q : (int64_t)d.batch * d.len_q;
   if (rows <= 0 || d.heads_q <= 0) return false;
   const int64_t slots = (int64_t)d.heads_q * kSupSlots * rows;
   const int64_t cnt = (int64_t)d.heads_q * (d.head_dim / 32) * rows;
+  if (slots >= (int64_t)1 << 31) return false;  // slot numbers are int32
+  l->nk = (int64_t)d.heads_kv * (d.cu_seqlens_q ? (int64_t)d.total_k : (int64_t)d.batch * d.len_k);
+  if (l->nk <= 0) return false;
   auto up = [](int64_t x) { return (x + 255) & ~int64_t(255); };
   l->flag = 0;
   l->cnt = 256;
   l->ent = l->cnt + up(cnt * 4);
   l->g = l->ent + up(slots * 8);
-  l->total = l->g + up(slots * 4);
+  l->kcnt = l->g + up(slots * 4);
+  l->koff = l->kcnt + up(l->nk * 4);
+  l->bsum = l->koff + up((l->nk + 1) * 4);
+  l->tr = l->bsum + up(sparse_key_blocks(l->nk) * 4);
+  l->total = l->tr + up(slots * 4);
   return true;
 }
 
@@ -185,6 +196,11 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
     p.sl_cnt = reinterpret_cast<int*>(w + l.cnt);
     p.sl_ent = reinterpret_cast<int2*>(w + l.ent);
     p.sl_g = reinterpret_cast<float*>(w + l.g);
+    p.sl_kcnt = reinterpret_cast<int*>(w + l.kcnt);
+    p.sl_koff = reinterpret_cast<int*>(w + l.koff);
+    p.sl_bsum = reinterpret_cast<int*>(w + l.bsum);
+    p.sl_tr = reinterpret_cast<int*>(w + l.tr);
+    p.sl_nk = l.nk;
   }
   if (desc->wmean.data != nullptr && desc->normalizer != HFAN_SOFTMAX1) {
     const hfan_tensor& w = desc->wmean;

@@ -7,6 +7,16 @@
 namespace hfan {
 
 constexpr int kSupSlots = 128;  // support-list slots per query row
+constexpr int kKeyScanBlock = 4096;  // key counters per block of the key-offset prefix kernels
+
+constexpr int kKeyMaxEntries = 1024;  // longest key segment the list dK/dV kernel sorts
+// sl_flag bits: a row's support list overflowed in the forward (the backward
+// runs both tile kernels), or a key's segment exceeds kKeyMaxEntries (the
+// tile dK/dV kernel runs; dQ still comes from the lists).
+constexpr int kListRowOverflow = 1;
+constexpr int kListKeyOverflow = 2;
+
+inline int64_t sparse_key_blocks(int64_t nk) { return (nk + kKeyScanBlock - 1) / kKeyScanBlock; }
 
 struct AttnParams {
   const void* q;
@@ -72,12 +82,28 @@ struct AttnParams {
   float* sl_g;
   int* sl_cnt;
   int* sl_flag;
+  // The same entries transposed to the key side for dK/dV: key id kid =
+  // (b * hkv + kvh) * len_k + token (dense) or kvh * rows_k + token (varlen),
+  // sl_nk ids.  sl_kcnt: entries per key (then the fill cursor); sl_koff:
+  // [sl_nk + 1] exclusive prefix; sl_bsum: per-block sums of the prefix
+  // kernels; sl_tr: slot numbers grouped by key, sorted within each key.
+  int* sl_kcnt;
+  int* sl_koff;
+  int* sl_bsum;
+  int* sl_tr;
+  int64_t sl_nk;
 
   float scale;
   int causal, window_left, norm;
   int grad_f32;          // dq/dk/dv element type is float32 (else the input type)
   int* dev_status;       // first device-side error, see DeviceError
 };
+
+// Key id of a support-list entry (see AttnParams::sl_kcnt): key is the K/V
+// token the forward stored, b the sequence of the row (0 for varlen).
+__device__ __forceinline__ int64_t list_kid(const AttnParams& p, int b, int kvh, int key) {
+  return p.cu_k != nullptr ? (int64_t)kvh * p.rows_k + key : ((int64_t)b * p.hkv + kvh) * p.len_k + key;
+}
 
 // Key count of sequence b in the paged and lens_only layouts, clamped to the
 // declared maximum len_k: a larger entry would index past the sequence's

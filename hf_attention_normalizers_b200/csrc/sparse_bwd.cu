@@ -4,7 +4,7 @@
 // tile and apply dS = w (dP - c) to all of it, although w is zero outside the
 // support: on random scores sparsemax keeps about 5 keys of a 4096-key row
 // and entmax15 about 25.  When the forward wrote every row's support list
-// (keys with p > 0, see AttnParams::sl_key), dQ only needs those keys:
+// (keys with p > 0, see AttnParams::sl_ent), dQ only needs those keys:
 //
 //   dP_j = dO . v_j                        for j in the support
 //   c    = sum_j w_j dP_j / sum_j w_j      (w = 1 for sparsemax, sqrt(p) for entmax15)
@@ -20,6 +20,8 @@
 // run instead.
 #include "common.cuh"
 #include "params.cuh"
+
+#include <climits>
 
 namespace hfan {
 namespace {
@@ -54,7 +56,7 @@ constexpr int kRowsPerBlock = 64;  // 256 threads: 64 rows x 4 lanes
 
 template <int HD, bool BF16, int NORM>
 __global__ void __launch_bounds__(256) sparse_dq_kernel(const AttnParams p) {
-  if (*p.sl_flag != 0) return;  // a list overflowed: the tile kernels run
+  if (*p.sl_flag & kListRowOverflow) return;  // a row list overflowed: the tile kernels run
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr int NWG = HD / 32;          // sub-lists per row
   constexpr int LW = kSupSlots / NWG;   // slots per sub-list
@@ -146,7 +148,10 @@ __global__ void __launch_bounds__(256) sparse_dq_kernel(const AttnParams p) {
         for (int x = 0; x < 8; ++x) acc[v * 8 + x] = fmaf(ds, f[x], acc[v * 8 + x]);
       }
       __syncwarp(qmask);  // every lane has read dP before lane 0 replaces it
-      if (q == 0) p.sl_g[slot] = ds;
+      if (q == 0) {
+        p.sl_g[slot] = ds;
+        atomicAdd(p.sl_kcnt + list_kid(p, b, kvh, key), 1);  // the key side's entry count
+      }
     }
   }
   uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.dq) + (int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh +
@@ -163,24 +168,246 @@ __global__ void __launch_bounds__(256) sparse_dq_kernel(const AttnParams p) {
   if (q == 0) p.corr[(int64_t)h * p.rows_total + r] = c;
 }
 
+// ---- key side: dK_j = scale sum_i dS_ij q_i and dV_j = sum_i p_ij dO_i over
+// the rows i whose lists hold key j.  The entries are counted per key by the
+// dQ kernel, offset by a two-kernel prefix over the key counters, scattered
+// into key order by key_fill_kernel and sorted by slot number within each key
+// (slot order is (query head, row) order), so every dK/dV sum runs in the
+// same order on every run.
+
+// Sum of each kKeyScanBlock block of key counters.
+__global__ void __launch_bounds__(256) key_block_sum_kernel(const AttnParams p) {
+  if (*p.sl_flag != 0) return;
+  __shared__ int part[8];
+  const int64_t base = (int64_t)blockIdx.x * kKeyScanBlock;
+  int sum = 0;
+  for (int i = threadIdx.x; i < kKeyScanBlock; i += 256) {
+    const int64_t k = base + i;
+    sum += k < p.sl_nk ? p.sl_kcnt[k] : 0;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < 8; ++w) t += part[w];
+    p.sl_bsum[blockIdx.x] = t;
+  }
+}
+
+// Exclusive prefix of the key counters into sl_koff (and the fill cursors in
+// sl_kcnt); a key with more than kKeyMaxEntries entries sets kListKeyOverflow.
+__global__ void __launch_bounds__(256) key_scan_kernel(const AttnParams p) {
+  if (*p.sl_flag != 0) return;
+  constexpr int PER = kKeyScanBlock / 256;  // consecutive counters per thread
+  __shared__ int wsum[8];
+  __shared__ int carry;
+  if (threadIdx.x < 32) {  // the sums of all earlier blocks
+    int c = 0;
+    for (int j = threadIdx.x; j < (int)blockIdx.x; j += 32) c += p.sl_bsum[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (threadIdx.x == 0) carry = c;
+  }
+  const int64_t base = (int64_t)blockIdx.x * kKeyScanBlock + threadIdx.x * PER;
+  int v[PER];
+  int tsum = 0;
+  bool longk = false;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    v[e] = base + e < p.sl_nk ? p.sl_kcnt[base + e] : 0;
+    longk |= v[e] > kKeyMaxEntries;
+    tsum += v[e];
+  }
+  if (longk) atomicOr(p.sl_flag, kListKeyOverflow);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = tsum;  // inclusive warp scan of the thread sums
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  int off = carry + incl - tsum;
+  for (int w = 0; w < warp; ++w) off += wsum[w];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    if (base + e < p.sl_nk) {
+      p.sl_koff[base + e] = off;
+      p.sl_kcnt[base + e] = off;
+    }
+    off += v[e];
+  }
+  if (base + PER >= p.sl_nk && base < p.sl_nk) p.sl_koff[p.sl_nk] = off;  // the thread holding the last key
+}
+
+// Scatter the slot numbers of every sub-list into their keys' segments.
+template <int HD>
+__global__ void __launch_bounds__(256) key_fill_kernel(const AttnParams p) {
+  if (*p.sl_flag != 0) return;
+  constexpr int NWG = HD / 32;
+  constexpr int LW = kSupSlots / NWG;
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // (h, r, w)
+  if (idx >= (int64_t)p.hq * p.rows_total * NWG) return;
+  const int w = (int)(idx % NWG);
+  const int64_t hr = idx / NWG;
+  const int h = (int)(hr / p.rows_total);
+  const int r = (int)(hr - (int64_t)h * p.rows_total);
+  const int kvh = h / (p.hq / p.hkv);
+  const int b = p.cu_q != nullptr ? 0 : r / p.len_q;
+  const int n = p.sl_cnt[idx];
+  const int slot0 = (int)(hr * kSupSlots + w * LW);
+  for (int e = 0; e < n; ++e) {
+    const int key = p.sl_ent[slot0 + e].x;
+    const int pos = atomicAdd(p.sl_kcnt + list_kid(p, b, kvh, key), 1);
+    p.sl_tr[pos] = slot0 + e;
+  }
+}
+
+// One warp per key: sort the key's slots, then four groups of eight lanes take
+// every fourth entry (each lane HD / 8 columns), and the groups' sums are
+// combined in a fixed order.
 template <int HD, bool BF16>
-cudaError_t launch_dq(const AttnParams& p, cudaStream_t s) {
+__global__ void __launch_bounds__(256) key_dkdv_kernel(const AttnParams p) {
+  if (*p.sl_flag != 0) return;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int DL = HD / 8;  // columns per lane
+  constexpr int NV = DL / 8;  // 16-byte vectors per lane and row
+  __shared__ int sbuf[8][kKeyMaxEntries];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t kid = (int64_t)blockIdx.x * 8 + warp;
+  if (kid >= p.sl_nk) return;
+  const bool varlen = p.cu_k != nullptr;
+  const int64_t lk = varlen ? p.rows_k : p.len_k;
+  const int64_t tok = kid % lk;
+  const int kvh = (int)((kid / lk) % p.hkv);
+  const int b = varlen ? 0 : (int)(kid / lk / p.hkv);
+  const int off = p.sl_koff[kid];
+  const int n = p.sl_koff[kid + 1] - off;
+  int* seg = p.sl_tr + off;
+
+  // sort the segment by slot number
+  if (n > 1 && n <= 32) {
+    int x = lane < n ? seg[lane] : INT_MAX;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        const int y = __shfl_xor_sync(0xffffffffu, x, j);
+        const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+        x = (lower == up) ? min(x, y) : max(x, y);
+      }
+    }
+    if (lane < n) seg[lane] = x;
+    __syncwarp();
+  } else if (n > 32) {
+    int* a = sbuf[warp];
+    for (int e = lane; e < n; e += 32) a[e] = seg[e];
+    __syncwarp();
+    for (int e = lane; e < n; e += 32) {
+      const int x = a[e];
+      int rank = 0;
+      for (int f = 0; f < n; ++f) rank += a[f] < x ? 1 : 0;
+      seg[rank] = x;
+    }
+    __syncwarp();
+  }
+
+  const int grp = lane >> 3, c0 = (lane & 7) * DL;
+  float dk[DL], dv[DL];
+#pragma unroll
+  for (int x = 0; x < DL; ++x) dk[x] = dv[x] = 0.f;
+  auto row_ptr = [&](int slot, const void* base, int64_t sb, int64_t sh, int64_t st) -> const uint4* {
+    const int64_t hr = slot / kSupSlots;
+    const int h = (int)(hr / p.rows_total);
+    const int r = (int)(hr - (int64_t)h * p.rows_total);
+    const int rb = varlen ? 0 : r / p.len_q;
+    const int64_t tq = varlen ? r : r % p.len_q;
+    return reinterpret_cast<const uint4*>(static_cast<const T*>(base) + (int64_t)rb * sb + (int64_t)h * sh +
+                                          tq * st + c0);
+  };
+  for (int e = grp; e < n; e += 4) {
+    const int slot = seg[e];
+    const float pv = __int_as_float(p.sl_ent[slot].y);
+    const float ds = p.sl_g[slot];
+    const uint4* qp = row_ptr(slot, p.q, p.q_sb, p.q_sh, p.q_st);
+    const uint4* dp = row_ptr(slot, p.dout, p.do_sb, p.do_sh, p.do_st);
+    uint4 qv[NV], dv4[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      qv[v] = __ldg(qp + v);
+      dv4[v] = __ldg(dp + v);
+    }
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      float f[8], g[8];
+      unpack8<BF16>(qv[v], f);
+      unpack8<BF16>(dv4[v], g);
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        dk[v * 8 + x] = fmaf(ds, f[x], dk[v * 8 + x]);
+        dv[v * 8 + x] = fmaf(pv, g[x], dv[v * 8 + x]);
+      }
+    }
+  }
+  // groups 0+1 and 2+3, then the two halves
+#pragma unroll
+  for (int x = 0; x < DL; ++x) {
+    dk[x] += __shfl_xor_sync(0xffffffffu, dk[x], 8);
+    dv[x] += __shfl_xor_sync(0xffffffffu, dv[x], 8);
+    dk[x] += __shfl_xor_sync(0xffffffffu, dk[x], 16);
+    dv[x] += __shfl_xor_sync(0xffffffffu, dv[x], 16);
+  }
+  if (grp != 0) return;
+  const int64_t ko = varlen ? 0 : (int64_t)b;
+  uint4* kd = reinterpret_cast<uint4*>(static_cast<T*>(p.dk) + ko * p.dk_sb + (int64_t)kvh * p.dk_sh + tok * p.dk_st + c0);
+  uint4* vd = reinterpret_cast<uint4*>(static_cast<T*>(p.dv) + ko * p.dv_sb + (int64_t)kvh * p.dv_sh + tok * p.dv_st + c0);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    uint4 a, c;
+    a.x = pack_pair<BF16>(dk[v * 8 + 0] * p.scale, dk[v * 8 + 1] * p.scale);
+    a.y = pack_pair<BF16>(dk[v * 8 + 2] * p.scale, dk[v * 8 + 3] * p.scale);
+    a.z = pack_pair<BF16>(dk[v * 8 + 4] * p.scale, dk[v * 8 + 5] * p.scale);
+    a.w = pack_pair<BF16>(dk[v * 8 + 6] * p.scale, dk[v * 8 + 7] * p.scale);
+    c.x = pack_pair<BF16>(dv[v * 8 + 0], dv[v * 8 + 1]);
+    c.y = pack_pair<BF16>(dv[v * 8 + 2], dv[v * 8 + 3]);
+    c.z = pack_pair<BF16>(dv[v * 8 + 4], dv[v * 8 + 5]);
+    c.w = pack_pair<BF16>(dv[v * 8 + 6], dv[v * 8 + 7]);
+    kd[v] = a;
+    vd[v] = c;
+  }
+}
+
+template <int HD, bool BF16>
+cudaError_t launch_list_bwd(const AttnParams& p, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(p.sl_kcnt, 0, (size_t)p.sl_nk * sizeof(int), s);
+  if (e != cudaSuccess) return e;
   const dim3 grid((p.rows_total + kRowsPerBlock - 1) / kRowsPerBlock, p.hq);
   if (p.norm == HFAN_SPARSEMAX)
     sparse_dq_kernel<HD, BF16, HFAN_SPARSEMAX><<<grid, 256, 0, s>>>(p);
   else
     sparse_dq_kernel<HD, BF16, HFAN_ENTMAX15><<<grid, 256, 0, s>>>(p);
+  const unsigned nb = (unsigned)sparse_key_blocks(p.sl_nk);
+  key_block_sum_kernel<<<nb, 256, 0, s>>>(p);
+  key_scan_kernel<<<nb, 256, 0, s>>>(p);
+  const int64_t subs = (int64_t)p.hq * p.rows_total * (HD / 32);
+  key_fill_kernel<HD><<<(unsigned)((subs + 255) / 256), 256, 0, s>>>(p);
+  key_dkdv_kernel<HD, BF16><<<(unsigned)((p.sl_nk + 7) / 8), 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-// dQ and the row correction from the support lists (no-op on the device when
-// a list overflowed).  16-bit inputs and gradients, head_dim 64 or 128.
-cudaError_t sparse_list_dq(int dtype, const AttnParams& p, cudaStream_t s) {
+// dQ, the row correction, dK and dV from the support lists.  Every kernel
+// reads the overflow flags on the device and returns at once when its tile
+// counterpart has to run instead.  16-bit inputs and gradients, head_dim 64
+// or 128.
+cudaError_t sparse_list_bwd(int dtype, const AttnParams& p, cudaStream_t s) {
   const bool bf16 = dtype == HFAN_BFLOAT16;
-  if (p.d == 128) return bf16 ? launch_dq<128, true>(p, s) : launch_dq<128, false>(p, s);
-  return bf16 ? launch_dq<64, true>(p, s) : launch_dq<64, false>(p, s);
+  if (p.d == 128) return bf16 ? launch_list_bwd<128, true>(p, s) : launch_list_bwd<128, false>(p, s);
+  return bf16 ? launch_list_bwd<64, true>(p, s) : launch_list_bwd<64, false>(p, s);
 }
 
 }  // namespace hfan

@@ -36,7 +36,7 @@
 
 namespace hfan {
 
-cudaError_t sparse_list_dq(int dtype, const AttnParams& p, cudaStream_t s);  // sparse_bwd.cu
+cudaError_t sparse_list_bwd(int dtype, const AttnParams& p, cudaStream_t s);  // sparse_bwd.cu
 
 namespace {
 
@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const AttnParams p) {
-  // the support lists are complete: sparse_list_dq computed dQ and c
-  if (NORM != HFAN_SOFTMAX1 && p.sl_flag != nullptr && *p.sl_flag == 0) return;
+  // the support lists are complete: sparse_list_bwd computed dQ and c
+  if (NORM != HFAN_SOFTMAX1 && p.sl_flag != nullptr && (*p.sl_flag & kListRowOverflow) == 0) return;
   using L = QLayout<HD>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr int NH = L::NH;
@@ -601,6 +601,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const AttnParams p) {
+  // the support lists are complete and every key segment was short enough:
+  // sparse_list_bwd computed dK and dV
+  if (NORM != HFAN_SOFTMAX1 && p.sl_flag != nullptr && *p.sl_flag == 0) return;
   using L = KLayout<HD>;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr int NH = L::NH;
@@ -1034,9 +1037,9 @@ cudaError_t launch_bwd_t(const AttnParams& p, int max_q, int max_k, cudaStream_t
                     Roles<HD, 2>::THREADS, KLayout<HD>::TOTAL, s, mq64, mdo64, mk, mv, pk);
   }
   cudaError_t e = cudaSuccess;
-  // Support lists from the forward: the list kernel computes dQ and c, and
-  // the tile dQ kernel returns at once (both read the overflow flag).
-  if (NORM != HFAN_SOFTMAX1 && p.sl_ent != nullptr) e = sparse_list_dq(BF16 ? HFAN_BFLOAT16 : HFAN_FLOAT16, p, s);
+  // Support lists from the forward: the list kernels compute dQ, c, dK and
+  // dV, and the tile kernels return at once (all read the overflow flags).
+  if (NORM != HFAN_SOFTMAX1 && p.sl_ent != nullptr) e = sparse_list_bwd(BF16 ? HFAN_BFLOAT16 : HFAN_FLOAT16, p, s);
   if (e != cudaSuccess) return e;
   e = launch_k(tc_bwd_dq_kernel<HD, BF16, NORM, false>, dim3((max_q + kBM - 1) / kBM, p.hq, p.batch),
                Roles<HD, 2>::THREADS, QLayout<HD>::TOTAL, s, mq, mdo, mk, mv, pq);

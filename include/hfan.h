@@ -114,14 +114,16 @@ typedef struct hfan_attn_desc {
                         /* over the keys.  data = NULL: not produced / not used.  No   */
                         /* counterpart in the reference (its backward sweeps twice,    */
                         /* kernels/sparse_entmax_hopper.py:230-300).                   */
-  void* support;        /* sparsemax/entmax15 without dropout, 16-bit inputs, head_dim */
+  void* support;        /* sparsemax without dropout, 16-bit inputs, head_dim          */
                         /* 64/128: device workspace of hfan_attn_support_bytes(desc)   */
                         /* bytes (256-byte aligned), or NULL.  hfan_attn_fwd writes    */
                         /* every row's support list into it (the keys with p > 0, up  */
                         /* to 128 per row); hfan_attn_bwd given the same workspace    */
-                        /* computes dQ and the row correction from the lists instead  */
-                        /* of sweeping every key tile, and falls back to the tile     */
-                        /* kernels when a list overflowed.  No counterpart in the     */
+                        /* computes dQ, the row correction, dK and dV from the lists  */
+                        /* (transposed to the keys) instead of sweeping every key     */
+                        /* tile, and falls back to the tile kernels when a list       */
+                        /* overflowed or a key has more than 1024 entries.  Results   */
+                        /* are the same on every run.  No counterpart in the          */
                         /* reference (its backward recomputes every tile,             */
                         /* kernels/sparse_entmax_hopper.py:230-319).                   */
 } hfan_attn_desc;
@@ -151,8 +153,8 @@ int hfan_attn_fwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan
 int64_t hfan_attn_tile_mask_words(const hfan_attn_desc* desc);
 
 /* Bytes of the support-list workspace for desc (see hfan_attn_desc.support), or
- * 0 when the request takes none (softmax1, dropout, fp32 inputs, other head
- * dims).  No counterpart in the reference. */
+ * 0 when the request takes none (softmax1, entmax15, dropout, fp32 inputs,
+ * other head dims).  No counterpart in the reference. */
 int64_t hfan_attn_support_bytes(const hfan_attn_desc* desc);
 
 int hfan_attn_bwd(const hfan_attn_desc* desc, hfan_tensor q, hfan_tensor k, hfan_tensor v,

@@ -260,33 +260,74 @@ def test_saved_wmean_matches_oracle_and_two_pass_backward(norm, d, dtype):
         assert err <= 1e-2 * float(e.float().abs().max()) + 1e-5, f"{name}: max err {err:.3e}"
 
 
-@pytest.mark.parametrize("norm", SPARSE)
-@pytest.mark.parametrize("d,dtype", [(128, torch.bfloat16), (64, torch.float16)])
-def test_support_list_backward_matches_tile_backward(norm, d, dtype):
-    """The forward's support lists (every row's keys with p > 0) drive a dQ
-    kernel that touches only those keys; it must agree with the tile kernels
-    that recompute every tile, and its gradients with the oracle.  On N(0, 1)
-    scores no list overflows; on the pre-scaled wide-support case the lists
-    overflow and the backward falls back to the tile kernels (checked against
-    the oracle by the wide-support tests)."""
-    b, hq, hkv, s = 1, 8, 2, 1024
-    q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=13)
-    nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
-    o, st, mk, wm, sup = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
-    assert sup.numel() > 0 and not ops.support_overflowed(sup)
+def _list_and_tile_grads(q, k, v, do, nid, scale, sup, o, st, mk, wm):
+    b, hq, s, _ = q.shape
     grads = {}
-    for label, support in (("lists", sup), ("tiles", None)):
+    for label, support in (("lists", sup), ("lists again", sup), ("tiles", None)):
         corr = torch.empty((hq, b * s), dtype=torch.float32, device="cuda")
         g = [torch.empty_like(x) for x in (q, k, v)]
         ops.attn_bwd_into(do, q, k, v, o, st, corr, *g, nid, scale, True, mask=mk, wmean=wm, support=support)
         grads[label] = (corr, *g)
     torch.cuda.synchronize()
+    for name, a, e in zip(("corr", "dq", "dk", "dv"), grads["lists"], grads["lists again"]):
+        assert torch.equal(a, e), f"{name}: the list backward is not run-to-run deterministic"
     for name, a, e in zip(("corr", "dq", "dk", "dv"), grads["lists"], grads["tiles"]):
         err = float((a.float() - e.float()).abs().max())
         assert err <= 1e-2 * float(e.float().abs().max()) + 1e-5, f"{name}: max err {err:.3e}"
+    return grads["lists"]
+
+
+def test_support_lists_only_for_sparsemax():
+    """entmax15 takes no support lists (its wider supports make the gathers no
+    cheaper than the tile kernels): the workspace query answers 0 bytes."""
+    q, k, v, _ = _inputs((1, 4, 256, 128), (1, 2, 256, 128), torch.bfloat16, seed=3)
+    assert ops.new_dense_support(q, k, N.NORMALIZER_IDS["entmax15"]).numel() == 0
+    assert ops.new_dense_support(q, k, N.NORMALIZER_IDS["sparsemax"]).numel() > 0
+    assert ops.attn_fwd(q, k, v, N.NORMALIZER_IDS["entmax15"], 128 ** -0.5, True, -1, False)[4].numel() == 0
+
+
+def test_support_list_key_overflow_runs_tile_dkdv():
+    """An attention sink: every row keeps key 0, so key 0 has more entries than
+    the list dK/dV kernel sorts (1024).  dQ still comes from the lists, dK/dV
+    from the tile kernel; results match the tile-only backward and the oracle."""
+    d, dtype = 128, torch.bfloat16
+    b, hq, hkv, s = 1, 8, 2, 512
+    q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=19)
+    u = torch.randn(d, generator=torch.Generator().manual_seed(5)).to(dtype).cuda()
+    q = (q + u).to(dtype)
+    k[:, :, 0] = (0.5 * u).to(dtype)
+    nid, scale = N.NORMALIZER_IDS["sparsemax"], d ** -0.5
+    o, st, mk, wm, sup = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    assert not ops.support_overflowed(sup)
+    got = _list_and_tile_grads(q, k, v, do, nid, scale, sup, o, st, mk, wm)
+    flag = int(sup[:4].view(torch.int32).item())
+    assert flag == 2, f"expected the key-overflow flag, got {flag}"
+    ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), "sparsemax", scale=scale, causal=True)
+    for name, a, e in zip(("dq", "dk", "dv"), got[1:], ref[1:]):
+        assert_close(a, e, dtype, f"sink/{name}")
+
+
+@pytest.mark.parametrize("d,dtype", [(128, torch.bfloat16), (64, torch.float16)])
+def test_support_list_backward_matches_tile_backward(d, dtype):
+    """The forward's support lists (every row's keys with p > 0) drive dQ and
+    (transposed to the keys) dK/dV kernels that touch only those entries; they
+    must agree with the tile kernels that recompute every tile, give the same
+    bits on a second run, and match the oracle.  On N(0, 1) scores no list
+    overflows; on nearly flat scores the lists overflow and the backward falls
+    back to the tile kernels (checked against the oracle by the wide-support
+    tests)."""
+    norm = "sparsemax"
+    b, hq, hkv, s = 1, 8, 2, 1024
+    q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=13)
+    nid, scale = N.NORMALIZER_IDS[norm], d ** -0.5
+    o, st, mk, wm, sup = ops.attn_fwd(q, k, v, nid, scale, True, -1, False)
+    assert sup.numel() > 0 and not ops.support_overflowed(sup)
+    got = _list_and_tile_grads(q, k, v, do, nid, scale, sup, o, st, mk, wm)
+    assert not ops.support_overflowed(sup)  # neither a row list nor a key segment overflowed
     ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), norm, scale=scale, causal=True)
-    for name, a, e in zip(("dq", "dk", "dv"), grads["lists"][1:], ref[1:]):
+    for name, a, e in zip(("dq", "dk", "dv"), got[1:], ref[1:]):
         assert_close(a, e, dtype, f"lists/{name}")
-    qs, ks = q * d ** -0.25, k * d ** -0.25
-    _, _, _, _, wide = ops.attn_fwd(qs, ks, v, nid, scale, True, -1, False)
+    # nearly flat scores (std ~0.01) at 4096 keys: supports of hundreds of keys
+    qw, kw, vw, _ = _inputs((1, 2, 4096, d), (1, 1, 4096, d), dtype, seed=17)
+    _, _, _, _, wide = ops.attn_fwd(qw * d ** -0.5, kw * d ** -0.5, vw, nid, scale, True, -1, False)
     assert ops.support_overflowed(wide)
