@@ -544,7 +544,7 @@ def bench_varlen(dev, norms=("softmax1", "entmax15"), world=1, rank=0):
         ev[2].record()
         works = []
         for _ in range(reps):  # the sharded step: forward, backward and the gathers
-            o2, _, _ = fwd()
+            o2 = fwd()[0]
             works += gathers(o2)
             works += gathers(*bwd())
         for w in works:

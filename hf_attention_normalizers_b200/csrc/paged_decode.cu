@@ -579,6 +579,7 @@ inline bool make_cache_map(CUtensorMap* m, const void* base, bool bf16, int d, i
                            int64_t st, int64_t sh) {
   auto fn = tc::encode_fn();
   if (fn == nullptr) return false;
+  cudaFree(nullptr);  // a current context for the driver-side encoder (see tc::make_map)
   cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)hkv};
   cuuint64_t strides[2] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2};
   cuuint32_t box[3] = {64, (cuuint32_t)kBlk, (cuuint32_t)hkv};

@@ -6,7 +6,7 @@
 
 namespace hfan {
 
-constexpr int kSupSlots = 128;  // support-list slots per query row
+constexpr int kSupSlots = 64;  // support-list slots per query row (sparsemax keeps ~5 keys on N(0, 1) scores)
 constexpr int kKeyScanBlock = 4096;  // key counters per block of the key-offset prefix kernels
 
 constexpr int kKeyMaxEntries = 1024;  // longest key segment the list dK/dV kernel sorts

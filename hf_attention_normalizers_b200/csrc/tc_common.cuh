@@ -155,6 +155,11 @@ inline bool make_map(CUtensorMap* m, const void* base, bool bf16, int d, int64_t
               int64_t st, int64_t sh, int64_t sb, int box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
+  // The encoder is a driver call and needs a current context.  A thread that
+  // has made no runtime call yet (for example autograd's backward worker, when
+  // nothing ran on it before this library) has none: cudaFree(nullptr) binds
+  // the current device's primary context and does nothing else.
+  cudaFree(nullptr);
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)tokens, (cuuint64_t)heads, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)st * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
   cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};

@@ -228,9 +228,14 @@ def _attn_setup(ctx, inputs, output):
     ctx.save_for_backward(q, k, v, o, stats, mask, seed, key_lengths, wmean, support)
     ctx.args = (normalizer, scale, causal, window_left, out_bshd, dropout_p)
     ctx.mark_non_differentiable(stats, mask, wmean, support)
+    # no zero-filled gradients for the side outputs (the support workspace
+    # alone can be a gigabyte)
+    ctx.set_materialize_grads(False)
 
 
 def _attn_backward(ctx, do, dstats, dmask, dwmean, dsupport):
+    if do is None:
+        return (None,) * 11
     q, k, v, o, stats, mask, seed, key_lengths, wmean, support = ctx.saved_tensors
     normalizer, scale, causal, window_left, out_bshd, dropout_p = ctx.args
     dq, dk, dv = attn_bwd(_as_bhsd(do, out_bshd), q, k, v, _as_bhsd(o, out_bshd), stats, mask, normalizer,
@@ -357,9 +362,14 @@ def _varlen_setup(ctx, inputs, output):
     ctx.save_for_backward(q, k, v, o, stats, mask, cu_q, cu_k, wmean, support)
     ctx.args = (max_q, max_k, normalizer, scale, causal)
     ctx.mark_non_differentiable(stats, mask, wmean, support)
+    # no zero-filled gradients for the side outputs (the support workspace
+    # alone can be a gigabyte)
+    ctx.set_materialize_grads(False)
 
 
 def _varlen_backward(ctx, do, dstats, dmask, dwmean, dsupport):
+    if do is None:
+        return (None,) * 10
     q, k, v, o, stats, mask, cu_q, cu_k, wmean, support = ctx.saved_tensors
     max_q, max_k, normalizer, scale, causal = ctx.args
     dq, dk, dv = varlen_bwd(do, q, k, v, o, stats, mask, cu_q, cu_k, max_q, max_k, normalizer, scale, causal,
@@ -452,9 +462,12 @@ def _paged_setup(ctx, inputs, output):
     ctx.save_for_backward(q, kc, vc, o, stats, bt, sl)
     ctx.args = (page_size, max_len_k, normalizer, scale, causal)
     ctx.mark_non_differentiable(stats)
+    ctx.set_materialize_grads(False)
 
 
 def _paged_backward(ctx, do, dstats):
+    if do is None:
+        return (None,) * 10
     q, kc, vc, o, stats, bt, sl = ctx.saved_tensors
     page_size, max_len_k, normalizer, scale, causal = ctx.args
     dq, dkc, dvc = paged_bwd(do, q, kc, vc, o, stats, bt, sl, page_size, max_len_k, normalizer, scale, causal)

@@ -118,7 +118,7 @@ typedef struct hfan_attn_desc {
                         /* 64/128: device workspace of hfan_attn_support_bytes(desc)   */
                         /* bytes (256-byte aligned), or NULL.  hfan_attn_fwd writes    */
                         /* every row's support list into it (the keys with p > 0, up  */
-                        /* to 128 per row); hfan_attn_bwd given the same workspace    */
+                        /* to 64 per row); hfan_attn_bwd given the same workspace     */
                         /* computes dQ, the row correction, dK and dV from the lists  */
                         /* (transposed to the keys) instead of sweeping every key     */
                         /* tile, and falls back to the tile kernels when a list       */
