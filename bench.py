@@ -365,7 +365,10 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(total_flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "path": "kernels.hopper_{sparsemax,entmax15}_attention + autograd, pinned host inputs copied every step (copy stream, double-buffered prefetch of the next step)"},
-        "gpu_launches": args.steps * len(NORMS) * 3,
+        # per step: entmax15 forward, tile dQ, tile dK/dV; sparsemax forward,
+        # the five support-list kernels and the two tile kernels (which read
+        # the overflow flag and return at once)
+        "gpu_launches": args.steps * (3 + 8),
         "clocks": sampler.summary(),
     }
     extra = {}
