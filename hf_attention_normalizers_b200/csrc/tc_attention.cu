@@ -30,7 +30,11 @@
 // whole row (common.cuh, tau_step).  The final pass then forms
 // p = (z - tau)_+^a and P V; the output needs no normalisation.  It also
 // records, per 64-row half and key tile, whether any p > 0 (p.tile_mask):
-// the backward skips the tiles without support.  Optional dropout multiplies
+// the backward skips the tiles without support.  When every sparsemax row of
+// the CTA has its whole support in the candidate buffers (key index beside
+// each score), the final pass is skipped: P V and the w-weighted mean of V are gathered from the
+// buffered support, which is also written out as the row's support list for
+// the list backward (sparse_bwd.cu).  Optional dropout multiplies
 // the P fed to P V by keep / (1 - p_drop) (Philox keep bits, common.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>

@@ -11,10 +11,11 @@
 //     2 stages.  w = p for softmax1 (p = exp2(s log2e scale - m) / l from the
 //     saved row statistics) and w = 1[p>0] (sparsemax) or sqrt(p) (entmax15):
 //     the closed-form backwards of vutils/entmax.py:148-157 and :175-183 and
-//     the softmax Jacobian.  The row correction c is sum_j w dP / sum_j w for
-//     the sparse normalizers (a first pass over the key tiles) and O . dO for
-//     softmax1 (the implicit sink has value 0).  c is saved for the dk/dv
-//     kernel.
+//     the softmax Jacobian.  The row correction c is sum_j w dP / sum_j w =
+//     dO . wmean for the sparse normalizers (wmean = the w-weighted mean of V
+//     saved by the forward; without it, a first pass over the key tiles) and
+//     O . dO for softmax1 (the implicit sink has value 0).  c is saved for
+//     the dk/dv kernel.
 //
 // dk/dv kernel  (one CTA per 128 keys of one (batch, KV head); it walks every
 //                query head of the KV group, so GQA needs no atomics)
@@ -25,7 +26,10 @@
 //     Q / dO stream through a 3-stage ring of 64-row tiles.
 //
 // Sparse normalizers skip the key tiles (dq kernel) and units (dk/dv kernel)
-// whose probabilities are all zero, from the forward's tile mask.  Optional
+// whose probabilities are all zero, from the forward's tile mask.  With the
+// forward's support lists (sparsemax) both kernels return at once unless the
+// overflow flag asks for them: sparse_bwd.cu computes the gradients from the
+// lists.  Optional
 // dropout scales dP by the forward's keep / (1 - p_drop) and feeds dV the
 // dropped probabilities.  Gradients are written in the input dtype; dK
 // carries the softmax scale.
