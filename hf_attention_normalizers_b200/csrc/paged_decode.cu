@@ -16,9 +16,9 @@
 //            (reference kernels/paged_softmax1_hopper.py:17-83 semantics)
 // sparsemax / entmax15 (4 launches):
 //   scores   per unit: z = s * zs for every key -> workspace rows [B, Hq, max_len]
-//   tau      per (sequence, query head): the row (<= 32K keys) is staged in
-//            shared memory and tau is solved exactly (bracket + closed form,
-//            common.cuh)
+//   tau      per (sequence, query head): the scores above zmax - 1 (<= 4096)
+//            are compacted into shared memory and tau is solved exactly
+//            (bracket + closed form, common.cuh)
 //   pv       per unit: p = (z - tau)_+^a; V rows are read only for keys with
 //            p > 0 for some head of the group (zero-probability keys cost no
 //            V traffic)
@@ -91,6 +91,19 @@ __device__ __forceinline__ int64_t phys_token(const AttnParams& p, const int* bt
     return -1;
   }
   return tok;
+}
+
+// Row maxima of the sparse scores, kept in the tau slots of the workspace
+// until the tau kernel replaces them: floats mapped to unsigned integers in
+// the same order (so atomicMax finds the largest), 0 = no score yet (the
+// slots are zeroed before the scores kernel).
+__device__ __forceinline__ unsigned ordered_bits(float f) {
+  const unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ordered_float(unsigned u) {
+  if (u == 0u) return kNegInf;
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
 }
 
 // ------------------------------------------------------------------ softmax1
@@ -533,6 +546,7 @@ __global__ void __launch_bounds__(288, 1)
       }
     }
     float* srow = ws.scores + ((int64_t)b * p.hq + kvh * G + (g < G ? g : 0)) * max_len;
+    float zmax = kNegInf;
     const int mi = lane >> 3, ri = lane & 7;
     for (int blk = 0; blk < nblk; ++blk) {
       const int s_ = blk % NS;
@@ -566,10 +580,19 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
           const int t = tb + 8 * (x >> 1) + 2 * tq + (x & 1);
-          if (t < t1) srow[t] = sacc[x >> 1][x & 1] * zs;
+          if (t < t1) {
+            const float z = sacc[x >> 1][x & 1] * zs;
+            srow[t] = z;
+            zmax = fmaxf(zmax, z);
+          }
         }
       }
     }
+    // the four lanes of a head hold its keys: one atomic per head and CTA
+    zmax = fmaxf(zmax, __shfl_xor_sync(0xffffffffu, zmax, 1));
+    zmax = fmaxf(zmax, __shfl_xor_sync(0xffffffffu, zmax, 2));
+    if (g < G && tq == 0 && zmax > kNegInf)
+      atomicMax(reinterpret_cast<unsigned*>(ws.tau) + (int64_t)b * p.hq + kvh * G + g, ordered_bits(zmax));
   }
 }
 
@@ -656,6 +679,7 @@ __global__ void __launch_bounds__(256, 3) decode_sparse_scores(AttnParams p, Dec
       for (int i = 0; i < 8; ++i) q[h][i] *= zs;
     }
     float* srow = ws.scores + ((int64_t)b * p.hq + kvh * G) * max_len;
+    float zmax = kNegInf;  // of head li (lanes li < G write head li's scores)
     for (int tb = t0; tb < t1; tb += LN::TPW * kUnroll) {  // warp-uniform bound (shuffles)
       uint4 kr[kUnroll];
       bool valid[kUnroll];
@@ -677,10 +701,15 @@ __global__ void __launch_bounds__(256, 3) decode_sparse_scores(AttnParams p, Dec
 #pragma unroll
           for (int i = 0; i < 8; ++i) sv = fmaf(q[h][i], kx[i], sv);
           sv = group_sum<LN::LPT>(sv);
-          if (valid[u] && li == h % LN::LPT) srow[(int64_t)h * max_len + t] = sv;
+          if (valid[u] && li == h % LN::LPT) {
+            srow[(int64_t)h * max_len + t] = sv;
+            zmax = fmaxf(zmax, sv);
+          }
         }
       }
     }
+    if (li < G && zmax > kNegInf)
+      atomicMax(reinterpret_cast<unsigned*>(ws.tau) + (int64_t)b * p.hq + kvh * G + li, ordered_bits(zmax));
   }
 }
 
@@ -692,16 +721,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float r = 0.f;
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r += red[i];
-  return r;
-}
-__device__ __forceinline__ float block_max(float v, float* red) {
-  v = warp_max(v);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float r = kNegInf;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
   return r;
 }
 __device__ __forceinline__ float block_min(float v, float* red) {
@@ -716,73 +735,116 @@ __device__ __forceinline__ float block_min(float v, float* red) {
 }
 
 // One CTA per (sequence, query head): exact tau of the score row.
-// tau >= zmax - 1, so only the scores above zmax - 1 matter; they are
-// compacted (in index order, through a block scan) into a short shared-memory
-// list that one warp iterates on.  Rows with more candidates than the list
-// holds iterate over the whole row in global memory.
+// tau >= zmax - 1, so only the scores above zmax - 1 matter (zmax comes from
+// the scores kernel).  One pass over the row, coalesced with four keys per
+// thread in flight, compacts the candidates into a shared-memory list in index
+// order (per step of 2048 keys: a ballot per warp and quarter, one scan of the
+// 64 counts).  All 16 warps then iterate the solve on the list, the four sums
+// reduced across the block in a fixed order, so tau is the same on every run.
+// Rows with more candidates than the list holds iterate over the whole row in
+// global memory.
 constexpr int kTauCand = 4096;
+constexpr int kTauThreads = 512;
+constexpr int kTauWarps = kTauThreads / 32;
+constexpr int kTauVec = 4;  // keys per thread and step (loads in flight; 8 measured slower)
 
 template <int NORM>
-__global__ void __launch_bounds__(512) decode_sparse_tau(AttnParams p, DecodeWs ws, int max_len) {
+__global__ void __launch_bounds__(kTauThreads) decode_sparse_tau(AttnParams p, DecodeWs ws, int max_len) {
   __shared__ float red[32];
   __shared__ float cand[kTauCand];
-  __shared__ int wcount[16];
-  __shared__ float result[2];
+  __shared__ int qcount[kTauVec * kTauWarps];  // per step: candidates of (part, warp), then their offsets
+  __shared__ float part[2][kTauWarps][4];
+  __shared__ int s_total;
   const int b = blockIdx.y, hq = blockIdx.x;
   const int L = seq_len_k(p, b);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float* srow = ws.scores + ((int64_t)b * p.hq + hq) * max_len;
-  const float* zrow = srow;
-  float zmax = kNegInf;
-  for (int t = tid; t < L; t += blockDim.x) zmax = fmaxf(zmax, srow[t]);
-  zmax = block_max(zmax, red);
+  const float* zrow = ws.scores + ((int64_t)b * p.hq + hq) * max_len;
+  constexpr int STEP = kTauVec * kTauThreads;
+  // the row maximum, left in this row's tau slot by the scores kernel
+  const float zmax = ordered_float(reinterpret_cast<const unsigned*>(ws.tau)[(int64_t)b * p.hq + hq]);
+  __syncthreads();  // every thread has read the slot before thread 0 overwrites it
   float tau = kPosInf, support = 0.f;
   if (zmax > kNegInf) {
     const float t0 = zmax - 1.f;
-    // thread tid owns the contiguous slice [tid * per, (tid + 1) * per)
-    const int per = (L + blockDim.x - 1) / blockDim.x;
-    const int j0 = min(L, tid * per), j1 = min(L, j0 + per);
-    int mine = 0;
-    for (int j = j0; j < j1; ++j) mine += zrow[j] > t0 ? 1 : 0;
-    // exclusive scan of the per-thread counts
-    int incl = mine;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    if (lane == 31) wcount[warp] = incl;
+    if (tid == 0) s_total = 0;
     __syncthreads();
-    int wbase = 0, total = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-      if (w < warp) wbase += wcount[w];
-      total += wcount[w];
-    }
-    if (total <= kTauCand) {
-      int pos = wbase + incl - mine;
-      for (int j = j0; j < j1; ++j)
-        if (zrow[j] > t0) cand[pos++] = zrow[j];
-      __syncthreads();
-      if (warp == 0) {
-        float t = t0, tr = kPosInf, sup = 0.f;
-        for (int it = 0; it < 64; ++it) {
-          TauStats st{0.f, 0.f, 0.f, kPosInf};
-          for (int j = lane; j < total; j += 32) tau_accumulate(st, cand[j], t);
-          st.cnt = warp_sum(st.cnt);
-          st.s1 = warp_sum(st.s1);
-          st.s2 = warp_sum(st.s2);
-          st.zmin = warp_min(st.zmin);
-          sup = st.cnt;
-          if (tau_step(NORM, st, &t, &tr)) break;  // uniform: every lane holds the same sums
-        }
-        if (lane == 0) {
-          result[0] = tr;
-          result[1] = sup;
-        }
+    for (int j0 = 0; j0 < L; j0 += STEP) {
+      float x[kTauVec];
+      unsigned bal[kTauVec];
+#pragma unroll
+      for (int k = 0; k < kTauVec; ++k) {
+        const int j = j0 + k * kTauThreads + tid;
+        x[k] = j < L ? zrow[j] : kNegInf;
+      }
+#pragma unroll
+      for (int k = 0; k < kTauVec; ++k) {
+        bal[k] = __ballot_sync(0xffffffffu, x[k] > t0);
+        if (lane == 0) qcount[k * kTauWarps + warp] = __popc(bal[k]);
       }
       __syncthreads();
-      tau = result[0];
-      support = result[1];
+      if (warp == 0) {  // exclusive scan of the counts in (part, warp) order
+        constexpr int PL = kTauVec * kTauWarps / 32;  // counts per lane
+        int c[PL], sum = 0;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) sum += (c[i] = qcount[PL * lane + i]);
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        int base = s_total + incl - sum;
+        __syncwarp();  // every lane has read s_total
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+          qcount[PL * lane + i] = base;
+          base += c[i];
+        }
+        if (lane == 31) s_total = base;
+      }
+      __syncthreads();
+      const unsigned below = (1u << lane) - 1u;
+#pragma unroll
+      for (int k = 0; k < kTauVec; ++k) {
+        if (x[k] > t0) {
+          const int pos = qcount[k * kTauWarps + warp] + __popc(bal[k] & below);
+          if (pos < kTauCand) cand[pos] = x[k];
+        }
+      }
+      __syncthreads();  // qcount is rewritten by the next step
+    }
+    const int total = s_total;
+    if (total <= kTauCand) {
+      float t = t0, tr = kPosInf, sup = 0.f;
+      for (int it = 0; it < 64; ++it) {
+        TauStats st{0.f, 0.f, 0.f, kPosInf};
+        for (int j = tid; j < total; j += kTauThreads) tau_accumulate(st, cand[j], t);
+        st.cnt = warp_sum(st.cnt);
+        st.s1 = warp_sum(st.s1);
+        st.s2 = warp_sum(st.s2);
+        st.zmin = warp_min(st.zmin);
+        float* mine = part[it & 1][warp];
+        if (lane == 0) {
+          mine[0] = st.cnt;
+          mine[1] = st.s1;
+          mine[2] = st.s2;
+          mine[3] = st.zmin;
+        }
+        __syncthreads();  // parts of this iteration complete; the other buffer is free
+        TauStats all{0.f, 0.f, 0.f, kPosInf};
+#pragma unroll
+        for (int w = 0; w < kTauWarps; ++w) {
+          const float* o = part[it & 1][w];
+          all.cnt += o[0];
+          all.s1 += o[1];
+          all.s2 += o[2];
+          all.zmin = fminf(all.zmin, o[3]);
+        }
+        sup = all.cnt;
+        if (tau_step(NORM, all, &t, &tr)) break;  // uniform: every thread holds the same sums
+      }
+      tau = tr;
+      support = sup;
     } else {
       float t = t0;
       for (int it = 0; it < 64; ++it) {
@@ -949,15 +1011,18 @@ cudaError_t run(const AttnParams& p, int max_len, void* workspace, cudaStream_t 
     decode_sm1_combine<T, D, G><<<grid_r, D, 0, s>>>(p, ws);
     return cudaGetLastError();
   }
+  // the row maxima of the scores kernels start at "no score" (see ordered_bits)
+  cudaError_t e = cudaMemsetAsync(ws.tau, 0, (size_t)p.batch * p.hq * sizeof(float), s);
+  if (e != cudaSuccess) return e;
   if (p.norm == HFAN_SPARSEMAX) {
     if (!launch_scores_tiled<T, D, G, HFAN_SPARSEMAX>(p, ws, max_len, grid_u, s))
       decode_sparse_scores<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
-    decode_sparse_tau<HFAN_SPARSEMAX><<<grid_r, 512, 0, s>>>(p, ws, max_len);
+    decode_sparse_tau<HFAN_SPARSEMAX><<<grid_r, kTauThreads, 0, s>>>(p, ws, max_len);
     decode_sparse_pv<T, D, G, HFAN_SPARSEMAX><<<grid_u, ut, 0, s>>>(p, ws, max_len);
   } else {
     if (!launch_scores_tiled<T, D, G, HFAN_ENTMAX15>(p, ws, max_len, grid_u, s))
       decode_sparse_scores<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
-    decode_sparse_tau<HFAN_ENTMAX15><<<grid_r, 512, 0, s>>>(p, ws, max_len);
+    decode_sparse_tau<HFAN_ENTMAX15><<<grid_r, kTauThreads, 0, s>>>(p, ws, max_len);
     decode_sparse_pv<T, D, G, HFAN_ENTMAX15><<<grid_u, ut, 0, s>>>(p, ws, max_len);
   }
   decode_sparse_combine<T, D, G><<<grid_r, D, 0, s>>>(p, ws);
