@@ -130,7 +130,7 @@ int64_t mask_words(const hfan_attn_desc& d) {
 // Byte offsets of the support-list arrays inside the caller's workspace
 // (see AttnParams::sl_ent); false when the request takes no lists.
 struct SupportLayout {
-  int64_t flag, cnt, ent, g, kcnt, koff, bsum, tr, nk, total;
+  int64_t flag, cnt, ent, g, kcnt, koff, bsum, tr, lng, nk, long_cap, total;
 };
 
 bool support_layout(const hfan_attn_desc& d, SupportLayout* l) {
@@ -147,7 +147,7 @@ bool support_layout(const hfan_attn_desc& d, SupportLayout* l) {
   const int64_t cnt = (int64_t)d.heads_q * (d.head_dim / 32) * rows;
   if (slots >= (int64_t)1 << 31) return false;  // slot numbers are int32
   l->nk = (int64_t)d.heads_kv * (d.cu_seqlens_q ? (int64_t)d.total_k : (int64_t)d.batch * d.len_k);
-  if (l->nk <= 0) return false;
+  if (l->nk <= 0 || l->nk >= ((int64_t)1 << 31)) return false;  // key ids are int32 in the long-key list
   auto up = [](int64_t x) { return (x + 255) & ~int64_t(255); };
   l->flag = 0;
   l->cnt = 256;
@@ -157,7 +157,9 @@ bool support_layout(const hfan_attn_desc& d, SupportLayout* l) {
   l->koff = l->kcnt + up(l->nk * 4);
   l->bsum = l->koff + up((l->nk + 1) * 4);
   l->tr = l->bsum + up(sparse_key_blocks(l->nk) * 4);
-  l->total = l->tr + up(slots * 4);
+  l->lng = l->tr + up(slots * 4);
+  l->long_cap = slots / (kKeyMaxEntries + 1) + 1;  // keys that can exceed kKeyMaxEntries entries
+  l->total = l->lng + up((l->long_cap + 1) * 4);
   return true;
 }
 
@@ -201,6 +203,8 @@ int fill_attn(const hfan_attn_desc* desc, AttnParams& p) {
     p.sl_bsum = reinterpret_cast<int*>(w + l.bsum);
     p.sl_tr = reinterpret_cast<int*>(w + l.tr);
     p.sl_nk = l.nk;
+    p.sl_long = reinterpret_cast<int*>(w + l.lng);
+    p.sl_long_cap = (int)l.long_cap;
   }
   if (desc->wmean.data != nullptr && desc->normalizer != HFAN_SOFTMAX1) {
     const hfan_tensor& w = desc->wmean;

@@ -9,10 +9,10 @@ namespace hfan {
 constexpr int kSupSlots = 64;  // support-list slots per query row (sparsemax keeps ~5 keys on N(0, 1) scores)
 constexpr int kKeyScanBlock = 4096;  // key counters per block of the key-offset prefix kernels
 
-constexpr int kKeyMaxEntries = 1024;  // longest key segment the list dK/dV kernel sorts
+constexpr int kKeyMaxEntries = 1024;  // longest key segment a warp of the list dK/dV kernel sorts
 // sl_flag bits: a row's support list overflowed in the forward (the backward
-// runs both tile kernels), or a key's segment exceeds kKeyMaxEntries (the
-// tile dK/dV kernel runs; dQ still comes from the lists).
+// runs both tile kernels), or a long key segment could not be served by the
+// list kernels (the tile dK/dV kernel runs; dQ still comes from the lists).
 constexpr int kListRowOverflow = 1;
 constexpr int kListKeyOverflow = 2;
 
@@ -92,6 +92,10 @@ struct AttnParams {
   int* sl_bsum;
   int* sl_tr;
   int64_t sl_nk;
+  // Keys with more than kKeyMaxEntries entries (attention sinks): sl_long[0]
+  // counts them, sl_long[1 ..] lists their ids (at most sl_long_cap).
+  int* sl_long;
+  int sl_long_cap;
 
   float scale;
   int causal, window_left, norm;

@@ -193,11 +193,12 @@ __global__ void __launch_bounds__(256) key_block_sum_kernel(const AttnParams p) 
     int t = 0;
     for (int w = 0; w < 8; ++w) t += part[w];
     p.sl_bsum[blockIdx.x] = t;
+    if (blockIdx.x == 0) p.sl_long[0] = 0;  // no long key yet (key_scan_kernel runs next)
   }
 }
 
 // Exclusive prefix of the key counters into sl_koff (and the fill cursors in
-// sl_kcnt); a key with more than kKeyMaxEntries entries sets kListKeyOverflow.
+// sl_kcnt); keys with more than kKeyMaxEntries entries go to the long-key list.
 __global__ void __launch_bounds__(256) key_scan_kernel(const AttnParams p) {
   if (*p.sl_flag != 0) return;
   constexpr int PER = kKeyScanBlock / 256;  // consecutive counters per thread
@@ -220,7 +221,16 @@ __global__ void __launch_bounds__(256) key_scan_kernel(const AttnParams p) {
     longk |= v[e] > kKeyMaxEntries;
     tsum += v[e];
   }
-  if (longk) atomicOr(p.sl_flag, kListKeyOverflow);
+  if (longk) {
+    for (int e = 0; e < PER; ++e) {
+      if (v[e] <= kKeyMaxEntries) continue;
+      const int i = atomicAdd(p.sl_long, 1);
+      if (i < p.sl_long_cap)
+        p.sl_long[1 + i] = (int)(base + e);
+      else
+        atomicOr(p.sl_flag, kListKeyOverflow);
+    }
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = tsum;  // inclusive warp scan of the thread sums
 #pragma unroll
@@ -286,6 +296,7 @@ __global__ void __launch_bounds__(256) key_dkdv_kernel(const AttnParams p) {
   const int b = varlen ? 0 : (int)(kid / lk / p.hkv);
   const int off = p.sl_koff[kid];
   const int n = p.sl_koff[kid + 1] - off;
+  if (n > kKeyMaxEntries) return;  // a long key: key_long_kernel
   int* seg = p.sl_tr + off;
 
   // sort the segment by slot number
@@ -380,6 +391,164 @@ __global__ void __launch_bounds__(256) key_dkdv_kernel(const AttnParams p) {
   }
 }
 
+// Long keys (more than kKeyMaxEntries entries: attention sinks), one CTA per
+// key at a time.  The rows holding the key are marked in a shared-memory
+// bitmap over (query head of the group, row of the key's sequence), which
+// orders them without a sort; the 16 warps take fixed contiguous ranges of the
+// bitmap, each warp's four 8-lane groups take every fourth marked row in
+// order, find the key in the row's sub-lists, and the partial sums are added
+// in warp order, so the result is the same on every run.  A key whose
+// sequence needs a larger bitmap sets kListKeyOverflow (the tile dK/dV kernel
+// then recomputes every key).
+constexpr int kLongThreads = 512;
+constexpr int kLongWarps = kLongThreads / 32;
+constexpr int kLongBitWords = 16384;  // 524288 (head, row) pairs
+
+template <int HD>
+constexpr size_t long_smem_bytes() { return (size_t)kLongBitWords * 4 + (size_t)kLongWarps * 2 * HD * 4; }
+
+template <int HD, bool BF16>
+__global__ void __launch_bounds__(kLongThreads) key_long_kernel(const AttnParams p) {
+  if (*p.sl_flag != 0) return;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int DL = HD / 8, NV = DL / 8, NWG = HD / 32, LW = kSupSlots / NWG;
+  extern __shared__ uint32_t lsm[];
+  uint32_t* bits = lsm;
+  float* parts = reinterpret_cast<float*>(lsm + kLongBitWords);  // [warp][dk, dv][HD]
+  const int nlong = min(*(volatile int*)p.sl_long, p.sl_long_cap);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = lane >> 3, l8 = lane & 7, c0 = l8 * DL;
+  const unsigned gmask = 0xffu << (grp * 8);
+  const int G = p.hq / p.hkv;
+  const bool varlen = p.cu_k != nullptr;
+  const int64_t lk = varlen ? p.rows_k : p.len_k;
+  for (int li = blockIdx.x; li < nlong; li += gridDim.x) {
+    const int64_t kid = p.sl_long[1 + li];
+    const int tok = (int)(kid % lk);
+    const int kvh = (int)((kid / lk) % p.hkv);
+    const int b = varlen ? 0 : (int)(kid / lk / p.hkv);
+    int rlo, rn;  // the rows of the key's sequence
+    if (!varlen) {
+      rlo = b * p.len_q;
+      rn = p.len_q;
+    } else {
+      int lo = 0, hi = p.batch - 1;  // the last sequence whose first key is <= tok
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.cu_k[mid] <= tok) lo = mid; else hi = mid - 1;
+      }
+      rlo = p.cu_q[lo];
+      rn = p.cu_q[lo + 1] - rlo;
+    }
+    const int64_t nbits = (int64_t)G * rn;
+    if (nbits > (int64_t)kLongBitWords * 32) {
+      if (tid == 0) atomicOr(p.sl_flag, kListKeyOverflow);
+      continue;
+    }
+    const int words = (int)((nbits + 31) / 32);
+    for (int w = tid; w < words; w += kLongThreads) bits[w] = 0u;
+    __syncthreads();
+    const int off = p.sl_koff[kid], n = p.sl_koff[kid + 1] - off;
+    for (int e = tid; e < n; e += kLongThreads) {
+      const int slot = p.sl_tr[off + e];
+      const int64_t hr = slot / kSupSlots;
+      const int h = (int)(hr / p.rows_total);
+      const int r = (int)(hr - (int64_t)h * p.rows_total);
+      const int bit = (h - kvh * G) * rn + (r - rlo);
+      atomicOr(&bits[bit >> 5], 1u << (bit & 31));
+    }
+    __syncthreads();
+    float dk[DL], dv[DL];
+#pragma unroll
+    for (int x = 0; x < DL; ++x) dk[x] = dv[x] = 0.f;
+    const int per = (words + kLongWarps - 1) / kLongWarps;
+    int w = min(words, warp * per);
+    const int wend = min(words, w + per);
+    uint32_t m = w < wend ? bits[w] : 0u;
+    for (;;) {
+      // the next four marked rows of this warp's range, one per group (uniform)
+      int idx[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        while (m == 0u && w + 1 < wend) m = bits[++w];
+        if (m == 0u) {
+          idx[k] = -1;
+        } else {
+          idx[k] = w * 32 + __ffs(m) - 1;
+          m &= m - 1u;
+        }
+      }
+      if (idx[0] < 0) break;
+      const int mine = idx[grp];
+      if (mine >= 0) {
+        const int h = kvh * G + mine / rn;
+        const int r = rlo + mine % rn;
+        const int64_t hr = (int64_t)h * p.rows_total + r;
+        // the key's slot in the row's sub-lists
+        int slot = -1;
+        for (int sw = 0; sw < NWG && slot < 0; ++sw) {
+          const int c = p.sl_cnt[hr * NWG + sw];
+          for (int e0 = 0; e0 < c && slot < 0; e0 += 8) {
+            const int e = e0 + l8;
+            const int64_t sl = hr * kSupSlots + sw * LW + e;
+            const bool hit = e < c && p.sl_ent[sl].x == tok;
+            const unsigned bal = __ballot_sync(gmask, hit) & gmask;
+            if (bal) slot = __shfl_sync(gmask, (int)sl, __ffs(bal) - 1);
+          }
+        }
+        if (slot >= 0) {
+          const float pv = __int_as_float(p.sl_ent[slot].y);
+          const float ds = p.sl_g[slot];
+          const int rb = varlen ? 0 : r / p.len_q;
+          const int64_t tq = varlen ? r : r % p.len_q;
+          const uint4* qp = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (int64_t)rb * p.q_sb +
+                                                           (int64_t)h * p.q_sh + tq * p.q_st + c0);
+          const uint4* dp = reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) + (int64_t)rb * p.do_sb +
+                                                           (int64_t)h * p.do_sh + tq * p.do_st + c0);
+#pragma unroll
+          for (int v = 0; v < NV; ++v) {
+            float f[8], g[8];
+            unpack8<BF16>(__ldg(qp + v), f);
+            unpack8<BF16>(__ldg(dp + v), g);
+#pragma unroll
+            for (int x = 0; x < 8; ++x) {
+              dk[v * 8 + x] = fmaf(ds, f[x], dk[v * 8 + x]);
+              dv[v * 8 + x] = fmaf(pv, g[x], dv[v * 8 + x]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int x = 0; x < DL; ++x) {
+      dk[x] += __shfl_xor_sync(0xffffffffu, dk[x], 8);
+      dv[x] += __shfl_xor_sync(0xffffffffu, dv[x], 8);
+      dk[x] += __shfl_xor_sync(0xffffffffu, dk[x], 16);
+      dv[x] += __shfl_xor_sync(0xffffffffu, dv[x], 16);
+    }
+    if (grp == 0) {
+#pragma unroll
+      for (int x = 0; x < DL; ++x) {
+        parts[(warp * 2 + 0) * HD + c0 + x] = dk[x];
+        parts[(warp * 2 + 1) * HD + c0 + x] = dv[x];
+      }
+    }
+    __syncthreads();
+    if (tid < 2 * HD) {
+      const int which = tid / HD, d = tid % HD;
+      float acc = 0.f;
+      for (int wp = 0; wp < kLongWarps; ++wp) acc += parts[(wp * 2 + which) * HD + d];
+      const int64_t ko = varlen ? 0 : (int64_t)b;
+      if (which == 0)
+        static_cast<T*>(p.dk)[ko * p.dk_sb + (int64_t)kvh * p.dk_sh + (int64_t)tok * p.dk_st + d] =
+            from_f32<T>(acc * p.scale);
+      else
+        static_cast<T*>(p.dv)[ko * p.dv_sb + (int64_t)kvh * p.dv_sh + (int64_t)tok * p.dv_st + d] = from_f32<T>(acc);
+    }
+    __syncthreads();  // bits and parts are reused by the next key
+  }
+}
+
 template <int HD, bool BF16>
 cudaError_t launch_list_bwd(const AttnParams& p, cudaStream_t s) {
   cudaError_t e = cudaMemsetAsync(p.sl_kcnt, 0, (size_t)p.sl_nk * sizeof(int), s);
@@ -395,6 +564,10 @@ cudaError_t launch_list_bwd(const AttnParams& p, cudaStream_t s) {
   const int64_t subs = (int64_t)p.hq * p.rows_total * (HD / 32);
   key_fill_kernel<HD><<<(unsigned)((subs + 255) / 256), 256, 0, s>>>(p);
   key_dkdv_kernel<HD, BF16><<<(unsigned)((p.sl_nk + 7) / 8), 256, 0, s>>>(p);
+  cudaError_t le = cudaFuncSetAttribute(key_long_kernel<HD, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)long_smem_bytes<HD>());
+  if (le != cudaSuccess) return le;
+  key_long_kernel<HD, BF16><<<(unsigned)min(p.sl_long_cap, 296), kLongThreads, long_smem_bytes<HD>(), s>>>(p);
   return cudaGetLastError();
 }
 

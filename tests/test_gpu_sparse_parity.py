@@ -286,10 +286,11 @@ def test_support_lists_only_for_sparsemax():
     assert ops.attn_fwd(q, k, v, N.NORMALIZER_IDS["entmax15"], 128 ** -0.5, True, -1, False)[4].numel() == 0
 
 
-def test_support_list_key_overflow_runs_tile_dkdv():
+def test_support_list_attention_sink():
     """An attention sink: every row keeps key 0, so key 0 has more entries than
-    the list dK/dV kernel sorts (1024).  dQ still comes from the lists, dK/dV
-    from the tile kernel; results match the tile-only backward and the oracle."""
+    a warp of the list dK/dV kernel sorts (1024); the long-key kernel orders
+    its rows with a bitmap.  No fallback is needed, and the results match the
+    tile-only backward bit-stably and the oracle."""
     d, dtype = 128, torch.bfloat16
     b, hq, hkv, s = 1, 8, 2, 512
     q, k, v, do = _inputs((b, hq, s, d), (b, hkv, s, d), dtype, seed=19)
@@ -301,7 +302,7 @@ def test_support_list_key_overflow_runs_tile_dkdv():
     assert not ops.support_overflowed(sup)
     got = _list_and_tile_grads(q, k, v, do, nid, scale, sup, o, st, mk, wm)
     flag = int(sup[:4].view(torch.int32).item())
-    assert flag == 2, f"expected the key-overflow flag, got {flag}"
+    assert flag == 0, f"expected no fallback, got flag {flag}"
     ref = oracle.attention_backward(_np(q), _np(k), _np(v), _np(do), "sparsemax", scale=scale, causal=True)
     for name, a, e in zip(("dq", "dk", "dv"), got[1:], ref[1:]):
         assert_close(a, e, dtype, f"sink/{name}")
