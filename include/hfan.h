@@ -122,8 +122,9 @@ typedef struct hfan_attn_desc {
                         /* computes dQ, the row correction, dK and dV from the lists  */
                         /* (transposed to the keys) instead of sweeping every key     */
                         /* tile, and falls back to the tile kernels when a list       */
-                        /* overflowed or a key has more than 1024 entries.  Results   */
-                        /* are the same on every run.  No counterpart in the          */
+                        /* overflowed (or, for dK/dV, a key held by more than 524288  */
+                        /* (head, row) pairs).  Results are the same on every run.    */
+                        /* No counterpart in the                                       */
                         /* reference (its backward recomputes every tile,             */
                         /* kernels/sparse_entmax_hopper.py:230-319).                   */
 } hfan_attn_desc;
