@@ -88,6 +88,11 @@ constexpr int kScanStages = 2;
 constexpr int kCW = HFAN_CW;                          // keys per chunk of the scan's gate
 constexpr int kCompactRoom = kCW > 12 ? kCW : 12;     // free slots a compaction must leave
 constexpr int kMaxStages = 8;
+// The K-only passes (scan, sweeps) use all 512 TMEM columns as a 4-deep ring
+// of S tiles (O, P and U are idle until the final pass), so row warps that
+// run ahead or fall behind one another by up to three tiles do not hold up
+// the next S = Q K^T.
+constexpr int kKonlyBufs = 4;
 constexpr int kMaxSweeps = 24;     // exact bracket sweeps before giving up
 constexpr float kRescaleLog2 = 8.f;
 
@@ -99,6 +104,7 @@ struct Bars {
   uint64_t q_full;
   uint64_t full[kMaxStages], empty[kMaxStages];
   uint64_t s_full[2], s_empty[2];
+  uint64_t k_full[kKonlyBufs], k_empty[kKonlyBufs];  // S ring of the K-only passes
   uint64_t p_full[2], pv_done[2], ctrl;
 };
 
@@ -343,6 +349,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       mbar_init(&bars->s_full[s], 1);
       mbar_init(&bars->s_empty[s], Roles<HD>::ROW_THREADS / 32);
     }
+    for (int s = 0; s < kKonlyBufs; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], Roles<HD>::ROW_THREADS / 32);
+    }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->p_full[s], Roles<HD>::ROW_THREADS / 32);
       mbar_init(&bars->pv_done[s], 1);
@@ -441,15 +451,17 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       };
       int pass = SCAN ? kPassTopC : kPassFinal;
       bool ok = qk_issuer ? mbar_wait(&bars->q_full, 0, abort_flag) : true;
-      uint32_t sc = 0, npre = 0;  // S tiles issued; K-only passes finished
+      uint32_t sc = 0, kc = 0;  // S tiles issued in the final pass / in the K-only passes
       while (ok) {
         const bool fin = pass == kPassFinal;
         if (qk_issuer) {
           for (int t = 0; t < n_tiles && ok; ++t) {
             int ks;
-            const int sb = sc & 1;
+            const int sb = fin ? (int)(sc & 1) : (int)(kc % kKonlyBufs);
             if (!(ok = wait_item(fin ? (t ? 2 * t - 1 : 0) : t, fin ? L::NS : kScanStages, &ks))) break;
-            if (want_u && fin && t >= 2) {
+            if (!fin) {
+              if (!(ok = mbar_wait(&bars->k_empty[sb], ((kc / kKonlyBufs) & 1) ^ 1, abort_flag))) break;
+            } else if (want_u && t >= 2) {
               // the buffer holds P and W of final-pass tile t - 2 until its P V is done
               if (!(ok = mbar_wait(&bars->pv_done[sb], ((t >> 1) & 1) ^ 1, abort_flag))) break;
             } else {
@@ -462,13 +474,12 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
               const uint64_t bd = sw128_desc(ring_base + ks * KV_BYTES + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
               mma_f16_ss(tmem + sb * 128, a, bd, IDESC_QK, kk > 0);
             }
-            mma_commit(&bars->s_full[sb]);
+            mma_commit(fin ? &bars->s_full[sb] : &bars->k_full[sb]);
             mma_commit(&bars->empty[ks]);
-            ++sc;
+            if (fin) ++sc; else ++kc;
           }
         } else if (fin) {
-          // S buffer of final-pass tile j (the K-only passes issued sc0 tiles before)
-          const uint32_t sc0 = (uint32_t)n_tiles * npre;
+          // S buffer of final-pass tile j: j & 1 (the K-only passes have their own ring)
           for (int j = 0; j < n_tiles && ok; ++j) {
             int vs;
             const int pb = j & 1;
@@ -479,7 +490,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
               // A = P (and W) in the S buffer: keys [16 kk, 16 kk + 16) belong to
               // warpgroup 16 kk / PCOLS, whose P occupies the first PCOLS / 2
               // columns of its slice and W the next PCOLS / 2.
-              const int sbj = (int)((sc0 + (uint32_t)j) & 1u);
+              const int sbj = j & 1;
 #pragma unroll
               for (int kk = 0; kk < kBN / 16; ++kk) {
                 const int wk = (16 * kk) / PCOLS, ko = 16 * kk - wk * PCOLS;
@@ -512,7 +523,6 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           }
         }
         if (!ok || fin) break;
-        ++npre;
 #pragma unroll
         for (int s_ = 0; s_ < kScanStages; ++s_) {
           const int uses = n_tiles > s_ ? (n_tiles - s_ + kScanStages - 1) / kScanStages : 0;
@@ -564,18 +574,22 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     uint16_t* ibuf = ibuf0 + wg * CAPW * 128;
     float* xch = reinterpret_cast<float*>(smem + L::XCH);  // [4096] floats
 
-    uint32_t sc = 0, pc = 0;
+    uint32_t sc = 0, kc = 0, pc = 0;  // final-pass S tiles, K-only S tiles, P tiles
     bool ok = true;
     float sreg[COLS];  // raw scores s = q.k of this warpgroup's columns (masked: -inf)
 #ifdef HFAN_DIAG
     long long dls_w = 0, dls_l = 0;
 #endif
-    auto load_s = [&](int t) -> bool {
-      const int sb = sc & 1;
+    // konly: an S tile of a K-only pass (4-deep ring, buffer kc % 4)
+    auto load_s = [&](int t, bool konly) -> bool {
+      const int sb = konly ? (int)(kc % kKonlyBufs) : (int)(sc & 1);
+      uint64_t* sfull = konly ? &bars->k_full[sb] : &bars->s_full[sb];
+      uint64_t* sempty = konly ? &bars->k_empty[sb] : &bars->s_empty[sb];
+      const uint32_t sph = konly ? (kc / kKonlyBufs) & 1 : (sc >> 1) & 1;
 #ifdef HFAN_DIAG
       long long c0_ = clock64();
 #endif
-      if (!wait_warp(&bars->s_full[sb], (sc >> 1) & 1, abort_flag)) return false;
+      if (!wait_warp(sfull, sph, abort_flag)) return false;
       tc_fence_after();
 #ifdef HFAN_DIAG
       long long c1_ = clock64();
@@ -589,8 +603,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       dls_l += clock64() - c1_;
 #endif
       tc_fence_before();
-      warp_arrive(&bars->s_empty[sb]);
-      ++sc;
+      warp_arrive(sempty);
+      if (konly) ++kc; else ++sc;
       const int kb = k_lo + t * kBN + wg * COLS;
       const int lo = vis_lo - kb, hi = vis_hi - kb;
       if (__all_sync(0xffffffffu, lo <= 0 && hi >= COLS)) {
@@ -679,7 +693,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
 #define DIAG_LAP(acc) ((void)0)
 #endif
       for (int t = 0; t < n_tiles; ++t) {
-        if (ok) ok = load_s(t);
+        if (ok) ok = load_s(t, true);
         DIAG_LAP(dw);
         if (ok) {
         // chunk maxima (8 keys each) gate the candidate appends
@@ -859,7 +873,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         cd.n = 0;
         const bool refill = __any_sync(0xffffffffu, pending && sweep > 0 && support <= 0.75f * CAPW * NWG);
         for (int t = 0; t < n_tiles && ok; ++t) {
-          if (!(ok = load_s(t))) break;
+          if (!(ok = load_s(t, true))) break;
           if (pending) {
             if (refill) {
 #pragma unroll
@@ -1036,7 +1050,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     int sl_n = 0;      // entries of this warpgroup's support sub-list
     const int64_t sl_row = (int64_t)g.q_start + i;
     for (int t = 0; t < (gather ? 0 : n_tiles) && (ok || !SPARSE); ++t) {
-      if (ok) DIAG_T(dg_s, ok = load_s(t));
+      if (ok) DIAG_T(dg_s, ok = load_s(t, false));
       uint32_t wpk[COLS / 2];  // sparse with U: packed W of this warpgroup's keys
       float alpha = 1.f;
       bool rescale = false;
