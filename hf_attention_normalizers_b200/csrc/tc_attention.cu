@@ -48,12 +48,12 @@
 // the scan / solve / final phases and counters of compactions and sweeps,
 // read back with hfan_diag_read.  The product build contains none of it.
 #ifdef HFAN_DIAG
-__device__ unsigned long long g_hfan_diag[16];
+__device__ unsigned long long g_hfan_diag[24];
 extern "C" int hfan_diag_read(unsigned long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 16);
+  return (int)cudaMemcpyFromSymbol(out, g_hfan_diag, sizeof(unsigned long long) * 24);
 }
 extern "C" int hfan_diag_clear() {
-  unsigned long long z[16] = {0};
+  unsigned long long z[24] = {0};
   return (int)cudaMemcpyToSymbol(g_hfan_diag, z, sizeof(z));
 }
 #define DIAG_ADD(i, v) atomicAdd(&g_hfan_diag[i], (unsigned long long)(v))
@@ -148,8 +148,16 @@ struct Cand {
   int n;          // buffered entries (some may be <= thr: dead, ignored)
   bool overflow;  // more live candidates than the buffer holds
   float thr;      // admission threshold, z units
-  float thr_s;    // the same threshold in raw-score units (thr / zs)
+  float thr_s;    // the same threshold in raw-score units (thr / zs, or slightly below it)
 };
+
+// A raw-score gate at or a few ulps below z / zs (izs = 1 / zs): a gate that
+// is too low only admits a few dead entries, one that is too high could drop
+// a candidate.  One multiply instead of a division on the scan's hot path.
+__device__ __forceinline__ float raw_gate(float z, float izs) {
+  const float r = z * izs;
+  return r - fabsf(r) * 0x1p-20f;
+}
 
 // Solve f_A(t) = 1 on the buffered candidates starting from the lower bound
 // t0 (exact bracket + closed form of common.cuh).  Returns the root (or the
@@ -183,8 +191,9 @@ __device__ __forceinline__ float top_bound(const float (&zz)[KT]) {
   // test needs no root or division (1/k is a constant of the unrolled loop),
   // so a single closed form is evaluated at the end.
   const float z1 = zz[0];
-  float s1 = 0.f, s2 = 0.f, b1 = 0.f, b2 = 0.f;
-  int kb = 0;
+  float s1 = 0.f, s2 = 0.f;
+  float bt = 0.f, bmean = 0.f, bd = 0.f;  // the largest valid k's closed form (sparsemax) or its parts
+  bool any = false;
 #pragma unroll
   for (int k = 1; k <= KT; ++k) {
     const float y = zz[k - 1] - z1;
@@ -192,31 +201,56 @@ __device__ __forceinline__ float top_bound(const float (&zz)[KT]) {
     s2 += y * y;
     const float inv = 1.f / float(k);
     bool valid;
+    float tk = 0.f, mean = 0.f, d = 0.f;
     if (NORM == HFAN_SPARSEMAX) {
-      valid = (s1 - 1.f) * inv <= y;
+      tk = (s1 - 1.f) * inv;
+      valid = tk <= y;
     } else {
-      const float mean = s1 * inv;
-      const float d = (1.f - (s2 - s1 * mean)) * inv;  // t_k = mean - sqrt(d)
-      const float g = mean - y;                          // t_k <= y  <=>  g <= sqrt(d)
+      mean = s1 * inv;
+      d = (1.f - (s2 - s1 * mean)) * inv;  // t_k = mean - sqrt(d)
+      const float g = mean - y;             // t_k <= y  <=>  g <= sqrt(d)
       valid = g <= 0.f || (d >= 0.f && g * g <= d);
     }
     valid = valid && zz[k - 1] > kNegInf;
     if (valid) {
-      kb = k;
-      b1 = s1;
-      b2 = s2;
+      any = true;
+      bt = tk;
+      bmean = mean;
+      bd = d;
     }
   }
-  if (kb == 0) return z1 - 1.f;
-  const float inv = 1.f / float(kb);
-  float t;
-  if (NORM == HFAN_SPARSEMAX) {
-    t = (b1 - 1.f) * inv;
-  } else {
-    const float mean = b1 * inv;
-    t = mean - sqrtf(fmaxf((1.f - (b2 - b1 * mean)) * inv, 0.f));
-  }
+  if (!any) return z1 - 1.f;
+  const float t = NORM == HFAN_SPARSEMAX ? bt : bmean - sqrtf(fmaxf(bd, 0.f));
   return fmaxf(z1 - 1.f, z1 + t);
+}
+
+// a >= b after the call
+__device__ __forceinline__ void cswap(float& a, float& b) {
+  const float hi = fmaxf(a, b);
+  b = fminf(a, b);
+  a = hi;
+}
+
+// t[0..3] (descending) becomes the four largest of t and the unsorted c[0..3]:
+// c is sorted by a five-comparator network, the two sorted lists are folded
+// into the bitonic top four (max of t[i] and c[3 - i]), and two compare
+// levels sort it.  Depth 6 instead of the 16 of one insertion after another.
+__device__ __forceinline__ void top4_merge(float (&t)[4], const float (&c)[4]) {
+  float a = c[0], b = c[1], x = c[2], y = c[3];
+  cswap(a, b);
+  cswap(x, y);
+  cswap(a, x);
+  cswap(b, y);
+  cswap(b, x);  // a >= b >= x >= y
+  float r0 = fmaxf(t[0], y), r1 = fmaxf(t[1], x), r2 = fmaxf(t[2], b), r3 = fmaxf(t[3], a);
+  cswap(r0, r2);
+  cswap(r1, r3);
+  cswap(r0, r1);
+  cswap(r2, r3);
+  t[0] = r0;
+  t[1] = r1;
+  t[2] = r2;
+  t[3] = r3;
 }
 
 // The same solve over the NW per-warpgroup buffers of one row (buffer w holds
@@ -535,7 +569,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       }
       if (!ok) record_error(p, ctl, kDevWaitTimeout);
     }
-  } else {
+  } else if (warp < Roles<HD>::TMA_WARP) {
     // ------------------------------------------------------------ normalizer
     // NWG warpgroups share each 128-row tile: warpgroup wg owns key columns
     // [COLS wg, COLS (wg + 1)) of every S tile and head-dim columns
@@ -557,6 +591,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     if (p.window_left > 0) vis_lo = limit - p.window_left + 1;
     const float zs = NORM == HFAN_SOFTMAX1 ? p.scale * kLog2e
                                            : (NORM == HFAN_SPARSEMAX ? p.scale : 0.5f * p.scale);
+    const float izs = 1.f / zs;
     // During the scan passes the V ring and the P buffer are idle; they hold
     // the candidate buffers (the producer loads V only in the final pass),
     // one slice per warpgroup.
@@ -688,6 +723,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       // strand a warpgroup at its barrier.
 #ifdef HFAN_DIAG
       long long dw = 0, dt = 0, da = 0, dv = 0, dc = clock64(), dn;
+      long long n_vote = 0, n_heavy = 0, n_app = 0, n_chunk = 0, t_vbar = 0;
 #define DIAG_LAP(acc) (dn = clock64(), acc += dn - dc, dc = dn)
 #else
 #define DIAG_LAP(acc) ((void)0)
@@ -713,17 +749,26 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         // every fourth tile, to adopt the other warpgroups' bounds) update the
         // KT largest chunk maxima, the bound, and the buffers.
         const bool heavy = __any_sync(0xffffffffu, tm > cd.thr_s) || (t & 3) == 0;
+#ifdef HFAN_DIAG
+        n_heavy += heavy;
+#pragma unroll
+        for (int c = 0; c < COLS / kCW; ++c) n_chunk += __any_sync(0xffffffffu, heavy && !cd.overflow && tm > cd.thr_s && cm[c] > cd.thr_s);
+#endif
         if (heavy) {
+          if constexpr (KT == 4 && COLS / kCW == 4) {
+            top4_merge(tk, cm);
+          } else {
 #pragma unroll
-          for (int c = 0; c < COLS / kCW; ++c) {
-            float x = cm[c];
+            for (int c = 0; c < COLS / kCW; ++c) {
+              float x = cm[c];
 #pragma unroll
-            for (int k = 0; k < KT - 1; ++k) {  // branch-free insertion
-              const float hi_ = fmaxf(tk[k], x);
-              x = fminf(tk[k], x);
-              tk[k] = hi_;
+              for (int k = 0; k < KT - 1; ++k) {  // branch-free insertion
+                const float hi_ = fmaxf(tk[k], x);
+                x = fminf(tk[k], x);
+                tk[k] = hi_;
+              }
+              tk[KT - 1] = fmaxf(tk[KT - 1], x);
             }
-            tk[KT - 1] = fmaxf(tk[KT - 1], x);
           }
           float zk[KT];
 #pragma unroll
@@ -733,7 +778,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           for (int w = 0; w < NWG; ++w) lb = fmaxf(lb, xb[w * 128 + row]);
           if (lb > cd.thr) {
             cd.thr = lb;
-            cd.thr_s = lb / zs;
+            cd.thr_s = raw_gate(lb, izs);
           }
         }
         DIAG_LAP(dt);
@@ -751,6 +796,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
                   cbuf[cd.n * 128 + row] = x * zs;
                   if (IDX) ibuf[cd.n * 128 + row] = (uint16_t)((t << JB) | (c * kCW + e));
                   cd.n += x > cd.thr_s ? 1 : 0;
+#ifdef HFAN_DIAG
+                  n_app += x > cd.thr_s ? 1 : 0;
+#endif
                 }
               }
             }
@@ -770,7 +818,15 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         // (Sparsemax supports stay far below the capacity: no vote.)
         if (NORM != HFAN_ENTMAX15) continue;
         if ((t % HFAN_VOTE_PERIOD) != HFAN_VOTE_PERIOD - 1 && t != n_tiles - 1) continue;
-        if (named_bar_or(1, NT, ok && cd.n > CAPW - HFAN_VOTE_MARGIN && !cd.overflow)) {
+#ifdef HFAN_DIAG
+        const long long vb0_ = clock64();
+#endif
+        const bool vote_ = named_bar_or(1, NT, ok && cd.n > CAPW - HFAN_VOTE_MARGIN && !cd.overflow);
+#ifdef HFAN_DIAG
+        t_vbar += clock64() - vb0_;
+        n_vote += vote_;
+#endif
+        if (vote_) {
           float t0 = cd.thr;
 #pragma unroll
           for (int w = 0; w < NWG; ++w) t0 = fmaxf(t0, xb[w * 128 + row]);
@@ -778,7 +834,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           union_solve(cd, t0, ok && zmax > kNegInf, HFAN_VOTE_ITERS, &r, &sup);
           if (r > cd.thr) {
             cd.thr = r;
-            cd.thr_s = r / zs;
+            cd.thr_s = raw_gate(r, izs);
           }
           if (!cd.overflow) {
             int live = 0;
@@ -802,6 +858,11 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         DIAG_ADD(2, dt);
         DIAG_ADD(3, da);
         DIAG_ADD(4, dv);
+        DIAG_ADD(16, n_vote);
+        DIAG_ADD(17, t_vbar);
+        DIAG_ADD(18, n_app);
+        DIAG_ADD(19, n_chunk);
+        DIAG_ADD(20, n_heavy);
       }
 #endif
 #ifdef HFAN_DIAG
