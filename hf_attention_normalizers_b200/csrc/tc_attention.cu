@@ -733,11 +733,18 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         DIAG_LAP(dw);
         if (ok) {
         // chunk maxima (8 keys each) gate the candidate appends
-        float cm[COLS / kCW];
+        // (sparsemax: and their halves gate the predicated stores)
+        float cm[COLS / kCW], ch[2 * (COLS / kCW)];
         float tm = kNegInf;
 #pragma unroll
         for (int c = 0; c < COLS / kCW; ++c) {
-          cm[c] = max_n<kCW>(sreg + c * kCW);
+          if (NORM == HFAN_SPARSEMAX) {
+            ch[2 * c] = max_n<kCW / 2>(sreg + c * kCW);
+            ch[2 * c + 1] = max_n<kCW / 2>(sreg + c * kCW + kCW / 2);
+            cm[c] = fmaxf(ch[2 * c], ch[2 * c + 1]);
+          } else {
+            cm[c] = max_n<kCW>(sreg + c * kCW);
+          }
           tm = fmaxf(tm, cm[c]);
         }
         zmax = fmaxf(zmax, tm * zs);
@@ -787,18 +794,24 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           for (int c = 0; c < COLS / kCW; ++c) {
             if (!cd.overflow && cm[c] > cd.thr_s) {
               if (cd.n > CAPW - kCW) cd = buffer_compact<NORM, IDX>(cbuf, ibuf, row, cd, CAPW, zs);
-              if (!cd.overflow) {
-                // predicated appends: every value is written at slot n, and n
-                // only advances past the candidates
+              // predicated appends: every value of a (half) chunk holding a
+              // candidate is written at slot n, and n only advances past the
+              // candidates.  Sparsemax gates each half chunk (its candidates
+              // are sparse); entmax15's fill both halves, so it gates the chunk.
+              constexpr int NHC = NORM == HFAN_SPARSEMAX ? 2 : 1;
 #pragma unroll
-                for (int e = 0; e < kCW; ++e) {
-                  const float x = sreg[c * kCW + e];
-                  cbuf[cd.n * 128 + row] = x * zs;
-                  if (IDX) ibuf[cd.n * 128 + row] = (uint16_t)((t << JB) | (c * kCW + e));
-                  cd.n += x > cd.thr_s ? 1 : 0;
+              for (int hc = 0; hc < NHC; ++hc) {
+                if (!cd.overflow && (NHC == 1 || ch[2 * c + hc] > cd.thr_s)) {
+#pragma unroll
+                  for (int e = hc * (kCW / NHC); e < (hc + 1) * (kCW / NHC); ++e) {
+                    const float x = sreg[c * kCW + e];
+                    cbuf[cd.n * 128 + row] = x * zs;
+                    if (IDX) ibuf[cd.n * 128 + row] = (uint16_t)((t << JB) | (c * kCW + e));
+                    cd.n += x > cd.thr_s ? 1 : 0;
 #ifdef HFAN_DIAG
-                  n_app += x > cd.thr_s ? 1 : 0;
+                    n_app += x > cd.thr_s ? 1 : 0;
 #endif
+                  }
                 }
               }
             }
