@@ -807,6 +807,8 @@ def main():
                     help="B,S,HQ,HKV override for small profiling cases (default: the BASELINE config)")
     ap.add_argument("--model-step", action="store_true",
                     help="only run the Qwen3-1.7B training-step measurement (BASELINE configs[4])")
+    ap.add_argument("--nccl-ctas", type=int, default=0,
+                    help="cap on the CTAs of NCCL's collectives (0: NCCL's choice)")
     ap.add_argument("--profile-case", action="store_true",
                     help="run warmup+steps of the step only (no e2e, no phases): for ncu captures")
     args = ap.parse_args()
@@ -840,7 +842,16 @@ def main():
             os.environ["NCCL_DEBUG"] = "INFO"
             os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
             torch.cuda.set_device(local_rank)
-            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+            # The all-gathers run beside the attention kernels, which fill
+            # every SM with one CTA: each CTA NCCL holds is an SM the kernels
+            # lose while the gathers run.  --nccl-ctas caps that count; at 8
+            # GPUs a cap of 8 made the gathers the bottleneck (7.1 ms per step
+            # against 4.2 with NCCL's own choice), so the default is no cap.
+            opts = dist.ProcessGroupNCCL.Options()
+            if args.nccl_ctas > 0:
+                opts.config.max_ctas = args.nccl_ctas
+                opts.config.nvls_ctas = args.nccl_ctas
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank), pg_options=opts)
         args.cpu_baseline = args.cpu_baseline and rank == 0 and world == 1 and not args.shape
         args.decode = args.decode and not args.shape
         line = run_ours(args, rank, world, local_rank)
@@ -848,9 +859,16 @@ def main():
             import torch.distributed as dist
 
             dist.barrier()
-            dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)
+    if world > 1 and args.impl != "reference":
+        # Every rank is past the last collective.  The process group is not
+        # destroyed: NCCL would print its teardown lines after the JSON line
+        # (the exit frees the communicator), and the JSON line stays last on
+        # stdout.
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 if __name__ == "__main__":

@@ -1118,13 +1118,16 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
     // softmax1 meets a named barrier on every tile, so after a timeout the loop
     // keeps running (with the work skipped) instead of leaving it.
 #ifdef HFAN_DIAG
-    long long dg_s = 0, dg_pv = 0;
+    long long dg_s = 0, dg_pv = 0, dg_c = 0, dg_st = 0, dgc0 = 0;
 #endif
     float wsum = 0.f;  // sparse: sum_j w_j of this warpgroup's keys (U's normaliser)
     int sl_n = 0;      // entries of this warpgroup's support sub-list
     const int64_t sl_row = (int64_t)g.q_start + i;
     for (int t = 0; t < (gather ? 0 : n_tiles) && (ok || !SPARSE); ++t) {
       if (ok) DIAG_T(dg_s, ok = load_s(t, false));
+#ifdef HFAN_DIAG
+      dgc0 = clock64();
+#endif
       uint32_t wpk[COLS / 2];  // sparse with U: packed W of this warpgroup's keys
       float alpha = 1.f;
       bool rescale = false;
@@ -1229,6 +1232,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       if (!ok) continue;
       // O may be rescaled once every earlier P V has completed; P buffer pb
       // is free once the P V two tiles back (its last reader) has.
+#ifdef HFAN_DIAG
+      { const long long n_ = clock64(); dg_c += n_ - dgc0; dgc0 = n_; }
+#endif
       const int pb = pc & 1;
       if (__any_sync(0xffffffffu, rescale)) {
         if (!(ok = wait_warp(&bars->pv_done[(pc - 1) & 1], ((pc - 1) >> 1) & 1, abort_flag))) continue;
@@ -1276,6 +1282,9 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       tc_fence_before();
       warp_arrive(&bars->p_full[pb]);
       ++pc;
+#ifdef HFAN_DIAG
+      dg_st += clock64() - dgc0;
+#endif
     }
     if (lists && row_ok && !gather) {
       p.sl_cnt[((int64_t)h * p.rows_total + sl_row) * NWG + wg] = min(sl_n, kSupSlots / NWG);
@@ -1292,6 +1301,8 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       DIAG_ADD(7, clock64() - diag_t0);
       DIAG_ADD(12, dg_s);
       DIAG_ADD(13, dg_pv);
+      DIAG_ADD(22, dg_c);
+      DIAG_ADD(23, dg_st);
       DIAG_ADD(8, dls_w);
       DIAG_ADD(9, dls_l);
     }
