@@ -1195,6 +1195,22 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           sreg[j + 1] = f2_hi(d);
         }
         wsum += f2_lo(ws2) + f2_hi(ws2);
+        if (want_u && ok) {
+          // P, then W, over this warpgroup's own COLS columns of the S buffer
+          // the tile came from (read into registers above; nobody else reads
+          // them, and the buffer is reissued only after this tile's P V).
+          // Issued before the support lists and tile bits are worked out, so
+          // that the stores are in flight meanwhile.
+          const uint32_t sl = tmem + lane_addr + ((sc - 1) & 1) * 128 + wg * COLS;
+  #pragma unroll
+          for (int c = 0; c < COLS / 32; ++c) {
+            uint32_t pk[16];
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
+            tmem_st16(sl + c * 16, pk);
+            tmem_st16(sl + COLS / 2 + c * 16, *reinterpret_cast<uint32_t(*)[16]>(wpk + c * 16));
+          }
+        }
         if (lists && row_ok) {
           // this warpgroup's keys with p > 0, in key order, into the row's
           // sub-list (8-key chunks gate the predicated appends)
@@ -1249,20 +1265,7 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
         tmem_st32(tmem_o + lane_addr + wg * 32, r);
         tmem_wait_st();
       }
-      if (want_u) {
-        // P, then W, over this warpgroup's own COLS columns of the S buffer
-        // the tile came from (read into registers above; nobody else reads
-        // them, and the buffer is reissued only after this tile's P V)
-        const uint32_t sl = tmem + lane_addr + ((sc - 1) & 1) * 128 + wg * COLS;
-#pragma unroll
-        for (int c = 0; c < COLS / 32; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
-          tmem_st16(sl + c * 16, pk);
-          tmem_st16(sl + COLS / 2 + c * 16, *reinterpret_cast<uint32_t(*)[16]>(wpk + c * 16));
-        }
-      } else {
+      if (!want_u) {
         if (pc >= 2) {
           DIAG_T(dg_pv, ok = wait_warp(&bars->pv_done[pb], ((pc >> 1) & 1) ^ 1, abort_flag));
           if (!ok) continue;
