@@ -1202,10 +1202,10 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
           // Issued before the support lists and tile bits are worked out, so
           // that the stores are in flight meanwhile.
           const uint32_t sl = tmem + lane_addr + ((sc - 1) & 1) * 128 + wg * COLS;
-  #pragma unroll
+#pragma unroll
           for (int c = 0; c < COLS / 32; ++c) {
             uint32_t pk[16];
-  #pragma unroll
+#pragma unroll
             for (int j = 0; j < 16; ++j) pk[j] = pack2<BF16>(sreg[c * 32 + 2 * j], sreg[c * 32 + 2 * j + 1]);
             tmem_st16(sl + c * 16, pk);
             tmem_st16(sl + COLS / 2 + c * 16, *reinterpret_cast<uint32_t(*)[16]>(wpk + c * 16));
