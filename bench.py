@@ -11,9 +11,10 @@ Under torchrun (N>1) the 8 KV-head groups are sharded across ranks (strong
 scaling: the total problem is fixed); after each step the outputs and
 gradients are gathered with NCCL all-gather.  Rank 0 prints one JSON line.
 
-``--impl reference`` times the reference's own CPU algorithm (the numpy
-restatement under oracle/, all host threads) on a bounded sample of the same
-workload and prints the same metric.
+``--impl reference`` times the reference's own CPU algorithm (its eager torch
+path restated under oracle/torch_eager.py -- the reference package itself
+cannot be imported where the benchmarks run -- all host threads) on a bounded
+sample of the same workload and prints the same metric.
 
 Metric: algorithmic attention TFLOP/s of fwd+bwd (FlashAttention convention:
 fwd = 4 B Hq D sum_rows(visible keys), bwd = 2.5 x fwd; threshold-solve
@@ -699,27 +700,32 @@ def bench_model(dev, steps=3, warmup=2, world=1, rank=0):
 
 
 # --------------------------------------------------------------------------- CPU
+REF_ROWS = 512  # query rows of the CPU sample (reference arm step and cpu_baseline)
+
+
 def cpu_sample(threads: int, rows: int):
-    """One bounded sample of the workload through the CPU oracle.
+    """One bounded sample of the workload through the reference's eager path
+    restated in torch (``oracle/torch_eager.py``: the same sort / cumsum
+    thresholds, closed-form backwards and matmuls), on the host cores.
 
     The last `rows` query rows of one (batch, KV group) slice -- 4 query heads
     against all S keys under the causal mask, forward + backward of both
     normalizers, float32.  Returns (seconds, algorithmic FLOPs of the sample).
     """
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    import numpy as np
+    import torch
 
-    import oracle
+    from oracle import torch_eager
 
-    rng = np.random.default_rng(0)
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
     g = HQ // HKV
-    q = rng.standard_normal((1, g, rows, D)).astype(np.float32)
-    k = rng.standard_normal((1, 1, S, D)).astype(np.float32)
-    v = rng.standard_normal((1, 1, S, D)).astype(np.float32)
-    do = rng.standard_normal((1, g, rows, D)).astype(np.float32)
+    q = torch.randn(1, g, rows, D, generator=gen)
+    k = torch.randn(1, 1, S, D, generator=gen)
+    v = torch.randn(1, 1, S, D, generator=gen)
+    do = torch.randn(1, g, rows, D, generator=gen)
     t0 = time.perf_counter()
     for name in NORMS:
-        oracle.attention_backward(q, k, v, do, name, scale=D ** -0.5, causal=True, dtype=np.float32)
+        torch_eager.attention_backward(q, k, v, do, name, scale=D ** -0.5, causal=True)
     sec = time.perf_counter() - t0
     visible = sum(S - rows + i + 1 for i in range(rows))
     flops = 3.5 * 4.0 * g * D * visible * len(NORMS)
@@ -727,37 +733,45 @@ def cpu_sample(threads: int, rows: int):
 
 
 def cpu_baseline(budget_s: float = 20.0):
+    """The reference arm's sample (REF_ROWS query rows), 1 warm-up and the
+    median of up to 5 runs within the time budget, plus config 1 whole."""
     threads = os.cpu_count() or 1
-    rows = 64
-    sec, flops = cpu_sample(threads, rows)
-    # grow the sample toward the time budget (bounded)
-    if sec < budget_s / 4:
-        rows = int(min(1024, rows * max(1.0, budget_s / 2 / max(sec, 1e-3))))
-        sec, flops = cpu_sample(threads, rows)
+    rows = REF_ROWS
+    cpu_sample(threads, rows)
+    secs, flops, t_end = [], 0.0, time.perf_counter() + budget_s
+    while len(secs) < 5 and (not secs or time.perf_counter() < t_end):
+        sec_, flops = cpu_sample(threads, rows)
+        secs.append(sec_)
+    sec = statistics.median(secs)
     return {"value": round(flops / sec / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"last {rows} query rows x 4 heads of one (batch, KV group) slice, all {S} keys, "
-                      f"fwd+bwd sparsemax+entmax15, float32 numpy oracle; {sec:.1f} s",
+                      f"fwd+bwd sparsemax+entmax15, float32, the reference's eager path restated in torch "
+                      f"(oracle/torch_eager.py, {threads} threads); median of {len(secs)}, {sec:.2f} s each",
             "config1": cpu_config1(threads)}
 
 
 def cpu_config1(threads: int):
     """BASELINE configs[0] as a whole problem on the host cores: fp32 q,k,v
-    [2, 8, 512, 128], causal, fwd + bwd of every normalizer through the numpy
-    oracle (median of 3)."""
-    import numpy as np
+    [2, 8, 512, 128] (the reference's seed), causal, fwd + bwd of every
+    normalizer through the torch restatement of the reference's eager path
+    (1 warm-up, median of 5)."""
+    import torch
 
-    import oracle
+    from oracle import torch_eager
 
-    rng = np.random.default_rng(0)
-    q, k, v, g = (rng.standard_normal((2, 8, 512, 128)).astype(np.float32) for _ in range(4))
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    q, k, v, g = (torch.randn(2, 8, 512, 128) for _ in range(4))
     flops = 3.5 * causal_flops(2, 8, 512, 128)
-    out = {"workload": "BASELINE configs[0] (B=2 H=8 S=512 D=128 fp32, causal, fwd+bwd)", "cores": threads}
+    out = {"workload": "BASELINE configs[0] (B=2 H=8 S=512 D=128 fp32, causal, fwd+bwd)", "cores": threads,
+           "path": "oracle/torch_eager.py (the reference's eager torch ops)"}
     for name in ("softmax1", "sparsemax", "entmax15"):
         times = []
-        for _ in range(3):
+        for rep in range(6):
             t0 = time.perf_counter()
-            oracle.attention_backward(q, k, v, g, name, scale=128 ** -0.5, causal=True, dtype=np.float32)
-            times.append(time.perf_counter() - t0)
+            torch_eager.attention_backward(q, k, v, g, name, scale=128 ** -0.5, causal=True)
+            if rep:
+                times.append(time.perf_counter() - t0)
         sec = statistics.median(times)
         out[name] = {"ms": round(sec * 1e3, 1), "GFLOP/s": round(flops / sec / 1e9, 2)}
     return out
@@ -771,7 +785,7 @@ def run_reference(args, rank):
         cpu_sample(threads, 16)
     secs, flops = [], 0.0
     for _ in range(args.steps):
-        s_, f_ = cpu_sample(threads, 32)
+        s_, f_ = cpu_sample(threads, REF_ROWS)
         secs.append(s_)
         flops = f_
     sec = statistics.median(secs)
@@ -784,8 +798,9 @@ def run_reference(args, rank):
         "config": {"workload": "Qwen3-8B causal prefill fwd+bwd (BASELINE configs[1])", "batch": B,
                    "seq_len": S, "heads_q": HQ, "heads_kv": HKV, "head_dim": D, "normalizers": list(NORMS)},
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": "each step: last 32 query rows x 4 heads of one (batch, KV group) slice, "
-                                   f"all {S} keys, fwd+bwd sparsemax+entmax15, float32 numpy oracle"},
+                         "sample": f"each step: last {REF_ROWS} query rows x 4 heads of one (batch, KV group) "
+                                   f"slice, all {S} keys, fwd+bwd sparsemax+entmax15, float32, the reference's "
+                                   f"eager path restated in torch (oracle/torch_eager.py, {threads} threads)"},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

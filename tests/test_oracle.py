@@ -104,3 +104,38 @@ def test_dropout_keep_rate_and_oracle_identity():
     all_kept = oracle.attention_backward(q, k, v, do, "entmax15", dropout=(np.ones((1, 2, 16, 16), bool), 0.0))
     for a, b in zip(base, all_kept):
         assert np.allclose(a, b, rtol=0, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", ["softmax1", "sparsemax", "entmax15"])
+@pytest.mark.parametrize("hq,hkv,lq,lk", [(4, 4, 64, 64), (8, 2, 48, 96)])
+def test_torch_eager_restatement_matches_oracle(name, hq, hkv, lq, lk):
+    """The CPU baseline's torch restatement of the reference's eager path
+    computes what the pinned numpy oracle computes (float64, both causal)."""
+    from oracle import torch_eager
+
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((2, hq, lq, 32))
+    k = rng.standard_normal((2, hkv, lk, 32))
+    v = rng.standard_normal((2, hkv, lk, 32))
+    do = rng.standard_normal((2, hq, lq, 32))
+    ref = oracle.attention_backward(q, k, v, do, name, causal=True)
+    got = torch_eager.attention_backward(*(torch.from_numpy(x) for x in (q, k, v, do)), name, causal=True)
+    for label, a, e in zip(("o", "dq", "dk", "dv"), got, ref):
+        assert np.abs(a.numpy() - e).max() <= 1e-10 * max(1.0, np.abs(e).max()), label
+
+
+@pytest.mark.parametrize("name", NORMS)
+def test_torch_eager_config1_matches_reference(golden, name):
+    """BASELINE config 1 (float32, the reference's seed) through the torch
+    restatement, against the reference's own sampled rows and sums."""
+    from oracle import torch_eager
+
+    g = golden("config1")
+    torch.manual_seed(0)
+    q, k, v = (torch.randn(2, 8, 512, 128) for _ in range(3))
+    gr = torch.randn(q.shape)
+    got = torch_eager.attention_backward(q, k, v, gr, name, scale=1 / np.sqrt(128), causal=True)
+    for label, a in zip(("o", "dq", "dk", "dv"), got):
+        a = a.numpy()
+        np.testing.assert_allclose(a[:, :, ::61, :], g[f"config1_{name}_{label}_rows"], rtol=0, atol=2e-5)
+        assert abs(a.astype(np.float64).sum() - float(g[f"config1_{name}_{label}_sum"])) < 1e-2
