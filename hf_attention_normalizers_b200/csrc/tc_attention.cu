@@ -900,6 +900,23 @@ __global__ void __launch_bounds__(Roles<HD, 2>::THREADS, 1)
       named_bar_sync(1, NT);
       // Exact tau on the union of the row's buffers.
       const bool empty = !(zrow > kNegInf);
+      if (NORM == HFAN_SPARSEMAX && !empty && !ovf) {
+        // Entries at or below the merged bound (a lower bound of tau) are not
+        // in the support: drop them once, in order, so that the solve's
+        // iterations and the gather walk only live entries (the sums, taken
+        // over z > t in buffer order, are unchanged).  Sparsemax only: its
+        // buffers are never compacted by votes (entmax15's are, and the
+        // extra pass measured slower there).
+        int live = 0;
+        for (int e = 0; e < cd.n; ++e) {
+          const float z = cbuf[e * 128 + row];
+          if (z > lower) {
+            if (IDX) ibuf[live * 128 + row] = ibuf[e * 128 + row];
+            cbuf[live++ * 128 + row] = z;
+          }
+        }
+        cd.n = live;
+      }
       bool pending = !empty && ovf;  // overflowing rows go to whole-row sweeps
       float tsol = lower;
       if (union_solve(cd, lower, !empty && !ovf, 64, &tsol, &support, true, zrow)) {
